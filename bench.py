@@ -1,0 +1,419 @@
+"""Benchmark of one routed-expert NVFP4 MoE layer forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 2]
+
+One step = one MoE layer forward of the configured shape: router logits
+(tensor cores) + sigmoid/top-k/renorm, dispatch, NVFP4 gather-quantize,
+gate/up grouped GEMM with fused SwiGLU, hidden quantize, down grouped GEMM
+with fused rescale, weighted combine. Metric: routed-expert tokens/s per MoE
+layer (whole job: tokens of all ranks / max-over-ranks step time).
+
+Inputs are synthetic and seeded (x ~ N(0,1) bf16, expert weights ~ N(0,0.02)
+packed to NVFP4 on the GPU, router weight ~ N(0, 1/C) so the logits are
+~N(0,1)); x (100 MB) plus the packed weights (510 MB) exceed the 126 MB L2,
+so no L2 flush is needed between steps.
+
+N > 1 (torchrun): every rank runs the full layer on its own tokens (expert
+weights replicated): weak scaling, no data-path collective.
+
+--impl reference: the CPU port of the reference path (the oracle's NVFP4
+chain with weights dequantised once, float32 GEMMs, all host threads) on a
+bounded sample of tokens of the same layer; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: tokens, dim, experts, top_k, hidden, skew
+    "1": dict(tokens=256, dim=512, experts=8, top_k=2, hidden=1024, skew=False),
+    "2": dict(tokens=16384, dim=3072, experts=64, top_k=4, hidden=1536, skew=False),
+    "3": dict(tokens=16384, dim=3072, experts=64, top_k=4, hidden=1536, skew=True),
+    "5": dict(tokens=512, dim=1024, experts=32, top_k=2, hidden=2048, skew=False),
+    "ckpt": dict(tokens=16384, dim=3072, experts=128, top_k=8, hidden=1280, skew=False),
+}
+METRIC = "routed-expert tokens/sec per MoE layer"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def make_inputs(cfg, seed, device):
+    import torch
+
+    t, c, e, k, f = cfg["tokens"], cfg["dim"], cfg["experts"], cfg["top_k"], cfg["hidden"]
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(t, c, generator=g).to(torch.bfloat16)
+    router = torch.randn(e, c, generator=g) * (1.0 / c) ** 0.5
+    bias = torch.zeros(e)
+    if cfg["skew"]:
+        # Zipf(s=1.2) expert popularity through the routing bias
+        ranks = torch.randperm(e, generator=torch.Generator().manual_seed(0)).float() + 1
+        bias = -1.2 * torch.log(ranks) * 0.08
+    gw = torch.Generator(device=device).manual_seed(seed + 1)
+    gu = (torch.randn(e, c, 2 * f, generator=gw, device=device) * 0.02).to(torch.bfloat16)
+    down = (torch.randn(e, f, c, generator=gw, device=device) * 0.02).to(torch.bfloat16)
+    return x, router, bias, gu, down
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        else:
+            self.lines = []
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_port_forward(prep, x, router, bias, cfg):
+    """The oracle's NVFP4 chain with dequantised fp32 weights (CPU port)."""
+    import torch
+
+    from oracle import nvfp4_moe_oracle as O
+
+    e, k, c, f = cfg["experts"], cfg["top_k"], cfg["dim"], cfg["hidden"]
+    logits = O.router_logits(x, router)
+    top, gate = O.route(logits, bias, k)
+    order, inverse, tokens, _sg, offsets, csr = O.dispatch(top, gate, e)
+    pcsr = O.pad_csr(csr)
+    m = tokens.numel()
+    prows = O.padded_rows(m, e)
+    ag = O.segment_global_scales(O.row_amax(x), csr, tokens)
+    aq, asf = O.quantize_activations(x, csr, pcsr, prows, ag, row_indices=tokens)
+    a = O.dequant_rows(aq, asf, c)
+    gu = torch.zeros(prows, 2 * f, dtype=torch.bfloat16)
+    b = pcsr.tolist()
+    for ex in range(e):
+        if b[ex + 1] > b[ex]:
+            gu[b[ex]:b[ex + 1]] = (a[b[ex]:b[ex + 1]] @ prep["gu"][ex].t()).to(torch.bfloat16)
+    hidden, rowmax = O.rescale_swiglu_maximum(gu, pcsr, ag, prep["gug"])
+    hg = O.segment_global_scales(rowmax, pcsr)
+    hq, hsf = O.quantize_activations(hidden, pcsr, pcsr, prows, hg)
+    h = O.dequant_rows(hq, hsf, f)
+    raw = torch.zeros(prows, c, dtype=torch.bfloat16)
+    for ex in range(e):
+        if b[ex + 1] > b[ex]:
+            raw[b[ex]:b[ex + 1]] = (h[b[ex]:b[ex + 1]] @ prep["dn"][ex].t()).to(torch.bfloat16)
+    return O.rescale_combine(raw, inverse, top, gate, csr, pcsr, hg, prep["dng"], 2.5)
+
+
+def cpu_baseline(cfg, budget_s=12.0, sample_tokens=None):
+    """Time the CPU port on a bounded token sample of the layer; tokens/s."""
+    import torch
+
+    from oracle import nvfp4_moe_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    c, e, f = cfg["dim"], cfg["experts"], cfg["hidden"]
+    t = sample_tokens or min(cfg["tokens"], 1024)
+    sub = dict(cfg, tokens=t)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(t, c, generator=g).to(torch.bfloat16)
+    router = torch.randn(e, c, generator=g) * (1.0 / c) ** 0.5
+    bias = torch.zeros(e)
+    # packed weights -> dequantised once (load-time work, not timed)
+    gw = torch.Generator().manual_seed(8)
+    prep = {"gu": [], "dn": [], "gug": torch.empty(e), "dng": torch.empty(e)}
+    for ex in range(e):
+        w1 = (torch.randn(2 * f, c, generator=gw) * 0.02).to(torch.bfloat16)
+        q, sf, gg = O.pack_matrix(w1)
+        prep["gu"].append(O.dequant_matrix(q, sf, 2 * f, c))
+        prep["gug"][ex] = gg
+        w2 = (torch.randn(c, f, generator=gw) * 0.02).to(torch.bfloat16)
+        q, sf, gg = O.pack_matrix(w2)
+        prep["dn"].append(O.dequant_matrix(q, sf, c, f))
+        prep["dng"][ex] = gg
+    times = []
+    start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        cpu_port_forward(prep, x, router, bias, sub)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - start > budget_s or len(times) >= 5:
+            break
+    med = statistics.median(times)
+    return {"value": t / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{t} tokens of the layer (C={c}, E={e}, k={cfg['top_k']}, F={f}), median of {len(times)} "
+                      f"forwards, weights dequantised once outside the timing"}
+
+
+def run_reference(args, cfg):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    cb = cpu_baseline(cfg, budget_s=max(5.0, 2.0 * args.steps))
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"config {args.config}", **cfg}, "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module("praxis-1-oss_b200")
+    pkg.capi.load()
+    peaks = {}
+    pfile = ROOT / "MEASURED_PEAKS.json"
+    if pfile.exists():
+        peaks = json.loads(pfile.read_text())
+
+    t, c, e, k, f = cfg["tokens"], cfg["dim"], cfg["experts"], cfg["top_k"], cfg["hidden"]
+    x_cpu, router, bias, gu, down = make_inputs(cfg, 1000 + rank, dev)
+    mod = pkg.B200MoEFeedForward(c, f, e, k, 2.5, dispatch_chunk_size=t, shared_expert=False).to(dev)
+    with torch.no_grad():
+        mod.router.weight.copy_(router.to(dev))
+        mod.expert_bias.copy_(bias.to(dev))
+    mod.set_routed_weights(gu, down)
+    del gu, down
+    bank = mod.routed
+    bank.prepare()
+    terms = mod.router_terms()
+    gq, gsf = bank._kernel_gate_up
+    x = x_cpu.to(dev)
+    out = torch.empty_like(x)
+    ops = pkg.ops
+
+    def step():
+        return ops.moe_forward(x, None, None, gq, gsf, bank.gate_up_global, bank.down_q, bank.down_sf,
+                               bank.down_global, 2.5, router_terms=terms, router_bias=mod.expert_bias, top_k=k,
+                               out=out)
+
+    # correctness guard of the measured path: routing and output vs the
+    # stage-by-stage ops path (same kernels, separate launches)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.current_stream(dev)
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    value = t * world / (ms / 1e3)
+
+    # per-stage timing (same kernels launched stage by stage, events on the
+    # launching stream) for the roofline of the dominant kernel
+    stages = time_stages(pkg, x, terms, mod, bank, gq, gsf, cfg, reps=max(3, min(args.steps, 10)))
+    gemm1_ms = stages["gemm1_swiglu"]
+    flops1 = 2.0 * t * k * c * 2 * f
+    bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
+    fp4_peak = 4.0 * bf16_peak
+    roofline = {"bound": "tensor", "kernel": "gemm_nvfp4_kernel<128, EPI_SWIGLU> (gate/up)",
+                "achieved": flops1 / (gemm1_ms / 1e3) / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
+                "frac": flops1 / (gemm1_ms / 1e3) / 1e12 / fp4_peak, "traffic": None,
+                "peak_note": ("dense FP4 peak = 4 x measured cuBLAS bf16 burst "
+                              f"({bf16_peak} TFLOP/s, MEASURED_PEAKS.json); nominal dense FP4 9000 TFLOP/s")}
+    layer_flops = 6.0 * t * k * c * f
+    e2e = None
+    if not args.no_e2e:
+        e2e = time_e2e(step, x, x_cpu, out, args, dev, t, world)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 block16 scales, fp32 accumulate), bf16 I/O",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) expert weights packed to NVFP4)",
+        "config": {"workload": f"BASELINE config {args.config}: one MoE layer forward incl. router", "tokens": t,
+                   "dim": c, "experts": e, "top_k": k, "expert_hidden": f, "router": "sigmoid+renorm",
+                   "parallelism": "replicas" if world > 1 else "single-gpu",
+                   "l2": "inputs + packed weights (610 MB) exceed the 126 MB L2; no flush"},
+        "layer_tflops": layer_flops / (ms / 1e3) / 1e12,
+        "stages_ms": stages,
+        "roofline": roofline,
+        "clocks": clk.summary(),
+        "gpu_launches": 9 * args.steps,
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def time_stages(pkg, x, terms, mod, bank, gq, gsf, cfg, reps=5):
+    import torch
+
+    ops, capi = pkg.ops, pkg.capi
+    k = cfg["top_k"]
+    names = ["router_logits", "route", "dispatch", "quantize_gather", "gemm1_swiglu", "quantize_hidden",
+             "gemm2_rescale", "combine"]
+    acc = {n: 0.0 for n in names}
+    stream = torch.cuda.current_stream(x.device)
+    for rep in range(reps + 1):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        evs[0].record(stream)
+        logits, amax = ops.router_logits(x, terms)
+        evs[1].record(stream)
+        top, gate = ops.route(logits, mod.expert_bias, k)
+        evs[2].record(stream)
+        r = ops.dispatch(top, gate, cfg["experts"], amax, full=False)
+        evs[3].record(stream)
+        aq, asf = ops.quantize_gather(x, r, r.act_global)
+        evs[4].record(stream)
+        hamax = torch.zeros(cfg["experts"], dtype=torch.int32, device=x.device)
+        e_g0 = torch.cuda.Event(enable_timing=True)
+        e_g0.record(stream)
+        hidden = ops.grouped_gemm(aq, asf, gq, gsf, r, epilogue=capi.EPI_SWIGLU, act_global=r.act_global,
+                                  w_global=bank.gate_up_global, amax_out=hamax)
+        evs[5].record(stream)
+        hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
+        evs[6].record(stream)
+        rows = ops.grouped_gemm(hq, hsf, bank.down_q, bank.down_sf, r, epilogue=capi.EPI_RESCALE, act_amax=hamax,
+                                w_global=bank.down_global)
+        evs[7].record(stream)
+        ops.combine(rows, r, 2.5, rows_rescaled=True)
+        evs[8].record(stream)
+        torch.cuda.synchronize()
+        if rep == 0:
+            continue
+        for i, n in enumerate(names):
+            if n == "gemm1_swiglu":
+                acc[n] += e_g0.elapsed_time(evs[5])
+            else:
+                acc[n] += evs[i].elapsed_time(evs[i + 1])
+    return {n: v / reps for n, v in acc.items()}
+
+
+def time_e2e(step, x, x_cpu, out, args, dev, t, world):
+    """Same metric through the public API with host buffers: each step
+    copies its input from pinned host memory and reads the output back."""
+    import torch
+
+    host_in = x_cpu.pin_memory()
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(2):
+        x.copy_(host_in, non_blocking=True)
+        step()
+        host_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        x.copy_(host_in, non_blocking=True)
+        step()
+        host_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    return {"value": t * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": host_in.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 2}
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_b200(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,214 @@
+/*
+ * praxis_b200_moe.h - C ABI of the B200 (sm_100a) routed-expert NVFP4 MoE
+ * library (libpraxis_b200_moe.so).
+ *
+ * The reference (runwayml/praxis-1-oss) is Python; its hot path is the MoE
+ * module -> routed NVFP4 bank -> Triton/CuTe/FlashInfer kernel chain. Each
+ * entry point below replaces one function of that chain and says which
+ * (file:line in the reference). A Python binding is a ctypes stub over these
+ * declarations (praxis-1-oss_b200/capi.py is that binding).
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless stated otherwise. The caller
+ *    allocates every buffer (outputs and workspaces); no entry point
+ *    allocates device memory.
+ *  - bf16 tensors are passed as `void*` / `const void*` (raw 16-bit values).
+ *  - `stream` is a cudaStream_t; `device` the CUDA ordinal the buffers live
+ *    on (made current for the call). Work is enqueued on `stream` only;
+ *    nothing synchronizes the host, so every call can be captured in a CUDA
+ *    graph. Offsets and counts stay on the device.
+ *  - The return value is PRAXIS_B200_OK or an error code;
+ *    praxis_b200_last_error() gives a message (per host thread). Argument
+ *    errors are reported before any launch.
+ *  - Device-side faults never trap: waits are bounded and out-of-range
+ *    indices are clamped; either records a code in a per-device error word
+ *    that praxis_b200_device_error() reads (and clears) at a sync point.
+ */
+#ifndef PRAXIS_B200_MOE_H
+#define PRAXIS_B200_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PRAXIS_B200_ABI_VERSION 1
+
+enum {
+  PRAXIS_B200_OK = 0,
+  PRAXIS_B200_EINVAL = 1,      /* argument check failed (nothing launched) */
+  PRAXIS_B200_ECUDA = 2,       /* a CUDA call failed */
+  PRAXIS_B200_EUNSUPPORTED = 3 /* device is not sm_100 */
+};
+
+enum { PRAXIS_B200_SIGMOID = 0, PRAXIS_B200_SOFTMAX = 1 };
+
+/* Grouped-GEMM epilogues (praxis_b200_grouped_gemm). */
+enum {
+  PRAXIS_B200_EPI_PLAIN = 0,   /* out = bf16(acc) */
+  PRAXIS_B200_EPI_SWIGLU = 1,  /* rescale + SwiGLU + per-expert max |hidden| */
+  PRAXIS_B200_EPI_RESCALE = 2  /* out = bf16(bf16(acc) * bf16(g_act * g_w)) */
+};
+
+int praxis_b200_abi_version(void);
+const char* praxis_b200_last_error(void);
+/* Number of SMs of `device`; 0 if it is not an sm_100 device. */
+int praxis_b200_device_check(int device);
+/* Reads and clears the device error word (synchronizes `device`). */
+int praxis_b200_device_error(int device, uint32_t* code);
+
+/* Padded rows of the expert-grouped layout: ((rows + 127 * experts) / 128) * 128.
+ * Replaces praxis/kernels/nvfp4.py:212-213. Host function. */
+int64_t praxis_b200_padded_rows(int64_t routed_rows, int32_t experts);
+
+/* Router logits: logits[t, e] = sum_c f32(x[t, c]) * f32(W[e, c]) for bf16 x
+ * [T, C], and row_amax[t] = bf16(max_c |x[t, c]|) when row_amax != NULL.
+ * `weight` is [splits, E, C] bf16: splits = 1 for a bf16 router weight, 3 for
+ * an fp32 weight given as hi + mid + lo bf16 terms (exact).
+ * Replaces praxis/layers.py:1104-1122 (_router_logits_forward) and
+ * praxis/kernels/nvfp4_moe.py:15-21 (_row_absmax). E <= 256, C % 32 == 0. */
+int praxis_b200_router_logits(const void* x, const void* weight, int32_t weight_splits, int64_t tokens,
+                              int32_t dim, int32_t experts, float* logits, void* row_amax, int device,
+                              void* stream);
+
+/* Routing of fp32 logits [T, E]: sigmoid (or softmax) scores, + bias (fp32
+ * [E] or NULL), top-k (int64 [T, k], torch.topk's CUDA slot order incl.
+ * ties), gates bf16(score / sum) [T, k].
+ * Replaces praxis/layers.py:1647-1653 (== :2167-2173) and the routing half of
+ * praxis/kernels/router_fused.py:738-804 (route_dispatch). E <= 256, k <= 8. */
+int praxis_b200_route(const float* logits, const float* bias, int64_t tokens, int32_t experts, int32_t top_k,
+                      int32_t activation, int64_t* top_idx, void* gate, int device, void* stream);
+
+/* row_amax[r] = bf16(max |x[r, :]|) for bf16 x [rows, cols].
+ * Replaces praxis/kernels/nvfp4_moe.py:15-21. */
+int praxis_b200_row_amax(const void* x, int64_t rows, int32_t cols, void* out, int device, void* stream);
+
+/* Dispatch of top_idx [T, k] (int64) and gate [T, k] (bf16):
+ *   order[r], tokens[r] (int64), tokens32[r] (int32), sorted_gate[r] (bf16):
+ *      the stable expert-major order of the T*k (token, slot) rows;
+ *   inverse[p]: position of flat row p in that order;
+ *   offsets[e]: int32 end offsets; csr[E+1]; pcsr[E+1] (128-aligned starts);
+ *   tiles [max_tiles, 4] int32 {expert, first padded row, valid rows, 0} and
+ *      num_tiles[1]: the 128-row tiles holding routed rows, expert order;
+ *   act_global[e] (fp32) and act_amax[e] (fp32 bits) from row_amax [T] (bf16)
+ *      when row_amax != NULL: f32(bf16(max(amax, 1e-12))) * f32(1/2688).
+ * Any output pointer except csr, pcsr, tiles, num_tiles may be NULL.
+ * max_tiles = praxis_b200_padded_rows(T*k, E) / 128.
+ * Replaces praxis/layers.py:1330-1346 (_dispatch_rows),
+ * praxis/quantization/nvfp4.py:705-708 (inverse), praxis/kernels/nvfp4.py:37-41
+ * (_pad_csr), :344-352 (tile metadata), praxis/kernels/nvfp4_moe.py:24-57
+ * (segment global scales), and the dispatch half of
+ * praxis/kernels/router_fused.py:738-804. */
+size_t praxis_b200_dispatch_workspace_size(int64_t tokens, int32_t top_k, int32_t experts);
+int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
+                         int32_t top_k, int32_t experts, void* workspace, size_t workspace_size, int64_t* order,
+                         int64_t* inverse, int64_t* tokens_out, int32_t* tokens32, void* sorted_gate,
+                         int32_t* offsets, int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles,
+                         int32_t* num_tiles, float* act_global, uint32_t* act_amax, int device, void* stream);
+
+/* NVFP4 quantization of the routed rows (gathered from x [T, C] bf16 through
+ * inverse/top_idx) into the padded expert-grouped layout: q [Rp, C/2] (two
+ * E2M1 codes per byte, even element low), sf [Rp, C/16] (UE4M3, 128x4
+ * swizzled atoms); padding rows of the listed tiles are zeroed. Global scale
+ * per expert from act_global, or from act_amax when act_global is NULL.
+ * Replaces praxis/kernels/nvfp4.py:197-254 + :44-124 (quantize_activations
+ * with row_indices, alignment=128, grouped_scales=False). C % 64 == 0. */
+int praxis_b200_quantize_gather(const void* x, int64_t tokens, int32_t dim, const int64_t* top_idx,
+                                const int64_t* inverse, const int32_t* csr, const int32_t* pcsr,
+                                const float* act_global, const uint32_t* act_amax, int32_t top_k,
+                                int32_t experts, const int32_t* tiles, const int32_t* num_tiles,
+                                int32_t max_tiles, void* q, void* sf, int device, void* stream);
+
+/* NVFP4 quantization of every row of the listed tiles of x [Rp, K] (bf16),
+ * global per expert from globals, or from amax (fp32 bits) when NULL.
+ * Replaces praxis/kernels/nvfp4.py:197-254 for the hidden activations
+ * (praxis/quantization/nvfp4.py:365-372). K % 64 == 0. */
+int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, const int32_t* num_tiles,
+                              int32_t max_tiles, const float* globals, const uint32_t* amax, void* q, void* sf,
+                              int device, void* stream);
+
+/* Grouped NVFP4 GEMM on tcgen05: for each listed tile (expert e, rows r),
+ * acc[r, n] = sum_k dq(a[r, k]) * dq(b[e, n, k]) (alpha = 1), then the
+ * epilogue. a_q [Rp, K/2], a_sf [Rp, K/16], b_q [E, N, K/2], b_sf [E, N, K/16]
+ * (swizzled). EPI_PLAIN: out [Rp, N]. EPI_SWIGLU: b rows in 64-row gate/up
+ * blocks (praxis_b200_interleave_gate_up), out = hidden [Rp, N/2], amax_out[e]
+ * atomically maxed with the bits of max |hidden|. EPI_RESCALE: out [Rp, N].
+ * act_global (or act_amax) and w_global give bf16(g_act * g_w).
+ * Rows of a tile past its valid count are not stored (EPI_SWIGLU stores 0).
+ * Replaces praxis/kernels/nvfp4.py:355-419 (grouped_nvfp4_mm) with
+ * praxis/kernels/nvfp4_moe.py:102-158 (EPI_SWIGLU) or the rescale of
+ * praxis/kernels/nvfp4_moe.py:236-247 (EPI_RESCALE) fused. N, K % 128 == 0. */
+int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf,
+                             const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles,
+                             int64_t rows_padded, int32_t n, int32_t k, int32_t experts, int32_t epilogue,
+                             void* out, const float* act_global, const uint32_t* act_amax, const float* w_global,
+                             uint32_t* amax_out, int device, void* stream);
+
+/* Weighted combine: out[t] = bf16(((a0 + a1) + a2) + a3) with
+ * a_{s%4} += v_s * (f32(gate[t, s]) * f32(scaling)), v_s the routed row
+ * pcsr[e] + inverse[t*k+s] - csr[e] of rows [Rp, C] (bf16), rescaled by
+ * bf16(g_h[e] * g_w[e]) unless rows_rescaled; then out = bf16(out + shared)
+ * when shared != NULL. Replaces praxis/kernels/nvfp4_moe.py:206-311. */
+int praxis_b200_combine(const void* rows, int32_t cols, const int64_t* inverse, const int64_t* top_idx,
+                        const void* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
+                        const uint32_t* h_amax, const float* w_global, int32_t rows_rescaled, float scaling,
+                        const void* shared, void* out, int64_t tokens, int32_t top_k, int32_t experts, int device,
+                        void* stream);
+
+/* Packs expert-first bf16 weights w [E, K, N] (RoutedExperts layout: input
+ * features first) as W^T per expert: q [E, N, K/2], sf [E, N, K/16]
+ * (swizzled), global [E]. scratch: E uint32.
+ * Replaces praxis/quantization/nvfp4.py:67-146 (pack_routed_experts /
+ * _pack_matrix_cpu), same bytes. K % 64 == 0, N % 128 == 0. */
+int praxis_b200_pack_weights(const void* w, int32_t experts, int32_t k, int32_t n, void* q, void* sf,
+                             float* global_out, uint32_t* scratch, int device, void* stream);
+
+/* Copies gate_up q [E, 2F, C/2] / sf [E, 2F, C/16] into the fused-SwiGLU
+ * GEMM layout: 128-row blocks of 64 gate rows then the matching 64 up rows.
+ * Kernel-side layout only (the reference keeps gate rows 0..F-1, up rows
+ * F..2F-1: praxis/quantization/nvfp4.py:132-144). */
+int praxis_b200_interleave_gate_up(const void* q, const void* sf, int32_t experts, int32_t hidden, int32_t dim,
+                                   void* q_out, void* sf_out, int device, void* stream);
+
+/* One dispatch chunk of the routed bank (and optionally the router):
+ * NVFP4RoutedExperts.routed_forward[_with_shared] on SM100,
+ * praxis/quantization/nvfp4.py:490-544 and :616-747 for one chunk. */
+typedef struct praxis_b200_moe_args {
+  const void* x;             /* [T, C] bf16 */
+  const void* router_weight; /* [splits, E, C] bf16, or NULL: top_idx/gate are inputs */
+  int32_t router_splits;
+  int32_t activation;        /* PRAXIS_B200_SIGMOID / SOFTMAX */
+  const float* router_bias;  /* [E] or NULL */
+  int64_t* top_idx;          /* [T, k]: input, or output when router_weight != NULL */
+  void* gate;                /* [T, k] bf16: same */
+  const void* shared;        /* [T, C] bf16 or NULL */
+  void* out;                 /* [T, C] bf16 */
+  const void* gate_up_q;     /* interleaved layout (praxis_b200_interleave_gate_up) */
+  const void* gate_up_sf;
+  const float* gate_up_global;
+  const void* down_q;        /* [E, C, F/2] */
+  const void* down_sf;       /* [E, C, F/16] */
+  const float* down_global;
+  int64_t tokens;
+  int32_t dim;               /* C */
+  int32_t hidden;            /* F */
+  int32_t experts;           /* E */
+  int32_t top_k;
+  float scaling;
+  void* workspace;
+  size_t workspace_size;
+  int device;
+  void* stream;
+} praxis_b200_moe_args;
+
+size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,
+                                      int32_t with_router);
+int praxis_b200_moe_forward(const praxis_b200_moe_args* args);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRAXIS_B200_MOE_H */

@@ -1,0 +1,240 @@
+"""Drop-in routed NVFP4 bank for B200.
+
+``B200NVFP4RoutedExperts`` holds the reference's packed buffers (same names,
+shapes, dtypes and validation as praxis/quantization/nvfp4.py:149-227) and
+implements the routed-bank protocol that ``MoEFeedForward._routed_tail``
+calls (praxis/layers.py:2230-2270):
+
+    routed_forward(x, top_idx, gate, *, scaling, chunk_size, dispatch=None)
+    routed_forward_with_shared(x, top_idx, gate, *, scaling, chunk_size, shared, dispatch=None)
+
+so ``layer.routed = B200NVFP4RoutedExperts.from_packed(layer.routed.state_dict())``
+swaps the reference's FlashInfer/Triton kernels for this library's sm_100a
+kernels. The forward runs entirely on the GPU through the C ABI; there is no
+CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Mapping
+
+import torch
+from torch import Tensor, nn
+
+from . import ops
+
+PACKING_RECIPE = "qat-reciprocal-v1"
+_BUFFER_NAMES = frozenset(
+    ("gate_up_q", "gate_up_sf", "gate_up_global", "down_q", "down_sf", "down_global", "_unit_alpha")
+)
+
+
+def _validate(state: Mapping[str, Tensor]) -> tuple[int, int, int]:
+    """praxis/quantization/nvfp4.py:163-213."""
+    if not isinstance(state, Mapping) or set(state) != _BUFFER_NAMES:
+        raise ValueError("Unexpected NVFP4 packed buffer keys")
+    if any(
+        not isinstance(v, Tensor) or v.layout != torch.strided or not v.is_contiguous() or v.requires_grad
+        for v in state.values()
+    ):
+        raise ValueError("Reconstruction requires contiguous detached buffers")
+    gu = state["gate_up_q"]
+    if gu.ndim != 3:
+        raise ValueError("Expected grouped gate/up packed matrix")
+    e, n, k2 = gu.shape
+    c, h = k2 * 2, n // 2
+    if e <= 0 or c <= 0 or h <= 0 or n % 2 or c % 128 or h % 128:
+        raise ValueError("Invalid grouped NVFP4 dimensions")
+    expected = {
+        "gate_up_q": ((e, 2 * h, c // 2), torch.uint8),
+        "gate_up_sf": ((e, 2 * h, c // 16), torch.uint8),
+        "gate_up_global": ((e,), torch.float32),
+        "down_q": ((e, c, h // 2), torch.uint8),
+        "down_sf": ((e, c, h // 16), torch.uint8),
+        "down_global": ((e,), torch.float32),
+        "_unit_alpha": ((e,), torch.float32),
+    }
+    for name, (shape, dtype) in expected.items():
+        value = state[name]
+        if tuple(value.shape) != shape or value.dtype != dtype:
+            raise ValueError(f"Invalid NVFP4 buffer shape/dtype: {name}")
+        if name.endswith("_global"):
+            if not torch.isfinite(value).all().item() or not (value > 0).all().item():
+                raise ValueError(f"Invalid positive global scales: {name}")
+        if name.endswith("_sf"):
+            decoded = value.view(torch.float8_e4m3fn).float()
+            if not torch.isfinite(decoded).all().item() or (decoded < 0).any().item():
+                raise ValueError(f"Invalid E4M3 block scales: {name}")
+    if not torch.equal(state["_unit_alpha"].cpu(), torch.ones(e, dtype=torch.float32)):
+        raise ValueError("NVFP4 GEMM alpha must be one")
+    return e, c, h
+
+
+class B200NVFP4RoutedExperts(nn.Module):
+    """Packed NVFP4 routed experts executed by the sm_100a kernels.
+
+    Device moves are supported; dtype casts, training and gradients are not
+    (praxis/quantization/nvfp4.py:229-290). The fused SwiGLU GEMM reads the
+    gate/up weight in 64-row gate/up blocks: that copy is built on the device
+    by ``prepare()`` (called by the first forward; call it before capturing a
+    CUDA graph) and is not part of the state dict.
+    """
+
+    format = "nvfp4"
+    backend = "b200_sm100a_tcgen05_nvfp4"
+    ACCEPTS_DISPATCH = True
+
+    def __init__(self, state: Mapping[str, Tensor]) -> None:
+        super().__init__()
+        e, c, h = _validate(state)
+        self.num_experts, self.in_features, self.hidden_features = e, c, h
+        for name in sorted(_BUFFER_NAMES):
+            self.register_buffer(name, state[name].detach())
+        self._kernel_gate_up: tuple[Tensor, Tensor] | None = None
+        super().train(False)
+
+    @classmethod
+    def from_packed(cls, state: Mapping[str, Tensor]) -> B200NVFP4RoutedExperts:
+        return cls(state)
+
+    def train(self, mode: bool = True) -> B200NVFP4RoutedExperts:
+        if mode:
+            raise RuntimeError("NVFP4 routed experts support inference only")
+        super().train(False)
+        return self
+
+    def _apply(self, fn, recurse: bool = True) -> B200NVFP4RoutedExperts:
+        moved = {name: fn(value) for name, value in self._buffers.items()}
+        for name, value in self._buffers.items():
+            other = moved[name]
+            if other.dtype != value.dtype or other.shape != value.shape:
+                raise TypeError("NVFP4 buffers support device moves, not dtype/shape casts")
+        self._buffers.update(moved)
+        self._kernel_gate_up = None
+        return self
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        self._kernel_gate_up = None
+        super()._load_from_state_dict(*args, **kwargs)
+
+    def prepare(self) -> None:
+        """Build the kernel-layout gate/up copy on the buffers' device."""
+        if self.gate_up_q.device.type != "cuda":
+            raise RuntimeError("prepare() needs the bank on a CUDA device")
+        self._kernel_gate_up = ops.interleave_gate_up(self.gate_up_q, self.gate_up_sf)
+
+    def _kernel_weights(self) -> tuple[Tensor, Tensor]:
+        if self._kernel_gate_up is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("Call prepare() on the NVFP4 bank before CUDA Graph capture")
+            self.prepare()
+        return self._kernel_gate_up
+
+    # -- the routed-bank protocol -------------------------------------------
+    def routed_forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int,
+                       dispatch=None) -> Tensor:
+        """The scaled routed sum with the bf16 output boundary."""
+        return self._routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size)
+
+    def routed_forward_with_shared(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float,
+                                   chunk_size: int, shared: Tensor, dispatch=None) -> Tensor:
+        """Adds the shared expert after rounding the routed sum to bf16
+        (praxis/quantization/nvfp4.py:505-544, same fallback rule)."""
+        if (
+            shared.shape != x.shape
+            or shared.dtype != x.dtype
+            or shared.device != x.device
+            or not shared.is_contiguous()
+            or (torch.is_grad_enabled() and shared.requires_grad)
+        ):
+            return self.routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size) + shared
+        return self._routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size, shared=shared)
+
+    def forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int) -> Tensor:
+        return self.routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size)
+
+    def _check(self, x, top_idx, gate, scaling, chunk_size) -> None:
+        """praxis/quantization/nvfp4.py:630-682, the same errors."""
+        if self.training or (torch.is_grad_enabled() and (x.requires_grad or gate.requires_grad)):
+            raise RuntimeError("NVFP4 routed experts support inference only")
+        if (
+            x.ndim != 2
+            or x.shape[1] != self.in_features
+            or x.dtype != torch.bfloat16
+            or not x.is_contiguous()
+            or x.device.type != "cuda"
+        ):
+            raise ValueError("Expected contiguous CUDA BF16 routed activations")
+        if (
+            top_idx.ndim != 2
+            or top_idx.shape[0] != x.shape[0]
+            or not 1 <= top_idx.shape[1] <= min(8, self.num_experts)
+            or top_idx.dtype != torch.int64
+            or top_idx.device != x.device
+            or not top_idx.is_contiguous()
+        ):
+            raise ValueError("Expected contiguous CUDA int64 expert indices, top-k <= 8")
+        if gate.shape != top_idx.shape or gate.dtype != torch.bfloat16 or gate.device != x.device or not gate.is_contiguous():
+            raise ValueError("Expected contiguous CUDA BF16 gate weights")
+        if any(value.device != x.device for value in self.buffers()):
+            raise ValueError("Packed expert buffers and inputs must share a device")
+        if type(chunk_size) is not int or chunk_size <= 0:
+            raise ValueError("NVFP4 inference requires a positive dispatch chunk size")
+        if isinstance(scaling, bool) or not isinstance(scaling, float | int) or not math.isfinite(scaling):
+            raise ValueError("Routed scaling must be finite")
+        top_k = top_idx.shape[1]
+        if (min(chunk_size, x.shape[0]) * top_k + 127 * self.num_experts) * max(
+            self.in_features, 2 * self.hidden_features
+        ) >= 2**31 * 8:
+            raise ValueError("Routed chunk exceeds NVFP4 kernel indexing bounds")
+
+    def _routed_forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int,
+                        shared: Tensor | None = None) -> Tensor:
+        """The dispatch-chunk loop of praxis/quantization/nvfp4.py:683-747;
+        each chunk is one praxis_b200_moe_forward call."""
+        self._check(x, top_idx, gate, scaling, chunk_size)
+        gu_q, gu_sf = self._kernel_weights()
+        out = torch.empty_like(x)
+        for start in range(0, x.shape[0], chunk_size):
+            end = min(start + chunk_size, x.shape[0])
+            ops.moe_forward(
+                x[start:end], top_idx[start:end], gate[start:end], gu_q, gu_sf, self.gate_up_global,
+                self.down_q, self.down_sf, self.down_global, float(scaling),
+                None if shared is None else shared[start:end], out=out[start:end],
+            )
+        return out
+
+
+def pack_routed_experts(gate_up_weight: Tensor, down_weight: Tensor, *, keep_on_device: bool = False
+                        ) -> B200NVFP4RoutedExperts:
+    """Packs expert-first bf16 banks [E,C,2H] / [E,H,C] on the GPU with the
+    reference recipe (praxis/quantization/nvfp4.py:104-146, same bytes).
+    CPU banks are copied to the current CUDA device for packing; the packed
+    buffers come back to the CPU (as the reference returns them) unless
+    ``keep_on_device``."""
+    for weight in (gate_up_weight, down_weight):
+        if (
+            not isinstance(weight, Tensor)
+            or weight.ndim != 3
+            or weight.dtype != torch.bfloat16
+            or weight.layout != torch.strided
+            or weight.device.type == "meta"
+        ):
+            raise ValueError("Packing requires real BF16 expert-first banks")
+    e, c, doubled = gate_up_weight.shape
+    h = doubled // 2
+    if e <= 0 or c <= 0 or h <= 0 or doubled % 2 or c % 128 or h % 128 or tuple(down_weight.shape) != (e, h, c):
+        raise ValueError("Inconsistent routed banks; C and H must be multiples of 128")
+    if not torch.cuda.is_available():
+        raise RuntimeError("B200 NVFP4 packing runs on the GPU")
+    dev = gate_up_weight.device if gate_up_weight.device.type == "cuda" else torch.device("cuda")
+    state = {}
+    with torch.no_grad():
+        for name, weight in (("gate_up", gate_up_weight), ("down", down_weight)):
+            q, sf, g = ops.pack_weights(weight.to(dev).contiguous())
+            state[name + "_q"], state[name + "_sf"], state[name + "_global"] = q, sf, g
+        state["_unit_alpha"] = torch.ones(e, dtype=torch.float32, device=dev)
+    if not keep_on_device:
+        state = {k: v.cpu() for k, v in state.items()}
+    return B200NVFP4RoutedExperts.from_packed(state)

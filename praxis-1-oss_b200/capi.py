@@ -1,0 +1,142 @@
+"""ctypes binding of include/praxis_b200_moe.h.
+
+This is the reference-side stub a Python caller binds: plain pointers,
+sizes, a device ordinal and a ``cudaStream_t``. ``load()`` raises when the
+library is missing or cannot be loaded; nothing falls back to another path.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+from . import build as _build
+
+_LOCK = threading.Lock()
+_LIB: C.CDLL | None = None
+
+P = C.c_void_p
+I32 = C.c_int32
+I64 = C.c_int64
+F32 = C.c_float
+SZ = C.c_size_t
+
+OK, EINVAL, ECUDA, EUNSUPPORTED = 0, 1, 2, 3
+SIGMOID, SOFTMAX = 0, 1
+EPI_PLAIN, EPI_SWIGLU, EPI_RESCALE = 0, 1, 2
+
+
+class MoeArgs(C.Structure):
+    """``praxis_b200_moe_args``."""
+
+    _fields_ = [
+        ("x", P),
+        ("router_weight", P),
+        ("router_splits", I32),
+        ("activation", I32),
+        ("router_bias", P),
+        ("top_idx", P),
+        ("gate", P),
+        ("shared", P),
+        ("out", P),
+        ("gate_up_q", P),
+        ("gate_up_sf", P),
+        ("gate_up_global", P),
+        ("down_q", P),
+        ("down_sf", P),
+        ("down_global", P),
+        ("tokens", I64),
+        ("dim", I32),
+        ("hidden", I32),
+        ("experts", I32),
+        ("top_k", I32),
+        ("scaling", F32),
+        ("workspace", P),
+        ("workspace_size", SZ),
+        ("device", C.c_int),
+        ("stream", P),
+    ]
+
+
+# name -> (restype, argtypes); the order and types follow the header.
+SIGNATURES: dict[str, tuple] = {
+    "praxis_b200_abi_version": (C.c_int, []),
+    "praxis_b200_last_error": (C.c_char_p, []),
+    "praxis_b200_device_check": (C.c_int, [C.c_int]),
+    "praxis_b200_device_error": (C.c_int, [C.c_int, C.POINTER(C.c_uint32)]),
+    "praxis_b200_padded_rows": (I64, [I64, I32]),
+    "praxis_b200_router_logits": (C.c_int, [P, P, I32, I64, I32, I32, P, P, C.c_int, P]),
+    "praxis_b200_route": (C.c_int, [P, P, I64, I32, I32, I32, P, P, C.c_int, P]),
+    "praxis_b200_row_amax": (C.c_int, [P, I64, I32, P, C.c_int, P]),
+    "praxis_b200_dispatch_workspace_size": (SZ, [I64, I32, I32]),
+    "praxis_b200_dispatch": (
+        C.c_int,
+        [P, P, P, I64, I32, I32, P, SZ, P, P, P, P, P, P, P, P, P, I32, P, P, P, C.c_int, P],
+    ),
+    "praxis_b200_quantize_gather": (
+        C.c_int,
+        [P, I64, I32, P, P, P, P, P, P, I32, I32, P, P, I32, P, P, C.c_int, P],
+    ),
+    "praxis_b200_quantize_rows": (C.c_int, [P, I32, P, P, I32, P, P, P, P, C.c_int, P]),
+    "praxis_b200_grouped_gemm": (
+        C.c_int,
+        [P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, P, P, P, P, P, C.c_int, P],
+    ),
+    "praxis_b200_combine": (
+        C.c_int,
+        [P, I32, P, P, P, P, P, P, P, P, I32, F32, P, P, I64, I32, I32, C.c_int, P],
+    ),
+    "praxis_b200_pack_weights": (C.c_int, [P, I32, I32, I32, P, P, P, P, C.c_int, P]),
+    "praxis_b200_interleave_gate_up": (C.c_int, [P, P, I32, I32, I32, P, P, C.c_int, P]),
+    "praxis_b200_moe_workspace_size": (SZ, [I64, I32, I32, I32, I32, I32]),
+    "praxis_b200_moe_forward": (C.c_int, [C.POINTER(MoeArgs)]),
+}
+
+
+class PraxisB200Error(RuntimeError):
+    """A non-zero status from the C library."""
+
+
+def library_path() -> Path:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = False) -> C.CDLL:
+    """Load (once) and return the library with typed entry points."""
+    global _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        path = library_path()
+        if not path.exists():
+            if not build_if_missing:
+                raise PraxisB200Error(
+                    f"{path} is missing: build it first (python {Path(_build.__file__).name} or "
+                    "__graft_entry__.build())"
+                )
+            _build.build()
+        lib = C.CDLL(str(path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if lib.praxis_b200_abi_version() != 1:
+            raise PraxisB200Error("ABI version mismatch")
+        _LIB = lib
+        return lib
+
+
+def check(status: int) -> None:
+    if status != OK:
+        msg = load().praxis_b200_last_error().decode(errors="replace")
+        if status == EINVAL:
+            raise ValueError(msg)
+        raise PraxisB200Error(f"praxis_b200 status {status}: {msg}")
+
+
+def device_error(device: int) -> int:
+    """Read (and clear) the device error word; synchronizes the device."""
+    code = C.c_uint32(0)
+    check(load().praxis_b200_device_error(device, C.byref(code)))
+    return int(code.value)

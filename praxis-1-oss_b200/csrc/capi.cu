@@ -1,0 +1,354 @@
+// extern "C" entry points (include/praxis_b200_moe.h): argument checks,
+// device selection, workspace layout of the whole routed forward, and the
+// launch sequence of one dispatch chunk.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace praxis {
+
+// Internal entry points of the other .cu files.
+size_t dispatch_workspace_bytes(int64_t tokens, int top_k, int experts);
+int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* row_amax, int64_t tokens, int top_k,
+                 int experts, void* workspace, size_t workspace_bytes, int64_t* order, int64_t* inverse,
+                 int64_t* tokens_out, int32_t* tokens32, uint16_t* sorted_gate, int32_t* offsets, int32_t* csr,
+                 int32_t* pcsr, TileEntry* tiles, int max_tiles, int32_t* num_tiles, float* act_global,
+                 uint32_t* act_amax_bits, cudaStream_t stream);
+int run_row_amax(const uint16_t* x, int64_t rows, int cols, uint16_t* out, cudaStream_t stream);
+int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int64_t* top_idx, const int64_t* inverse,
+                        const int32_t* csr, const int32_t* pcsr, const float* globals, const uint32_t* amax_bits,
+                        int top_k, int experts, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
+                        uint8_t* q, uint8_t* sf, cudaStream_t stream);
+int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
+                      const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, cudaStream_t stream);
+int run_pack_weights(const uint16_t* w, int experts, int k_dim, int n_dim, uint8_t* q, uint8_t* sf, float* global_out,
+                     uint32_t* amax_scratch, cudaStream_t stream);
+int run_interleave_gate_up(const uint8_t* q, const uint8_t* sf, int experts, int f_dim, int c_dim, uint8_t* q_out,
+                           uint8_t* sf_out, cudaStream_t stream);
+int run_router_logits(const uint16_t* x, const uint16_t* w, int splits, int64_t tokens, int dim, int experts,
+                      float* logits, uint16_t* row_amax, cudaStream_t stream);
+int run_route(const float* logits, const float* bias, int64_t tokens, int experts, int top_k, int activation,
+              int64_t* top_idx, uint16_t* gate, cudaStream_t stream);
+int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx, const uint16_t* gate,
+                const int32_t* csr, const int32_t* pcsr, const float* h_global, const uint32_t* h_amax,
+                const float* w_global, int rows_rescaled, float scaling, const uint16_t* shared, uint16_t* out,
+                int64_t tokens, int top_k, int experts, cudaStream_t stream);
+
+static thread_local char g_message[1024] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_message, sizeof(g_message), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return PRAXIS_B200_OK;
+}
+
+static constexpr int kMaxDevices = 64;
+
+int sm_count() {
+  static int cache[kMaxDevices] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && cache[dev]) return cache[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < kMaxDevices) cache[dev] = n;
+  return n;
+}
+
+// Makes `device` current for this host thread and checks it is sm_100.
+static int use_device(int device) {
+  static int arch_ok[kMaxDevices] = {0};
+  if (device < 0 || device >= kMaxDevices) return set_error(PRAXIS_B200_EINVAL, "bad device %d", device);
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != device) {
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+  }
+  if (arch_ok[device] == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    arch_ok[device] = (major == 10 && minor == 0) ? 1 : -1;
+  }
+  if (arch_ok[device] < 0)
+    return set_error(PRAXIS_B200_EUNSUPPORTED, "device %d is not sm_100 (this library is built for sm_100a)", device);
+  return PRAXIS_B200_OK;
+}
+
+static int64_t padded_rows(int64_t rows, int64_t experts) { return (rows + 127 * experts) / 128 * 128; }
+
+// Workspace of one routed forward, 256-byte aligned pieces.
+struct MoeLayout {
+  size_t dispatch, row_amax, logits, inverse, csr, pcsr, offsets, tiles, num_tiles, act_amax, act_global, h_amax,
+      aq, asf, hidden, hq, hsf, rows, total;
+  int64_t rp;
+  int max_tiles;
+};
+
+static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int hidden, bool with_router) {
+  MoeLayout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  const int64_t r = tokens * top_k;
+  L.rp = padded_rows(r, experts);
+  L.max_tiles = (int)(L.rp / 128);
+  L.dispatch = take(dispatch_workspace_bytes(tokens, top_k, experts));
+  L.row_amax = take((size_t)tokens * 2);
+  L.logits = take(with_router ? (size_t)tokens * experts * 4 : 0);
+  L.inverse = take((size_t)r * 8);
+  L.csr = take((size_t)(experts + 1) * 4);
+  L.pcsr = take((size_t)(experts + 1) * 4);
+  L.offsets = take((size_t)experts * 4);
+  L.tiles = take((size_t)(L.max_tiles + 1) * sizeof(TileEntry));
+  L.num_tiles = take(4);
+  L.act_amax = take((size_t)experts * 4);
+  L.act_global = take((size_t)experts * 4);
+  L.h_amax = take((size_t)experts * 4);
+  L.aq = take((size_t)L.rp * dim / 2);
+  L.asf = take((size_t)L.rp * dim / 16);
+  L.hidden = take((size_t)L.rp * hidden * 2);
+  L.hq = take((size_t)L.rp * hidden / 2);
+  L.hsf = take((size_t)L.rp * hidden / 16);
+  L.rows = take((size_t)L.rp * dim * 2);
+  L.total = off;
+  return L;
+}
+
+}  // namespace praxis
+
+using namespace praxis;
+
+#define PRAXIS_STREAM(s) static_cast<cudaStream_t>(s)
+#define PRAXIS_DEVICE_OR_RETURN(d) \
+  do {                             \
+    int _rc = use_device(d);       \
+    if (_rc) return _rc;           \
+  } while (0)
+
+extern "C" {
+
+int praxis_b200_abi_version(void) { return PRAXIS_B200_ABI_VERSION; }
+
+const char* praxis_b200_last_error(void) { return g_message; }
+
+int praxis_b200_device_check(int device) {
+  if (use_device(device) != PRAXIS_B200_OK) return 0;
+  return sm_count();
+}
+
+int praxis_b200_device_error(int device, uint32_t* code) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "device error word: %s", cudaGetErrorString(e));
+  if (code) *code = v;
+  return PRAXIS_B200_OK;
+}
+
+int64_t praxis_b200_padded_rows(int64_t routed_rows, int32_t experts) { return padded_rows(routed_rows, experts); }
+
+int praxis_b200_router_logits(const void* x, const void* weight, int32_t weight_splits, int64_t tokens, int32_t dim,
+                              int32_t experts, float* logits, void* row_amax, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!x || !weight || !logits) return set_error(PRAXIS_B200_EINVAL, "router_logits: null pointer");
+  return run_router_logits(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(weight), weight_splits,
+                           tokens, dim, experts, logits, static_cast<uint16_t*>(row_amax), PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_route(const float* logits, const float* bias, int64_t tokens, int32_t experts, int32_t top_k,
+                      int32_t activation, int64_t* top_idx, void* gate, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!logits || !top_idx || !gate) return set_error(PRAXIS_B200_EINVAL, "route: null pointer");
+  return run_route(logits, bias, tokens, experts, top_k, activation, top_idx, static_cast<uint16_t*>(gate),
+                   PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_row_amax(const void* x, int64_t rows, int32_t cols, void* out, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!x || !out) return set_error(PRAXIS_B200_EINVAL, "row_amax: null pointer");
+  return run_row_amax(static_cast<const uint16_t*>(x), rows, cols, static_cast<uint16_t*>(out), PRAXIS_STREAM(stream));
+}
+
+size_t praxis_b200_dispatch_workspace_size(int64_t tokens, int32_t top_k, int32_t experts) {
+  return dispatch_workspace_bytes(tokens, top_k, experts);
+}
+
+int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
+                         int32_t top_k, int32_t experts, void* workspace, size_t workspace_size, int64_t* order,
+                         int64_t* inverse, int64_t* tokens_out, int32_t* tokens32, void* sorted_gate,
+                         int32_t* offsets, int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles,
+                         int32_t* num_tiles, float* act_global, uint32_t* act_amax, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!top_idx || !csr || !pcsr || !tiles || !num_tiles || !workspace)
+    return set_error(PRAXIS_B200_EINVAL, "dispatch: null pointer");
+  if (sorted_gate && !gate) return set_error(PRAXIS_B200_EINVAL, "dispatch: sorted_gate needs gate");
+  if (max_tiles < padded_rows(tokens * top_k, experts) / 128)
+    return set_error(PRAXIS_B200_EINVAL, "dispatch: max_tiles below padded_rows/128");
+  int32_t* off = offsets;
+  return run_dispatch(top_idx, static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(row_amax), tokens,
+                      top_k, experts, workspace, workspace_size, order, inverse, tokens_out, tokens32,
+                      static_cast<uint16_t*>(sorted_gate), off ? off : csr + 1, csr, pcsr,
+                      reinterpret_cast<TileEntry*>(tiles), max_tiles, num_tiles, act_global, act_amax,
+                      PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_quantize_gather(const void* x, int64_t tokens, int32_t dim, const int64_t* top_idx,
+                                const int64_t* inverse, const int32_t* csr, const int32_t* pcsr,
+                                const float* act_global, const uint32_t* act_amax, int32_t top_k, int32_t experts,
+                                const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles, void* q, void* sf,
+                                int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!x || !top_idx || !inverse || !csr || !pcsr || !tiles || !num_tiles || !q || !sf)
+    return set_error(PRAXIS_B200_EINVAL, "quantize_gather: null pointer");
+  return run_quantize_gather(static_cast<const uint16_t*>(x), tokens, dim, top_idx, inverse, csr, pcsr, act_global,
+                             act_amax, top_k, experts, reinterpret_cast<const TileEntry*>(tiles), num_tiles,
+                             max_tiles, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, const int32_t* num_tiles,
+                              int32_t max_tiles, const float* globals, const uint32_t* amax, void* q, void* sf,
+                              int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!x || !tiles || !num_tiles || !q || !sf) return set_error(PRAXIS_B200_EINVAL, "quantize_rows: null pointer");
+  return run_quantize_rows(static_cast<const uint16_t*>(x), k, reinterpret_cast<const TileEntry*>(tiles), num_tiles,
+                           max_tiles, globals, amax, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf),
+                           PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf,
+                             const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles, int64_t rows_padded,
+                             int32_t n, int32_t k, int32_t experts, int32_t epilogue, void* out,
+                             const float* act_global, const uint32_t* act_amax, const float* w_global,
+                             uint32_t* amax_out, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!a_q || !a_sf || !b_q || !b_sf || !tiles || !num_tiles || !out)
+    return set_error(PRAXIS_B200_EINVAL, "grouped_gemm: null pointer");
+  const int out_cols = epilogue == PRAXIS_B200_EPI_SWIGLU ? n / 2 : n;
+  return run_grouped_gemm(a_q, a_sf, b_q, b_sf, reinterpret_cast<const TileEntry*>(tiles), num_tiles, max_tiles,
+                          rows_padded, n, k, experts, epilogue, static_cast<uint16_t*>(out), out_cols, act_global,
+                          act_amax, w_global, amax_out, PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_combine(const void* rows, int32_t cols, const int64_t* inverse, const int64_t* top_idx,
+                        const void* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
+                        const uint32_t* h_amax, const float* w_global, int32_t rows_rescaled, float scaling,
+                        const void* shared, void* out, int64_t tokens, int32_t top_k, int32_t experts, int device,
+                        void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!rows || !inverse || !top_idx || !gate || !csr || !pcsr || !out)
+    return set_error(PRAXIS_B200_EINVAL, "combine: null pointer");
+  return run_combine(static_cast<const uint16_t*>(rows), cols, inverse, top_idx, static_cast<const uint16_t*>(gate),
+                     csr, pcsr, h_global, h_amax, w_global, rows_rescaled, scaling,
+                     static_cast<const uint16_t*>(shared), static_cast<uint16_t*>(out), tokens, top_k, experts,
+                     PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_pack_weights(const void* w, int32_t experts, int32_t k, int32_t n, void* q, void* sf,
+                             float* global_out, uint32_t* scratch, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!w || !q || !sf || !global_out || !scratch) return set_error(PRAXIS_B200_EINVAL, "pack_weights: null pointer");
+  return run_pack_weights(static_cast<const uint16_t*>(w), experts, k, n, static_cast<uint8_t*>(q),
+                          static_cast<uint8_t*>(sf), global_out, scratch, PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_interleave_gate_up(const void* q, const void* sf, int32_t experts, int32_t hidden, int32_t dim,
+                                   void* q_out, void* sf_out, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!q || !sf || !q_out || !sf_out) return set_error(PRAXIS_B200_EINVAL, "interleave: null pointer");
+  return run_interleave_gate_up(static_cast<const uint8_t*>(q), static_cast<const uint8_t*>(sf), experts, hidden, dim,
+                                static_cast<uint8_t*>(q_out), static_cast<uint8_t*>(sf_out), PRAXIS_STREAM(stream));
+}
+
+size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,
+                                      int32_t with_router) {
+  return moe_layout(tokens, top_k, experts, dim, hidden, with_router != 0).total;
+}
+
+int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
+  if (!a) return set_error(PRAXIS_B200_EINVAL, "moe_forward: null args");
+  PRAXIS_DEVICE_OR_RETURN(a->device);
+  const bool with_router = a->router_weight != nullptr;
+  if (!a->x || !a->top_idx || !a->gate || !a->out || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
+      !a->down_q || !a->down_sf || !a->down_global || !a->workspace)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: null pointer");
+  if (a->tokens < 0 || a->dim <= 0 || a->hidden <= 0 || a->experts <= 0 || a->top_k < 1 || a->top_k > 8 ||
+      a->top_k > a->experts)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: bad sizes");
+  if (a->dim % 128 || a->hidden % 128) return set_error(PRAXIS_B200_EINVAL, "moe_forward: C and F must be multiples of 128");
+  const int64_t r = a->tokens * a->top_k;
+  if ((r + 127 * (int64_t)a->experts) * (int64_t)(a->dim > 2 * a->hidden ? a->dim : 2 * a->hidden) >= ((int64_t)1 << 31) * 8)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: chunk exceeds the kernels' indexing range");
+  const MoeLayout L = moe_layout(a->tokens, a->top_k, a->experts, a->dim, a->hidden, with_router);
+  if (a->workspace_size < L.total)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: workspace %zu < %zu bytes", a->workspace_size, L.total);
+  if (a->tokens == 0) return PRAXIS_B200_OK;
+  cudaStream_t s = PRAXIS_STREAM(a->stream);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  uint16_t* row_amax = reinterpret_cast<uint16_t*>(ws + L.row_amax);
+  int64_t* inverse = reinterpret_cast<int64_t*>(ws + L.inverse);
+  int32_t* csr = reinterpret_cast<int32_t*>(ws + L.csr);
+  int32_t* pcsr = reinterpret_cast<int32_t*>(ws + L.pcsr);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  TileEntry* tiles = reinterpret_cast<TileEntry*>(ws + L.tiles);
+  int32_t* num_tiles = reinterpret_cast<int32_t*>(ws + L.num_tiles);
+  uint32_t* act_amax = reinterpret_cast<uint32_t*>(ws + L.act_amax);
+  float* act_global = reinterpret_cast<float*>(ws + L.act_global);
+  uint32_t* h_amax = reinterpret_cast<uint32_t*>(ws + L.h_amax);
+  uint8_t* aq = ws + L.aq;
+  uint8_t* asf = ws + L.asf;
+  uint16_t* hidden = reinterpret_cast<uint16_t*>(ws + L.hidden);
+  uint8_t* hq = ws + L.hq;
+  uint8_t* hsf = ws + L.hsf;
+  uint16_t* rows = reinterpret_cast<uint16_t*>(ws + L.rows);
+  const uint16_t* x = static_cast<const uint16_t*>(a->x);
+  uint16_t* gate = static_cast<uint16_t*>(a->gate);
+  int rc;
+  if (with_router) {
+    float* logits = reinterpret_cast<float*>(ws + L.logits);
+    rc = run_router_logits(x, static_cast<const uint16_t*>(a->router_weight), a->router_splits, a->tokens, a->dim,
+                           a->experts, logits, row_amax, s);
+    if (rc) return rc;
+    rc = run_route(logits, a->router_bias, a->tokens, a->experts, a->top_k, a->activation, a->top_idx, gate, s);
+  } else {
+    rc = run_row_amax(x, a->tokens, a->dim, row_amax, s);
+  }
+  if (rc) return rc;
+  rc = run_dispatch(a->top_idx, gate, row_amax, a->tokens, a->top_k, a->experts, ws + L.dispatch,
+                    L.row_amax - L.dispatch, nullptr, inverse, nullptr, nullptr, nullptr, offsets, csr, pcsr, tiles,
+                    L.max_tiles, num_tiles, act_global, act_amax, s);
+  if (rc) return rc;
+  rc = run_quantize_gather(x, a->tokens, a->dim, a->top_idx, inverse, csr, pcsr, act_global, nullptr, a->top_k,
+                           a->experts, tiles, num_tiles, L.max_tiles, aq, asf, s);
+  if (rc) return rc;
+  cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * a->experts, s);
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
+  rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
+                        a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
+                        h_amax, s);
+  if (rc) return rc;
+  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq, hsf, s);
+  if (rc) return rc;
+  rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
+                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, s);
+  if (rc) return rc;
+  return run_combine(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
+                     a->scaling, static_cast<const uint16_t*>(a->shared), static_cast<uint16_t*>(a->out), a->tokens,
+                     a->top_k, a->experts, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,99 @@
+// Weighted combine of the routed rows back to tokens (+ shared expert).
+//
+// Replaces praxis/kernels/nvfp4_moe.py:206-311 (_rescale_combine), the same
+// arithmetic in the same order, without FMA contraction:
+//   per token t and slot s: i = inverse[t*k+s], e = top[t,s],
+//   src = pcsr[e] + i - csr[e]
+//   v = bf16(raw[src] * bf16(g_h[e] * g_w[e]))   (skipped when the down GEMM
+//                                                  epilogue already did it)
+//   acc[s % 4] += v * (f32(gate[t,s]) * f32(scaling))
+//   y = bf16(((acc0 + acc1) + acc2) + acc3);  y = bf16(y + shared)
+// One warp per token, 16-byte gathers of the routed rows.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace praxis {
+
+__global__ void __launch_bounds__(256) combine_kernel(
+    const uint16_t* __restrict__ rows, int cols, const int64_t* __restrict__ inverse,
+    const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate, const int32_t* __restrict__ csr,
+    const int32_t* __restrict__ pcsr, const float* __restrict__ h_global, const uint32_t* __restrict__ h_amax,
+    const float* __restrict__ w_global, int rows_rescaled, float scaling, const uint16_t* __restrict__ shared,
+    uint16_t* __restrict__ out, int64_t tokens, int top_k, int experts) {
+  __shared__ int64_t s_src[8][8];
+  __shared__ float s_scale[8][8], s_mult[8][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+  if (t >= tokens) return;
+  if (lane < top_k) {
+    const int64_t p = t * top_k + lane;
+    int64_t e64 = top_idx[p];
+    int e = (int)e64;
+    if (e64 < 0 || e64 >= experts) {
+      record_error(kErrIndexRange);
+      e = e64 < 0 ? 0 : experts - 1;
+    }
+    s_src[warp][lane] = (int64_t)pcsr[e] + inverse[p] - csr[e];
+    s_scale[warp][lane] = mul_rn(bf16_to_f32(gate[p]), scaling);
+    float mult = 1.0f;
+    if (!rows_rescaled) {
+      const float gh = h_global != nullptr ? h_global[e] : global_from_amax_bits(h_amax[e]);
+      mult = bf16_round(mul_rn(gh, w_global[e]));
+    }
+    s_mult[warp][lane] = mult;
+  }
+  __syncwarp();
+  for (int c = lane * 8; c < cols; c += 256) {
+    float acc[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[a][i] = 0.0f;
+    for (int s = 0; s < top_k; ++s) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + s_src[warp][s] * cols + c));
+      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+      const float sc = s_scale[warp][s], mult = s_mult[warp][s];
+      const int a = s & 3;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float val = bf16_to_f32((uint16_t)((wv[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu));
+        if (!rows_rescaled) val = bf16_round(mul_rn(val, mult));
+        acc[a][i] = add_rn(acc[a][i], mul_rn(val, sc));
+      }
+    }
+    uint32_t packed[4];
+    uint4 sh = make_uint4(0, 0, 0, 0);
+    if (shared != nullptr) sh = __ldg(reinterpret_cast<const uint4*>(shared + t * cols + c));
+    const uint32_t shv[4] = {sh.x, sh.y, sh.z, sh.w};
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      uint32_t h2[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float y = bf16_round(add_rn(add_rn(add_rn(acc[0][i + j], acc[1][i + j]), acc[2][i + j]), acc[3][i + j]));
+        if (shared != nullptr) y = add_rn(y, bf16_to_f32((uint16_t)((shv[(i + j) >> 1] >> (((i + j) & 1) * 16)) & 0xFFFFu)));
+        h2[j] = f32_to_bf16(y);
+      }
+      packed[i >> 1] = h2[0] | (h2[1] << 16);
+    }
+    *reinterpret_cast<uint4*>(out + t * cols + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+}
+
+int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx, const uint16_t* gate,
+                const int32_t* csr, const int32_t* pcsr, const float* h_global, const uint32_t* h_amax,
+                const float* w_global, int rows_rescaled, float scaling, const uint16_t* shared, uint16_t* out,
+                int64_t tokens, int top_k, int experts, cudaStream_t stream) {
+  if (cols % 8 != 0) return set_error(PRAXIS_B200_EINVAL, "combine needs C %% 8 == 0");
+  if (top_k < 1 || top_k > 8) return set_error(PRAXIS_B200_EINVAL, "top_k must be 1..8");
+  if (!rows_rescaled && (w_global == nullptr || (h_global == nullptr && h_amax == nullptr)))
+    return set_error(PRAXIS_B200_EINVAL, "combine needs global scales to rescale raw rows");
+  if (tokens == 0) return PRAXIS_B200_OK;
+  const int64_t blocks = (tokens + 7) / 8;
+  combine_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, cols, inverse, top_idx, gate, csr, pcsr, h_global, h_amax,
+                                                        w_global, rows_rescaled, scaling, shared, out, tokens, top_k,
+                                                        experts);
+  return check_launch("combine");
+}
+
+}  // namespace praxis

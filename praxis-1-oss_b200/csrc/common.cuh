@@ -1,0 +1,318 @@
+// Shared device helpers for the sm_100a MoE kernels: bf16/fp8/fp4 element
+// conversions, mbarriers with bounded waits, TMA and tcgen05 wrappers.
+//
+// Every wait on an mbarrier is bounded (wall-clock limit from %globaltimer):
+// on expiry the waiting thread records a code in the device error word and
+// returns false, so a kernel never hangs the GPU; the host reads the word at
+// a sync point (praxis_b200_device_error).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/praxis_b200_moe.h"
+
+namespace praxis {
+
+// ---------------------------------------------------------------------------
+// Device error word (one per device, cleared by the host after reading)
+// ---------------------------------------------------------------------------
+// Defined here: the library is one translation unit (praxis_b200_moe.cu).
+__device__ unsigned int g_device_error = 0;
+
+enum DeviceError : unsigned int {
+  kErrNone = 0,
+  kErrTimeoutProducer = 1,
+  kErrTimeoutMma = 2,
+  kErrTimeoutEpilogue = 3,
+  kErrIndexRange = 4,
+};
+
+__device__ __forceinline__ void record_error(unsigned int code) {
+  atomicCAS(&g_device_error, 0u, code);
+}
+
+__device__ __forceinline__ bool error_raised() {
+  return *((volatile unsigned int*)&g_device_error) != 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Numeric helpers (explicit roundings; nothing here may be contracted)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) {
+  return __uint_as_float(((uint32_t)b) << 16);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  __nv_bfloat16 h = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+__device__ __forceinline__ float bf16_round(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// float -> e4m3 (RNE, satfinite) as a byte; input already clamped to [2^-6, 448].
+__device__ __forceinline__ uint32_t f32_to_e4m3_byte(float f) {
+  uint16_t pair;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(pair) : "f"(0.0f), "f"(f));
+  return (uint32_t)(pair & 0xFFu);
+}
+
+// e4m3 byte -> float (exact).
+__device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
+  uint32_t h2;
+  uint16_t in = (uint16_t)(b & 0xFFu);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(in));
+  __half h = __ushort_as_half((unsigned short)(h2 & 0xFFFFu));
+  return __half2float(h);
+}
+
+// Two floats -> one byte of two E2M1 codes: `lo` in bits 0-3, `hi` in 4-7
+// (round to nearest even, satfinite).
+__device__ __forceinline__ uint32_t f32x2_to_e2m1_byte(float lo, float hi) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n\t"
+      "cvt.u32.u8 %0, b;\n\t}"
+      : "=r"(out)
+      : "f"(hi), "f"(lo));
+  return out;
+}
+
+// IEEE round-to-nearest division and product/sum with no contraction.
+__device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+
+// Triton's fp32 sigmoid as the reference's SwiGLU kernels compile it:
+// 1 / (1 + ex2.approx(-x * log2 e)) with an IEEE division.
+__device__ __forceinline__ float sigmoid_triton(float x) {
+  float t = mul_rn(-x, 1.4426950408889634f);
+  float e;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t));
+  return div_rn(1.0f, add_rn(1.0f, e));
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory addresses and mbarriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete. Bounded: gives up
+// after `limit_ns` of wall time (or when another thread already raised an
+// error), records `code` and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code,
+                                          uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t start = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0u) {
+      if (error_raised()) return false;
+      if (globaltimer_ns() - start > limit_ns) {
+        record_error(code);
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (no multicast anywhere in this library)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
+}
+
+// 2-D tiled load; c0 is the innermost coordinate in elements (bytes here),
+// always a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* desc, uint64_t* bar, int32_t c0,
+                                            int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 1-D bulk copy global -> shared; both addresses 16-byte aligned, size a
+// multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor core, accumulators in tensor memory)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrive on an mbarrier once every tcgen05 operation issued so far by this
+// thread has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// Block-scaled FP4 x FP4 -> FP32 MMA, 16-element blocks with UE4M3 scales,
+// both operands K-major in shared memory, scales in tensor memory.
+__device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Copy 32 rows x 128 bits from shared memory into tensor memory, replicated
+// into all four 32-lane sub-partitions (the scale-factor layout the
+// block-scaled MMA reads).
+__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 format): start address, leading
+// and stride byte offsets (16-byte units), version 1, layout type.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout_type) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version for sm_100
+  d |= (uint64_t)(layout_type & 7u) << 61;
+  return d;
+}
+
+constexpr uint32_t kLayoutSwizzleNone = 0;
+constexpr uint32_t kLayoutSwizzle128B = 2;
+
+// Instruction descriptor of kind::mxf4nvf4 (E2M1 x E2M1, UE4M3 scales,
+// K-major A and B, dense K = 64, F32 accumulate).
+__host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t m, uint32_t n) {
+  return (1u << 7)                 // A format: E2M1
+         | (1u << 10)              // B format: E2M1
+         | ((n >> 3) << 17)        // N / 8
+         | (0u << 23)              // scale format: UE4M3
+         | ((m >> 4) << 24);       // M / 16
+}
+
+__device__ __forceinline__ uint32_t lane_id() {
+  uint32_t l;
+  asm volatile("mov.u32 %0, %%laneid;" : "=r"(l));
+  return l;
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// ---------------------------------------------------------------------------
+// Tile table entry written by the dispatch kernel, read by GEMMs/quantize
+// ---------------------------------------------------------------------------
+struct TileEntry {
+  int32_t expert;  // expert of the 128-row tile
+  int32_t row0;    // first padded row of the tile
+  int32_t valid;   // rows of the tile that hold routed rows (1..128)
+  int32_t pad;
+};
+
+constexpr int kTileRows = 128;
+
+}  // namespace praxis

@@ -1,0 +1,297 @@
+// Token dispatch: stable expert-major permutation, CSR offsets, padded CSR,
+// 128-row tile table and per-expert activation global scales.
+//
+// Replaces, with identical values:
+//   praxis/layers.py:1330-1346            _dispatch_rows (stable sort by expert,
+//                                         tokens, sorted gates, int32 end offsets)
+//   praxis/quantization/nvfp4.py:705-708  inverse[order] = arange(R)
+//   praxis/kernels/nvfp4.py:37-41         _pad_csr (alignment 128)
+//   praxis/kernels/nvfp4.py:344-352       per-tile expert metadata (here: only
+//                                         tiles that hold routed rows)
+//   praxis/kernels/nvfp4_moe.py:15-57     row max |x| and per-expert global scale
+//
+// Three launches, no host synchronisation and no atomics on the data path:
+//   1. count   one warp per segment of positions: per-segment expert
+//              histogram and max row-amax (warp-aggregated shared atomics)
+//   2. scan    one CTA: per-expert exclusive scan over segments, block scan
+//              over experts -> csr, pcsr, offsets, tiles, global scales
+//   3. scatter one warp per segment, positions in order; rank among equal
+//              experts by __match_any_sync -> bit-exact stable order
+#include "common.cuh"
+#include "kernels.h"
+
+namespace praxis {
+
+constexpr int kDispatchWarps = 8;
+constexpr int kMaxExperts = 1024;
+
+__device__ __forceinline__ int clamp_expert(int64_t e, int experts) {
+  if (e < 0 || e >= experts) {
+    record_error(kErrIndexRange);
+    return e < 0 ? 0 : experts - 1;
+  }
+  return (int)e;
+}
+
+// ---------------------------------------------------------------------------
+// Row max |x| (bf16), praxis/kernels/nvfp4_moe.py:15-21
+// ---------------------------------------------------------------------------
+__global__ void row_amax_kernel(const uint16_t* __restrict__ x, int64_t rows, int cols, uint16_t* __restrict__ out) {
+  const int warps = blockDim.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
+  float m = 0.0f;
+  for (int i = lane; i < cols / 8; i += 32) {
+    uint4 v = __ldg(src + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m = fmaxf(m, fabsf(bf16_to_f32((uint16_t)(w[j] & 0xFFFFu))));
+      m = fmaxf(m, fabsf(bf16_to_f32((uint16_t)(w[j] >> 16))));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) out[row] = f32_to_bf16(m);
+}
+
+// ---------------------------------------------------------------------------
+// 1. count
+// ---------------------------------------------------------------------------
+__global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ row_amax,
+                                      int64_t positions, int top_k, int experts, int seg_len, int segments,
+                                      int32_t* __restrict__ seg_count, uint32_t* __restrict__ seg_max) {
+  extern __shared__ uint32_t s_dc[];
+  uint32_t* hist = s_dc;                                  // [warps][experts]
+  uint32_t* hmax = s_dc + kDispatchWarps * experts;       // [warps][experts]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kDispatchWarps * experts; i += blockDim.x) {
+    hist[i] = 0;
+    hmax[i] = 0;
+  }
+  __syncthreads();
+  const int seg = blockIdx.x * kDispatchWarps + warp;
+  if (seg < segments) {
+    const int64_t begin = (int64_t)seg * seg_len;
+    const int64_t end = min(positions, begin + seg_len);
+    uint32_t* h = hist + warp * experts;
+    uint32_t* hm = hmax + warp * experts;
+    for (int64_t p0 = begin; p0 < end; p0 += 32) {
+      const int64_t p = p0 + lane;
+      const bool live = p < end;
+      const int e = live ? clamp_expert(top_idx[p], experts) : -1;
+      const uint32_t peers = __match_any_sync(0xffffffffu, e);
+      const int leader = __ffs(peers) - 1;
+      if (live && lane == leader) atomicAdd(&h[e], (uint32_t)__popc(peers));
+      if (live && row_amax != nullptr) {
+        const uint32_t bits = __float_as_uint(bf16_to_f32(row_amax[p / top_k]));
+        atomicMax(&hm[e], bits);
+      }
+    }
+  }
+  __syncwarp();
+  if (seg < segments) {
+    for (int e = lane; e < experts; e += 32) {
+      seg_count[(int64_t)seg * experts + e] = (int32_t)hist[warp * experts + e];
+      seg_max[(int64_t)seg * experts + e] = hmax[warp * experts + e];
+    }
+  }
+}
+
+// Block-wide exclusive scan of one value per thread (blockDim.x <= 1024).
+__device__ int block_exclusive_scan(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nwarps ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nwarps) s_warp[lane] = w;
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? s_warp[warp - 1] : 0) + x - v;
+  if (total) *total = s_warp[nwarps - 1];
+  __syncthreads();
+  return before;
+}
+
+// ---------------------------------------------------------------------------
+// 2. scan (single CTA of 1024 threads; experts <= 1024)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(
+    int32_t* __restrict__ seg_count, const uint32_t* __restrict__ seg_max, int segments, int experts,
+    int64_t positions, int align, int32_t* __restrict__ offsets, int32_t* __restrict__ csr,
+    int32_t* __restrict__ pcsr, TileEntry* __restrict__ tiles, int max_tiles, int32_t* __restrict__ num_tiles,
+    float* __restrict__ act_global, uint32_t* __restrict__ act_amax_bits) {
+  __shared__ int s_warp[32];
+  const int e = threadIdx.x;
+  int count = 0;
+  uint32_t m = 0;
+  if (e < experts) {
+    // exclusive scan over segments in place: seg_count becomes the offset of
+    // the segment's first row inside the expert.
+    for (int s = 0; s < segments; ++s) {
+      const int64_t i = (int64_t)s * experts + e;
+      const int c = seg_count[i];
+      seg_count[i] = count;
+      count += c;
+      m = max(m, seg_max[i]);
+    }
+  }
+  int total = 0;
+  const int start = block_exclusive_scan(e < experts ? count : 0, s_warp, &total);
+  if (e < experts) {
+    csr[e] = start;
+    offsets[e] = start + count;
+    if (e == experts - 1) csr[experts] = start + count;
+    const int64_t pstart = ((int64_t)start + (int64_t)(align - 1) * e) / align * align;
+    pcsr[e] = (int32_t)pstart;
+    if (e == experts - 1)
+      pcsr[experts] = (int32_t)(((int64_t)start + count + (int64_t)(align - 1) * experts) / align * align);
+    if (act_amax_bits) act_amax_bits[e] = m;
+    if (act_global) act_global[e] = global_from_amax_bits(m);
+  }
+  // Tile table: ceil(count / 128) tiles per expert, in expert order.
+  const int ntile = e < experts ? (count + kTileRows - 1) / kTileRows : 0;
+  int tiles_total = 0;
+  const int tstart = block_exclusive_scan(ntile, s_warp, &tiles_total);
+  if (e < experts) {
+    const int64_t pstart = ((int64_t)start + (int64_t)(align - 1) * e) / align * align;
+    for (int j = 0; j < ntile; ++j) {
+      if (tstart + j < max_tiles) {
+        TileEntry t;
+        t.expert = e;
+        t.row0 = (int32_t)(pstart + (int64_t)j * kTileRows);
+        t.valid = min(kTileRows, count - j * kTileRows);
+        t.pad = 0;
+        tiles[tstart + j] = t;
+      } else {
+        record_error(kErrIndexRange);
+      }
+    }
+  }
+  if (threadIdx.x == 0) *num_tiles = min(tiles_total, max_tiles);
+}
+
+// ---------------------------------------------------------------------------
+// 3. scatter
+// ---------------------------------------------------------------------------
+__global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate,
+                                        int64_t positions, int top_k, int experts, int seg_len, int segments,
+                                        const int32_t* __restrict__ seg_start, const int32_t* __restrict__ csr,
+                                        int64_t* __restrict__ order, int64_t* __restrict__ inverse,
+                                        int64_t* __restrict__ tokens, int32_t* __restrict__ tokens32,
+                                        uint16_t* __restrict__ sorted_gate) {
+  extern __shared__ int32_t s_cursor[];  // [warps][experts]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seg = blockIdx.x * kDispatchWarps + warp;
+  if (seg >= segments) return;
+  int32_t* cur = s_cursor + warp * experts;
+  for (int e = lane; e < experts; e += 32) cur[e] = csr[e] + seg_start[(int64_t)seg * experts + e];
+  __syncwarp();
+  const int64_t begin = (int64_t)seg * seg_len;
+  const int64_t end = min(positions, begin + seg_len);
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int64_t p0 = begin; p0 < end; p0 += 32) {
+    const int64_t p = p0 + lane;
+    const bool live = p < end;
+    const int e = live ? clamp_expert(top_idx[p], experts) : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    int dest = 0;
+    if (live) dest = cur[e] + __popc(peers & lt);
+    __syncwarp();
+    if (live && lane == __ffs(peers) - 1) cur[e] += __popc(peers);
+    __syncwarp();
+    if (live) {
+      if (order) order[dest] = p;
+      if (inverse) inverse[p] = dest;
+      if (tokens) tokens[dest] = p / top_k;
+      if (tokens32) tokens32[dest] = (int32_t)(p / top_k);
+      if (sorted_gate) sorted_gate[dest] = gate[p];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host entry
+// ---------------------------------------------------------------------------
+static void dispatch_geometry(int64_t positions, int* seg_len, int* segments) {
+  // Segments of >= 256 positions, at most 2048 of them (bounds the serial
+  // per-expert scan of the single-CTA pass).
+  int64_t len = 256;
+  while ((positions + len - 1) / len > 2048) len *= 2;
+  *seg_len = (int)len;
+  *segments = (int)((positions + len - 1) / len);
+  if (*segments == 0) *segments = 1;
+}
+
+size_t dispatch_workspace_bytes(int64_t tokens, int top_k, int experts) {
+  int seg_len, segments;
+  dispatch_geometry(tokens * top_k, &seg_len, &segments);
+  return (size_t)segments * experts * 8 + 256;
+}
+
+int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* row_amax, int64_t tokens, int top_k,
+                 int experts, void* workspace, size_t workspace_bytes, int64_t* order, int64_t* inverse,
+                 int64_t* tokens_out, int32_t* tokens32, uint16_t* sorted_gate, int32_t* offsets, int32_t* csr,
+                 int32_t* pcsr, TileEntry* tiles, int max_tiles, int32_t* num_tiles, float* act_global,
+                 uint32_t* act_amax_bits, cudaStream_t stream) {
+  if (experts <= 0 || experts > kMaxExperts) return set_error(PRAXIS_B200_EINVAL, "experts must be 1..%d", kMaxExperts);
+  if (top_k <= 0 || tokens < 0) return set_error(PRAXIS_B200_EINVAL, "bad tokens/top_k");
+  if (tokens * top_k >= (int64_t)1 << 31) return set_error(PRAXIS_B200_EINVAL, "too many routed rows");
+  if (workspace_bytes < dispatch_workspace_bytes(tokens, top_k, experts))
+    return set_error(PRAXIS_B200_EINVAL, "dispatch workspace too small");
+  const int64_t positions = tokens * top_k;
+  int seg_len, segments;
+  dispatch_geometry(positions, &seg_len, &segments);
+  int32_t* seg_count = static_cast<int32_t*>(workspace);
+  uint32_t* seg_max = reinterpret_cast<uint32_t*>(seg_count + (size_t)segments * experts);
+  const int blocks = (segments + kDispatchWarps - 1) / kDispatchWarps;
+  const size_t smem_count = (size_t)2 * kDispatchWarps * experts * 4;
+  const size_t smem_scatter = (size_t)kDispatchWarps * experts * 4;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(dispatch_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kDispatchWarps * kMaxExperts * 4);
+    cudaFuncSetAttribute(dispatch_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDispatchWarps * kMaxExperts * 4);
+    attr_done = true;
+  }
+  dispatch_count_kernel<<<blocks, 32 * kDispatchWarps, smem_count, stream>>>(
+      top_idx, row_amax, positions, top_k, experts, seg_len, segments, seg_count, seg_max);
+  int rc = check_launch("dispatch_count");
+  if (rc) return rc;
+  dispatch_scan_kernel<<<1, 1024, 0, stream>>>(seg_count, seg_max, segments, experts, positions, kTileRows, offsets,
+                                               csr, pcsr, tiles, max_tiles, num_tiles,
+                                               row_amax ? act_global : nullptr, row_amax ? act_amax_bits : nullptr);
+  rc = check_launch("dispatch_scan");
+  if (rc) return rc;
+  if (positions > 0) {
+    dispatch_scatter_kernel<<<blocks, 32 * kDispatchWarps, smem_scatter, stream>>>(
+        top_idx, gate, positions, top_k, experts, seg_len, segments, seg_count, csr, order, inverse, tokens_out,
+        tokens32, sorted_gate);
+    rc = check_launch("dispatch_scatter");
+  }
+  return rc;
+}
+
+int run_row_amax(const uint16_t* x, int64_t rows, int cols, uint16_t* out, cudaStream_t stream) {
+  if (cols % 8 != 0) return set_error(PRAXIS_B200_EINVAL, "row_amax needs cols % 8 == 0");
+  if (rows == 0) return PRAXIS_B200_OK;
+  const int warps = 8;
+  const int64_t blocks = (rows + warps - 1) / warps;
+  row_amax_kernel<<<(unsigned)blocks, 32 * warps, 0, stream>>>(x, rows, cols, out);
+  return check_launch("row_amax");
+}
+
+}  // namespace praxis

@@ -1,0 +1,380 @@
+// Grouped NVFP4 x NVFP4 GEMM for routed experts on sm_100a (tcgen05).
+//
+// Replaces praxis/kernels/nvfp4.py:355-419 (grouped_nvfp4_mm -> FlashInfer's
+// CuTe-DSL block-scaled contiguous grouped GEMM, alpha = 1, 128-row expert
+// tiles) and fuses the element-wise stage that follows it:
+//   EPI_PLAIN   out = bf16(acc)
+//   EPI_SWIGLU  praxis/kernels/nvfp4_moe.py:102-133 (rescale, SwiGLU with
+//               Triton's sigmoid, every bf16 rounding kept) + the per-expert
+//               max |hidden| that praxis/kernels/nvfp4_moe.py:60-81 reduces
+//   EPI_RESCALE bf16(bf16(acc) * bf16(g_a * g_w)), the first step of
+//               praxis/kernels/nvfp4_moe.py:236-247 (rescale_combine)
+//
+// Design (one CTA per SM, persistent over (m-tile, n-tile) units):
+//   warp 0      TMA producer: A and B tiles (2-D, 128B swizzle) and the
+//               pre-swizzled scale atoms (1-D bulk copies) into a 5-stage ring
+//   warp 1      tcgen05 issuer: scale atoms smem -> TMEM (tcgen05.cp), then
+//               kind::mxf4nvf4 block16 MMAs (M=128, N=BLOCK_N, K=64) into a
+//               double-buffered TMEM accumulator
+//   warps 2..5  epilogue: TMEM -> registers (tcgen05.ld), fused math, stores
+// Every mbarrier wait is bounded (see common.cuh).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace praxis {
+
+template <int BLOCK_N>
+struct GemmShape {
+  static constexpr int BM = kTileRows;          // rows per tile
+  static constexpr int BK_BYTES = 128;          // 256 FP4 values per k-tile
+  static constexpr int STAGES = 5;
+  static constexpr int A_BYTES = BM * BK_BYTES;  // 16 KB
+  static constexpr int B_BYTES = BLOCK_N * BK_BYTES;
+  static constexpr int SF_ATOM = 512;           // 128 rows x 4 scales
+  static constexpr int SFA_BYTES = 4 * SF_ATOM;
+  static constexpr int SFB_BYTES = (BLOCK_N / 128) * 4 * SF_ATOM;
+  static constexpr int ACC_BUFS = 2;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SFA_COL = ACC_BUFS * BLOCK_N;  // 4 columns per k-block
+  static constexpr int SFB_COL = SFA_COL + 16;        // (BLOCK_N/128)*4 per k-block
+  static constexpr size_t SMEM_BYTES =
+      1024 + (size_t)STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES) + 256;
+  static_assert(SFB_COL + 4 * (BLOCK_N / 128) * 4 <= TMEM_COLS, "tensor memory budget");
+};
+
+__device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&packed)[16]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    d[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+}
+
+__device__ __forceinline__ float expert_multiplier(const GemmParams& p, int e) {
+  // bf16(g_a * g_w) in float32 (praxis/kernels/nvfp4_moe.py:117-121, :237-241)
+  float ga;
+  if (p.act_global != nullptr) {
+    ga = p.act_global[e];
+  } else {
+    ga = global_from_amax_bits(p.act_amax[e]);
+  }
+  return bf16_round(mul_rn(ga, p.w_global[e]));
+}
+
+template <int BLOCK_N, int EPI>
+__global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constant__ GemmParams p) {
+  using S = GemmShape<BLOCK_N>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + S::STAGES * S::A_BYTES;
+  uint8_t* sSFA = sB + S::STAGES * S::B_BYTES;
+  uint8_t* sSFB = sSFA + S::STAGES * S::SFA_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + S::STAGES * S::SFB_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S::STAGES;
+  uint64_t* acc_full = bars + 2 * S::STAGES;
+  uint64_t* acc_empty = acc_full + S::ACC_BUFS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + S::ACC_BUFS);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < S::ACC_BUFS; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_a);
+    tma_prefetch_desc(&p.tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int n_tiles = p.N / BLOCK_N;
+  const int num_m = *p.num_tiles;
+  const int total = num_m * n_tiles;
+  const int k_tiles = (p.K + 255) / 256;
+  const int kb_total = p.K / 64;  // scale atoms per 128-row tile
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
+        const TileEntry t = p.tiles[m];
+        const int brow = t.expert * p.N + n * BLOCK_N;
+        const uint8_t* sfa = p.sfa + (size_t)(t.row0 / 128) * kb_total * S::SF_ATOM;
+        const uint8_t* sfb =
+            p.sfb + ((size_t)t.expert * (p.N / 128) + (size_t)n * (BLOCK_N / 128)) * kb_total * S::SF_ATOM;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const int kb = min(4, kb_total - kt * 4);
+          const uint32_t sf_bytes = (uint32_t)kb * S::SF_ATOM;
+          mbar_arrive_expect_tx(&full[stage],
+                                S::A_BYTES + S::B_BYTES + sf_bytes * (1 + BLOCK_N / 128));
+          tma_load_2d(sA + stage * S::A_BYTES, &p.tmap_a, &full[stage], kt * S::BK_BYTES, t.row0);
+          tma_load_2d(sB + stage * S::B_BYTES, &p.tmap_b, &full[stage], kt * S::BK_BYTES, brow);
+          bulk_load(sSFA + stage * S::SFA_BYTES, sfa + (size_t)kt * 4 * S::SF_ATOM, sf_bytes, &full[stage]);
+#pragma unroll
+          for (int h = 0; h < BLOCK_N / 128; ++h)
+            bulk_load(sSFB + stage * S::SFB_BYTES + h * S::SFA_BYTES,
+                      sfb + ((size_t)h * kb_total + (size_t)kt * 4) * S::SF_ATOM, sf_bytes, &full[stage]);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- tcgen05 issuer ----------------
+      constexpr uint32_t idesc = idesc_nvf4(128, BLOCK_N);
+      const uint32_t sfa_t = tmem + S::SFA_COL;
+      const uint32_t sfb_t = tmem + S::SFB_COL;
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * BLOCK_N;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int kb_n = min(4, kb_total - kt * 4);
+          const uint32_t a_base = smem_u32(sA + stage * S::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
+          const uint32_t sfa_s = smem_u32(sSFA + stage * S::SFA_BYTES);
+          const uint32_t sfb_s = smem_u32(sSFB + stage * S::SFB_BYTES);
+          for (int kb = 0; kb < kb_n; ++kb) {
+            tc_cp_32x128b_warpx4(sfa_t + kb * 4, smem_desc(sfa_s + kb * S::SF_ATOM, 0, 128, kLayoutSwizzleNone));
+#pragma unroll
+            for (int h = 0; h < BLOCK_N / 128; ++h)
+              tc_cp_32x128b_warpx4(sfb_t + (kb * (BLOCK_N / 128) + h) * 4,
+                                   smem_desc(sfb_s + h * S::SFA_BYTES + kb * S::SF_ATOM, 0, 128, kLayoutSwizzleNone));
+          }
+          for (int kb = 0; kb < kb_n; ++kb) {
+            const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+            const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+            tc_mma_nvf4(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * (BLOCK_N / 128) * 4,
+                        (kt | kb) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const uint32_t quad = (uint32_t)(warp & 3);  // TMEM lanes 32*quad .. +31
+    const int row_in_tile = (int)(quad * 32 + lane);
+    uint32_t acc = 0, acc_phase = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+      const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
+      const TileEntry t = p.tiles[m];
+      if (!mbar_wait(&acc_full[acc], acc_phase, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const bool valid = row_in_tile < t.valid;
+      const size_t grow = (size_t)t.row0 + row_in_tile;
+      const uint32_t taddr = tmem + ((quad * 32u) << 16) + acc * BLOCK_N;
+      if constexpr (EPI == EPI_SWIGLU) {
+        const float mult = expert_multiplier(p, t.expert);
+        float rmax = 0.0f;
+        constexpr int HALF = BLOCK_N / 2;
+#pragma unroll 1
+        for (int c = 0; c < HALF / 32; ++c) {
+          uint32_t g[32], up[32];
+          tc_ld_32x32b_x32(taddr + c * 32, g);
+          tc_ld_32x32b_x32(taddr + HALF + c * 32, up);
+          tc_wait_ld();
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            uint32_t hv[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const float gate = bf16_round(mul_rn(bf16_round(__uint_as_float(g[j + i])), mult));
+              const float upv = bf16_round(mul_rn(bf16_round(__uint_as_float(up[j + i])), mult));
+              const float silu = bf16_round(mul_rn(gate, sigmoid_triton(gate)));
+              uint16_t h = f32_to_bf16(mul_rn(silu, upv));
+              if (!valid) h = 0;
+              rmax = fmaxf(rmax, fabsf(bf16_to_f32(h)));
+              hv[i] = h;
+            }
+            packed[j / 2] = hv[0] | (hv[1] << 16);
+          }
+          store_row_chunk(p.out + grow * p.out_cols + (size_t)n * HALF + c * 32, packed);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+        if (lane == 0) atomicMax(p.amax_out + t.expert, __float_as_uint(rmax));
+      } else {
+        const float mult = (EPI == EPI_RESCALE) ? expert_multiplier(p, t.expert) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < BLOCK_N / 32; ++c) {
+          uint32_t r[32];
+          tc_ld_32x32b_x32(taddr + c * 32, r);
+          tc_wait_ld();
+          if (valid) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float v0 = bf16_round(__uint_as_float(r[j]));
+              float v1 = bf16_round(__uint_as_float(r[j + 1]));
+              if constexpr (EPI == EPI_RESCALE) {
+                v0 = mul_rn(v0, mult);
+                v1 = mul_rn(v1, mult);
+              }
+              packed[j / 2] = (uint32_t)f32_to_bf16(v0) | ((uint32_t)f32_to_bf16(v1) << 16);
+            }
+            store_row_chunk(p.out + grow * p.out_cols + (size_t)n * BLOCK_N + c * 32, packed);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// Packed FP4 rows viewed as bytes: dims {K/2, rows}, box {128 B, box_rows}.
+static int make_fp4_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t gdim[2] = {(cuuint64_t)(k / 2), (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)(k / 2)};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PRAXIS_B200_OK;
+}
+
+template <int BLOCK_N, int EPI>
+static int launch_gemm(const GemmParams& p, int max_tiles, cudaStream_t stream) {
+  using S = GemmShape<BLOCK_N>;
+  auto kernel = gemm_nvfp4_kernel<BLOCK_N, EPI>;
+  static bool configured[8] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 8 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  const int units = max_tiles * (p.N / BLOCK_N);
+  if (units <= 0) return PRAXIS_B200_OK;
+  const int grid = units < sm_count() ? units : sm_count();
+  kernel<<<grid, 192, S::SMEM_BYTES, stream>>>(p);
+  return check_launch("gemm_nvfp4");
+}
+
+int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, const TileEntry* tiles,
+                     const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
+                     int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
+                     const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, cudaStream_t stream) {
+  if (n % 128 != 0 || k % 128 != 0 || n <= 0 || k <= 0)
+    return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs N and K multiples of 128 (N=%d K=%d)", n, k);
+  if (max_tiles < 0 || rows_padded < (int64_t)max_tiles * 128)
+    return set_error(PRAXIS_B200_EINVAL, "tile table larger than the padded rows");
+  if (epilogue == EPI_SWIGLU && (out_cols * 2 != n || amax_out == nullptr || w_global == nullptr))
+    return set_error(PRAXIS_B200_EINVAL, "SwiGLU epilogue needs out_cols = N/2, amax_out and w_global");
+  if (epilogue == EPI_PLAIN && out_cols != n)
+    return set_error(PRAXIS_B200_EINVAL, "plain epilogue needs out_cols = N");
+  if (epilogue == EPI_RESCALE && (out_cols != n || w_global == nullptr || (act_global == nullptr && act_amax == nullptr)))
+    return set_error(PRAXIS_B200_EINVAL, "rescale epilogue needs global scales");
+  if (epilogue != EPI_PLAIN && epilogue != EPI_SWIGLU && epilogue != EPI_RESCALE)
+    return set_error(PRAXIS_B200_EINVAL, "unknown epilogue %d", epilogue);
+  if (((uintptr_t)a_sf | (uintptr_t)b_sf | (uintptr_t)out) & 15)
+    return set_error(PRAXIS_B200_EINVAL, "scale and output buffers must be 16-byte aligned");
+  if (rows_padded == 0 || max_tiles == 0) return PRAXIS_B200_OK;
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  int rc = make_fp4_map(&p.tmap_a, a_q, rows_padded, k, 128);
+  if (rc) return rc;
+  rc = make_fp4_map(&p.tmap_b, b_q, (int64_t)experts * n, k, 128);
+  if (rc) return rc;
+  p.sfa = static_cast<const uint8_t*>(a_sf);
+  p.sfb = static_cast<const uint8_t*>(b_sf);
+  p.tiles = tiles;
+  p.num_tiles = num_tiles;
+  p.N = n;
+  p.K = k;
+  p.out = out;
+  p.out_cols = out_cols;
+  p.act_global = act_global;
+  p.act_amax = act_amax;
+  p.w_global = w_global;
+  p.amax_out = amax_out;
+  switch (epilogue) {
+    case EPI_SWIGLU:
+      return launch_gemm<128, EPI_SWIGLU>(p, max_tiles, stream);
+    case EPI_RESCALE:
+      return launch_gemm<128, EPI_RESCALE>(p, max_tiles, stream);
+    default:
+      return launch_gemm<128, EPI_PLAIN>(p, max_tiles, stream);
+  }
+}
+
+}  // namespace praxis

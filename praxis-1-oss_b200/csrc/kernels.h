@@ -1,0 +1,59 @@
+// Internal declarations shared by the .cu files of the library (not part of
+// the C ABI; see include/praxis_b200_moe.h for that).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace praxis {
+
+enum Epilogue : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESCALE = 2 };
+
+struct GemmParams {
+  CUtensorMap tmap_a;  // packed FP4 activation rows (padded, expert-grouped)
+  CUtensorMap tmap_b;  // packed FP4 weights, E*N rows
+  const uint8_t* sfa;  // swizzled UE4M3 scales of A
+  const uint8_t* sfb;  // swizzled UE4M3 scales of B, per expert
+  const TileEntry* tiles;
+  const int32_t* num_tiles;
+  int32_t N;
+  int32_t K;
+  uint16_t* out;
+  int32_t out_cols;
+  const float* act_global;
+  const uint32_t* act_amax;
+  const float* w_global;
+  uint32_t* amax_out;
+};
+
+// Records a message for praxis_b200_last_error and returns `code`.
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+int sm_count();
+
+// f32(bf16(max(amax, 1e-12))) * f32(1/2688): the QAT global scale from the
+// float bits of a bf16-valued maximum (praxis/kernels/nvfp4_moe.py:55-57).
+__host__ __device__ __forceinline__ float global_from_amax_bits(uint32_t bits) {
+#ifdef __CUDA_ARCH__
+  float a = __uint_as_float(bits);
+  a = fmaxf(a, 1.0e-12f);
+  a = bf16_round(a);
+  return __fmul_rn(a, 1.0f / 2688.0f);
+#else
+  float a;
+  memcpy(&a, &bits, 4);
+  (void)a;
+  return 0.0f;
+#endif
+}
+
+int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, const TileEntry* tiles,
+                     const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
+                     int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
+                     const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, cudaStream_t stream);
+
+}  // namespace praxis

@@ -1,0 +1,289 @@
+// NVFP4 quantization kernels (E2M1 codes + UE4M3 scale per 16 elements +
+// FP32 per-expert global scale), bit-identical to the reference recipe:
+//
+//   praxis/kernels/nvfp4.py:44-124   _quantize: bs = max|v| * f32(1/6);
+//                                    sf = e4m3(clamp(div_rn(bs, g), 2^-6, 448));
+//                                    rc = div_rn(div_rn(1, g), sf);
+//                                    code = e2m1_rn(clamp(v * rc, -6, 6));
+//                                    even element in the low nibble; scales in
+//                                    128x4 swizzled atoms (:114-119)
+//   praxis/quantization/nvfp4.py:67-146  the same recipe for weights, one
+//                                    global per expert matrix, rows = output
+//                                    features of W^T
+//
+// quantize_gather  token-major: each token row is read once and quantized for
+//                  each of its top-k experts with that expert's global scale;
+//                  extra CTAs zero the padding rows of partly filled tiles
+// quantize_rows    the hidden rows of every tile that holds routed rows
+// pack_weights     GPU packing of expert-first bf16 banks (replaces the
+//                  ~18 min CPU packing of praxis/quantization/loading.py)
+// interleave       gate/up row blocks of 64 for the fused SwiGLU GEMM
+#include "common.cuh"
+#include "kernels.h"
+
+namespace praxis {
+
+constexpr float kOneSixth = 0.16666667163372040f;  // f32(1/6)
+
+__device__ __forceinline__ uint32_t sf_offset(int64_t row, int col, int kb) {
+  return (uint32_t)(((row >> 7) * (kb >> 2) + (col >> 2)) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 +
+                    (col & 3));
+}
+
+__device__ __forceinline__ float clamp6(float x) { return fminf(fmaxf(x, -6.0f), 6.0f); }
+
+// Quantize 16 values with global g (inv_g = div_rn(1, g)); returns the 8
+// code bytes in (lo, hi) and the scale byte.
+__device__ __forceinline__ void quantize16(const float (&v)[16], float amax, float g, float inv_g, uint32_t& lo,
+                                           uint32_t& hi, uint32_t& sf) {
+  const float bs = mul_rn(amax, kOneSixth);
+  const float sfv = fminf(fmaxf(div_rn(bs, g), 0.015625f), 448.0f);
+  sf = f32_to_e4m3_byte(sfv);
+  const float rc = div_rn(inv_g, e4m3_byte_to_f32(sf));
+  lo = 0;
+  hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    lo |= f32x2_to_e2m1_byte(clamp6(mul_rn(v[2 * i], rc)), clamp6(mul_rn(v[2 * i + 1], rc))) << (8 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    hi |= f32x2_to_e2m1_byte(clamp6(mul_rn(v[8 + 2 * i], rc)), clamp6(mul_rn(v[9 + 2 * i], rc))) << (8 * i);
+}
+
+__device__ __forceinline__ void load16_bf16(const uint16_t* src, float (&v)[16], float& amax) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  uint4 a = __ldg(s), b = __ldg(s + 1);
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = bf16_to_f32((uint16_t)(w[i] & 0xFFFFu));
+    v[2 * i + 1] = bf16_to_f32((uint16_t)(w[i] >> 16));
+    amax = fmaxf(amax, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
+  }
+}
+
+// Gather the four scale bytes of lanes 4i..4i+3 into lane 4i and store them
+// as one word (the 4 scales of a 64-element group are adjacent in the atom).
+__device__ __forceinline__ void store_sf_group(uint8_t* sf_base, int64_t row, int col, int kb, uint32_t byte,
+                                               bool active) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t b1 = __shfl_down_sync(0xffffffffu, byte, 1);
+  uint32_t b2 = __shfl_down_sync(0xffffffffu, byte, 2);
+  uint32_t b3 = __shfl_down_sync(0xffffffffu, byte, 3);
+  if (active && (lane & 3) == 0) {
+    const uint32_t word = byte | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    *reinterpret_cast<uint32_t*>(sf_base + sf_offset(row, col, kb)) = word;
+  }
+}
+
+__device__ __forceinline__ float expert_global(const float* g, const uint32_t* amax, int e) {
+  return g != nullptr ? g[e] : global_from_amax_bits(amax[e]);
+}
+
+// ---------------------------------------------------------------------------
+// Gather quantize of the GEMM1 input (one warp per token)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) quantize_gather_kernel(
+    const uint16_t* __restrict__ x, int64_t tokens, int k_dim, const int64_t* __restrict__ top_idx,
+    const int64_t* __restrict__ inverse, const int32_t* __restrict__ csr, const int32_t* __restrict__ pcsr,
+    const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int top_k, int experts,
+    const TileEntry* __restrict__ tiles, const int32_t* __restrict__ num_tiles, int token_blocks,
+    uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  __shared__ int64_t s_dest[8][8];
+  __shared__ float s_g[8][8], s_ig[8][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = k_dim / 16;
+  if ((int)blockIdx.x >= token_blocks) {
+    // Zero the padding rows of partly filled tiles (the reference allocates
+    // these buffers with zeros, praxis/kernels/nvfp4.py:227-231).
+    const int m = blockIdx.x - token_blocks;
+    if (m >= *num_tiles) return;
+    const TileEntry t = tiles[m];
+    for (int r = t.valid + warp; r < kTileRows; r += 8) {
+      const int64_t row = (int64_t)t.row0 + r;
+      uint4* qr = reinterpret_cast<uint4*>(q + row * (k_dim / 2));
+      for (int i = lane; i < k_dim / 32; i += 32) qr[i] = make_uint4(0, 0, 0, 0);
+      for (int g4 = lane; g4 < kb / 4; g4 += 32)
+        *reinterpret_cast<uint32_t*>(sf + sf_offset(row, g4 * 4, kb)) = 0u;
+    }
+    return;
+  }
+  const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+  if (t >= tokens) return;
+  if (lane < top_k) {
+    int64_t e64 = top_idx[t * top_k + lane];
+    int e = (int)e64;
+    if (e64 < 0 || e64 >= experts) {
+      record_error(kErrIndexRange);
+      e = e64 < 0 ? 0 : experts - 1;
+    }
+    const float g = expert_global(globals, amax_bits, e);
+    s_dest[warp][lane] = (int64_t)pcsr[e] + inverse[t * top_k + lane] - csr[e];
+    s_g[warp][lane] = g;
+    s_ig[warp][lane] = div_rn(1.0f, g);
+  }
+  __syncwarp();
+  const uint16_t* xr = x + t * k_dim;
+  for (int j0 = 0; j0 < kb; j0 += 32) {
+    const int j = j0 + lane;
+    const bool active = j < kb;
+    float v[16];
+    float amax = 0.0f;
+    if (active) load16_bf16(xr + j * 16, v, amax);
+    for (int s = 0; s < top_k; ++s) {
+      uint32_t lo = 0, hi = 0, sfb = 0;
+      const int64_t dest = s_dest[warp][s];
+      if (active) {
+        quantize16(v, amax, s_g[warp][s], s_ig[warp][s], lo, hi, sfb);
+        *reinterpret_cast<uint2*>(q + dest * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
+      }
+      store_sf_group(sf, dest, j, kb, sfb, active);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row quantize of the hidden activations (one warp per padded row of a tile)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) quantize_rows_kernel(
+    const uint16_t* __restrict__ x, int k_dim, const TileEntry* __restrict__ tiles,
+    const int32_t* __restrict__ num_tiles, const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits,
+    uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * 8 + warp;  // tile * 128 + row
+  const int m = (int)(item / kTileRows);
+  if (m >= *num_tiles) return;
+  const TileEntry t = tiles[m];
+  const int64_t row = (int64_t)t.row0 + (item % kTileRows);
+  const float g = expert_global(globals, amax_bits, t.expert);
+  const float ig = div_rn(1.0f, g);
+  const int kb = k_dim / 16;
+  const uint16_t* xr = x + row * k_dim;
+  for (int j0 = 0; j0 < kb; j0 += 32) {
+    const int j = j0 + lane;
+    const bool active = j < kb;
+    uint32_t lo = 0, hi = 0, sfb = 0;
+    if (active) {
+      float v[16];
+      float amax;
+      load16_bf16(xr + j * 16, v, amax);
+      quantize16(v, amax, g, ig, lo, hi, sfb);
+      *reinterpret_cast<uint2*>(q + row * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
+    }
+    store_sf_group(sf, row, j, kb, sfb, active);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Weight packing (expert-first bf16 [E, K, N] -> W^T rows of N outputs)
+// ---------------------------------------------------------------------------
+__global__ void pack_amax_kernel(const uint16_t* __restrict__ w, int64_t per_expert, uint32_t* __restrict__ amax) {
+  const int e = blockIdx.y;
+  const uint16_t* src = w + (int64_t)e * per_expert;
+  float m = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per_expert; i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(bf16_to_f32(src[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax + e, __float_as_uint(m));
+}
+
+__global__ void pack_quant_kernel(const uint16_t* __restrict__ w, int k_dim, int n_dim,
+                                  const uint32_t* __restrict__ amax, uint8_t* __restrict__ q,
+                                  uint8_t* __restrict__ sf, float* __restrict__ global_out) {
+  const int e = blockIdx.z;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int j = blockIdx.y;  // 16-element block along K
+  const float g = global_from_amax_bits(amax[e]);
+  if (n == 0 && j == 0) global_out[e] = g;
+  if (n >= n_dim) return;
+  const uint16_t* src = w + (int64_t)e * k_dim * n_dim + (int64_t)j * 16 * n_dim + n;
+  float v[16];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = bf16_to_f32(src[(int64_t)i * n_dim]);
+    m = fmaxf(m, fabsf(v[i]));
+  }
+  uint32_t lo, hi, sfb;
+  quantize16(v, m, g, div_rn(1.0f, g), lo, hi, sfb);
+  const int kb = k_dim / 16;
+  *reinterpret_cast<uint2*>(q + ((int64_t)e * n_dim + n) * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
+  sf[(int64_t)e * n_dim * kb + sf_offset(n, j, kb)] = (uint8_t)sfb;
+}
+
+// ---------------------------------------------------------------------------
+// Gate/up interleave: kernel-layout row r of an expert's [2F, C] gate_up
+// matrix is gate row 64*(r/128) + r%128 for r%128 < 64, else up row
+// F + 64*(r/128) + r%128 - 64. One CTA per (row, expert).
+// ---------------------------------------------------------------------------
+__global__ void interleave_gate_up_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sf, int f_dim,
+                                          int c_dim, uint8_t* __restrict__ q_out, uint8_t* __restrict__ sf_out) {
+  const int r = blockIdx.x, e = blockIdx.y;
+  const int blk = r / 128, w = r % 128;
+  const int src = w < 64 ? 64 * blk + w : f_dim + 64 * blk + (w - 64);
+  const int64_t rows = 2 * (int64_t)f_dim;
+  const uint4* qs = reinterpret_cast<const uint4*>(q + ((int64_t)e * rows + src) * (c_dim / 2));
+  uint4* qd = reinterpret_cast<uint4*>(q_out + ((int64_t)e * rows + r) * (c_dim / 2));
+  for (int i = threadIdx.x; i < c_dim / 32; i += blockDim.x) qd[i] = qs[i];
+  const int kb = c_dim / 16;
+  const uint8_t* ss = sf + (int64_t)e * rows * kb;
+  uint8_t* sd = sf_out + (int64_t)e * rows * kb;
+  for (int j = threadIdx.x; j < kb; j += blockDim.x) sd[sf_offset(r, j, kb)] = ss[sf_offset(src, j, kb)];
+}
+
+// ---------------------------------------------------------------------------
+// Host entries
+// ---------------------------------------------------------------------------
+int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int64_t* top_idx, const int64_t* inverse,
+                        const int32_t* csr, const int32_t* pcsr, const float* globals, const uint32_t* amax_bits,
+                        int top_k, int experts, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
+                        uint8_t* q, uint8_t* sf, cudaStream_t stream) {
+  if (k_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "quantize needs K % 64 == 0");
+  if (top_k < 1 || top_k > 8) return set_error(PRAXIS_B200_EINVAL, "top_k must be 1..8");
+  if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
+  const int token_blocks = (int)((tokens + 7) / 8);
+  const int grid = token_blocks + max_tiles;
+  if (grid == 0) return PRAXIS_B200_OK;
+  quantize_gather_kernel<<<grid, 256, 0, stream>>>(x, tokens, k_dim, top_idx, inverse, csr, pcsr, globals, amax_bits,
+                                                   top_k, experts, tiles, num_tiles, token_blocks, q, sf);
+  return check_launch("quantize_gather");
+}
+
+int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
+                      const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, cudaStream_t stream) {
+  if (k_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "quantize needs K % 64 == 0");
+  if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
+  const int64_t blocks = (int64_t)max_tiles * kTileRows / 8;
+  if (blocks == 0) return PRAXIS_B200_OK;
+  quantize_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, k_dim, tiles, num_tiles, globals, amax_bits, q, sf);
+  return check_launch("quantize_rows");
+}
+
+int run_pack_weights(const uint16_t* w, int experts, int k_dim, int n_dim, uint8_t* q, uint8_t* sf, float* global_out,
+                     uint32_t* amax_scratch, cudaStream_t stream) {
+  if (k_dim % 64 != 0 || n_dim % 128 != 0) return set_error(PRAXIS_B200_EINVAL, "pack needs K%64==0, N%128==0");
+  if (experts <= 0) return PRAXIS_B200_OK;
+  cudaError_t err = cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t) * experts, stream);
+  if (err != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(err));
+  const int64_t per = (int64_t)k_dim * n_dim;
+  dim3 g1((unsigned)((per + 256 * 16 - 1) / (256 * 16)), (unsigned)experts);
+  pack_amax_kernel<<<g1, 256, 0, stream>>>(w, per, amax_scratch);
+  int rc = check_launch("pack_amax");
+  if (rc) return rc;
+  dim3 g2((unsigned)((n_dim + 127) / 128), (unsigned)(k_dim / 16), (unsigned)experts);
+  pack_quant_kernel<<<g2, 128, 0, stream>>>(w, k_dim, n_dim, amax_scratch, q, sf, global_out);
+  return check_launch("pack_quant");
+}
+
+int run_interleave_gate_up(const uint8_t* q, const uint8_t* sf, int experts, int f_dim, int c_dim, uint8_t* q_out,
+                           uint8_t* sf_out, cudaStream_t stream) {
+  if (f_dim % 64 != 0 || c_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "interleave needs F,C % 64 == 0");
+  if (experts <= 0) return PRAXIS_B200_OK;
+  dim3 grid((unsigned)(2 * f_dim), (unsigned)experts);
+  interleave_gate_up_kernel<<<grid, 128, 0, stream>>>(q, sf, f_dim, c_dim, q_out, sf_out);
+  return check_launch("interleave_gate_up");
+}
+
+}  // namespace praxis

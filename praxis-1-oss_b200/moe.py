@@ -1,0 +1,164 @@
+"""``B200MoEFeedForward``: the MoE module of praxis/layers.py:1584-1631 with
+the router and the routed experts on this library's sm_100a kernels.
+
+Constructor, state-dict keys (``router.weight``, ``expert_bias``,
+``routed.*`` packed NVFP4 buffers, ``shared.gate_up``, ``shared.down``) and the
+forward contract follow the reference module; the routed bank is a
+``B200NVFP4RoutedExperts``. The shared expert stays a torch bf16 SwiGLU (the
+reference's ``SharedExpert``, praxis/layers.py:1033-1089), added after the
+routed sum is rounded to bf16.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor, nn
+
+from . import ops
+from .bank import B200NVFP4RoutedExperts, pack_routed_experts
+
+_NVTX = os.environ.get("PRAXIS_NVTX", "0") not in ("", "0")
+
+
+class _Range:
+    """``praxis::moe:<name>`` NVTX range (praxis/nvtx.py naming) when PRAXIS_NVTX=1."""
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+
+    def __enter__(self):
+        if _NVTX:
+            torch.cuda.nvtx.range_push(f"praxis::moe:{self.name}")
+
+    def __exit__(self, *exc):
+        if _NVTX:
+            torch.cuda.nvtx.range_pop()
+
+
+class SharedExpert(nn.Module):
+    """The always-on dense SwiGLU expert (praxis/layers.py:1033-1089)."""
+
+    def __init__(self, dim: int, hidden: int) -> None:
+        super().__init__()
+        self.gate_up = nn.Parameter(torch.empty(dim, 2 * hidden))
+        self.down = nn.Parameter(torch.empty(hidden, dim))
+
+    def forward(self, x: Tensor) -> Tensor:
+        gate, up = (x @ self.gate_up).chunk(2, dim=-1)
+        return (F.silu(gate) * up) @ self.down
+
+
+class B200MoEFeedForward(nn.Module):
+    """Router (sigmoid or softmax) + top-k routed NVFP4 experts + optional
+    shared expert, inference only."""
+
+    expert_bias: Tensor
+
+    def __init__(
+        self,
+        dim: int = 3072,
+        hidden: int = 1280,
+        num_experts: int = 128,
+        top_k: int = 8,
+        routed_scaling_factor: float = 2.5,
+        dispatch_chunk_size: int | None = None,
+        *,
+        router_activation: str = "sigmoid",
+        shared_expert: bool = True,
+    ) -> None:
+        super().__init__()
+        if dispatch_chunk_size is not None and dispatch_chunk_size <= 0:
+            raise ValueError("dispatch_chunk_size must be positive")
+        if router_activation not in ("sigmoid", "softmax"):
+            raise ValueError("router_activation must be 'sigmoid' or 'softmax'")
+        self.dim, self.hidden = dim, hidden
+        self.dispatch_chunk_size = dispatch_chunk_size
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.routed_scaling_factor = routed_scaling_factor
+        self.router_activation = router_activation
+        self.router = nn.Linear(dim, num_experts, bias=False)
+        self.routed: B200NVFP4RoutedExperts | None = None
+        self.shared = SharedExpert(dim, hidden) if shared_expert else None
+        self.register_buffer("expert_bias", torch.zeros(num_experts))
+        self._router_terms: Tensor | None = None
+
+    def _apply(self, fn, recurse: bool = True):
+        bias = self.expert_bias
+        super()._apply(fn, recurse)
+        # The routing bias stays float32 under dtype casts (praxis/layers.py:1617-1622).
+        self.expert_bias = bias.to(device=self.expert_bias.device)
+        self._router_terms = None
+        return self
+
+    def set_routed_weights(self, gate_up_weight: Tensor, down_weight: Tensor) -> None:
+        """Pack expert-first bf16 banks [E,C,2H] / [E,H,C] on the GPU."""
+        self.routed = pack_routed_experts(gate_up_weight, down_weight, keep_on_device=True)
+
+    @classmethod
+    def from_reference(cls, layer: nn.Module) -> B200MoEFeedForward:
+        """Build from a reference ``praxis.layers.MoEFeedForward`` whose routed
+        bank is either ``RoutedExperts`` (bf16, packed here on the GPU) or
+        ``NVFP4RoutedExperts`` (buffers reused as they are)."""
+        router_w = layer.router.weight
+        e, c = router_w.shape
+        routed = layer.routed
+        if hasattr(routed, "gate_up_q"):
+            h = routed.down_q.shape[2] * 2
+        else:
+            h = routed.gate_up_weight.shape[2] // 2
+        new = cls(c, h, e, layer.top_k, layer.routed_scaling_factor, layer.dispatch_chunk_size,
+                  shared_expert=getattr(layer, "shared", None) is not None)
+        with torch.no_grad():
+            new.router.weight = nn.Parameter(router_w.detach().clone(), requires_grad=False)
+            new.expert_bias = layer.expert_bias.detach().clone().float()
+            if new.shared is not None:
+                new.shared.gate_up = nn.Parameter(layer.shared.gate_up.detach().clone(), requires_grad=False)
+                new.shared.down = nn.Parameter(layer.shared.down.detach().clone(), requires_grad=False)
+        if hasattr(routed, "gate_up_q"):
+            state = {name: buf.detach().cpu().contiguous() for name, buf in routed.named_buffers()
+                     if name in ("gate_up_q", "gate_up_sf", "gate_up_global", "down_q", "down_sf",
+                                 "down_global", "_unit_alpha")}
+            new.routed = B200NVFP4RoutedExperts.from_packed(state)
+        else:
+            new.set_routed_weights(routed.gate_up_weight.detach().to(torch.bfloat16),
+                                   routed.down_weight.detach().to(torch.bfloat16))
+        return new
+
+    def router_terms(self) -> Tensor:
+        """The router weight as bf16 terms for the tensor-core logits kernel."""
+        w = self.router.weight
+        if self._router_terms is None or self._router_terms.device != w.device:
+            self._router_terms = ops.split_router_weight(w.detach())
+        return self._router_terms
+
+    @torch.no_grad()
+    def route(self, x_flat: Tensor) -> tuple[Tensor, Tensor]:
+        """(top_idx, gate) of ``MoEFeedForward._route`` (praxis/layers.py:1632-1655)."""
+        with _Range("router"):
+            logits, _ = ops.router_logits(x_flat, self.router_terms())
+        with _Range("topk_dispatch"):
+            bias = self.expert_bias.to(device=x_flat.device, dtype=torch.float32).contiguous()
+            return ops.route(logits, bias, self.top_k, self.router_activation)
+
+    @torch.no_grad()
+    def forward(self, x: Tensor) -> Tensor:
+        if self.routed is None:
+            raise RuntimeError("routed experts are not set (set_routed_weights / from_reference)")
+        shape = x.shape
+        x_flat = x.reshape(-1, x.size(-1)).contiguous()
+        top_idx, gate = self.route(x_flat)
+        y_shared = self.shared(x_flat) if self.shared is not None else None
+        chunk = self.dispatch_chunk_size or max(1, x_flat.shape[0])
+        with _Range("routed"):
+            if y_shared is None:
+                out = self.routed.routed_forward(x_flat, top_idx, gate, scaling=self.routed_scaling_factor,
+                                                 chunk_size=chunk)
+            else:
+                out = self.routed.routed_forward_with_shared(
+                    x_flat, top_idx, gate, scaling=self.routed_scaling_factor, chunk_size=chunk,
+                    shared=y_shared.contiguous())
+        return out.reshape(shape)

@@ -1,0 +1,306 @@
+"""Torch-facing functions over the C ABI (one per reference kernel function).
+
+Each function checks its tensors (``ValueError`` before any launch, like
+praxis/quantization/nvfp4.py:631-675), allocates its outputs with the torch
+caching allocator, and enqueues the CUDA library's kernels on the current
+stream of the tensors' device. No host synchronisation, so every op can be
+captured in a CUDA graph. There is no CPU path: the library must be built
+and a sm_100 GPU present.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import NamedTuple
+
+import torch
+from torch import Tensor
+
+from . import capi
+
+BF16 = torch.bfloat16
+
+
+def _p(t: Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dev(t: Tensor) -> int:
+    if t.device.type != "cuda":
+        raise ValueError("praxis_b200 ops need CUDA tensors")
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def _stream(t: Tensor) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need(t: Tensor, name: str, dtype, ndim: int | None = None, device=None) -> None:
+    if not isinstance(t, Tensor) or t.dtype != dtype or not t.is_contiguous() or t.device.type != "cuda":
+        raise ValueError(f"{name}: expected a contiguous CUDA {dtype} tensor")
+    if ndim is not None and t.ndim != ndim:
+        raise ValueError(f"{name}: expected {ndim} dims, got {t.ndim}")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name}: tensors must share a device")
+
+
+def padded_rows(routed_rows: int, experts: int) -> int:
+    """praxis/kernels/nvfp4.py:213 with alignment 128."""
+    return (routed_rows + 127 * experts) // 128 * 128
+
+
+class Routing(NamedTuple):
+    """``praxis.kernels.router_fused.Routing`` (router_fused.py:58-68) plus the
+    grouped-GEMM metadata of this library (csr, pcsr, tiles, globals)."""
+
+    top_idx: Tensor
+    gate: Tensor
+    order: Tensor
+    inverse: Tensor
+    sorted_gate: Tensor
+    tokens: Tensor
+    tokens32: Tensor
+    seg_csr: Tensor
+    offsets: Tensor
+    rows: tuple
+    csr: Tensor
+    pcsr: Tensor
+    tiles: Tensor
+    num_tiles: Tensor
+    act_global: Tensor | None
+    act_amax: Tensor | None
+
+
+def split_router_weight(weight: Tensor) -> Tensor:
+    """[E, C] router weight -> [S, E, C] bf16 terms whose sum is the weight:
+    S = 1 for bf16, S = 3 (hi, mid, lo) for fp32 (exact decomposition)."""
+    if weight.dtype == BF16:
+        return weight.contiguous().unsqueeze(0)
+    w = weight.to(torch.float32)
+    hi = w.to(BF16)
+    r1 = w - hi.float()
+    mid = r1.to(BF16)
+    lo = (r1 - mid.float()).to(BF16)
+    return torch.stack([hi, mid, lo]).contiguous()
+
+
+def router_logits(x: Tensor, weight_terms: Tensor) -> tuple[Tensor, Tensor]:
+    """fp32 logits x @ W^T (praxis/layers.py:1104-1122) and bf16 row max |x|
+    (praxis/kernels/nvfp4_moe.py:15-21) in one pass."""
+    _need(x, "x", BF16, 2)
+    _need(weight_terms, "router weight", BF16, 3, x.device)
+    t, c = x.shape
+    s, e, c2 = weight_terms.shape
+    if c2 != c:
+        raise ValueError("router weight / activation width mismatch")
+    logits = torch.empty(t, e, dtype=torch.float32, device=x.device)
+    amax = torch.empty(t, dtype=BF16, device=x.device)
+    capi.check(capi.load().praxis_b200_router_logits(
+        _p(x), _p(weight_terms), s, t, c, e, _p(logits), _p(amax), _dev(x), _stream(x)))
+    return logits, amax
+
+
+def route(logits: Tensor, bias: Tensor | None, top_k: int, activation: str = "sigmoid") -> tuple[Tensor, Tensor]:
+    """Gating + top-k + renormalised bf16 gates (praxis/layers.py:1647-1653)."""
+    _need(logits, "logits", torch.float32, 2)
+    if bias is not None:
+        _need(bias, "expert bias", torch.float32, 1, logits.device)
+    t, e = logits.shape
+    act = {"sigmoid": capi.SIGMOID, "softmax": capi.SOFTMAX}[activation]
+    top_idx = torch.empty(t, top_k, dtype=torch.int64, device=logits.device)
+    gate = torch.empty(t, top_k, dtype=BF16, device=logits.device)
+    capi.check(capi.load().praxis_b200_route(
+        _p(logits), _p(bias), t, e, top_k, act, _p(top_idx), _p(gate), _dev(logits), _stream(logits)))
+    return top_idx, gate
+
+
+def row_amax(x: Tensor) -> Tensor:
+    _need(x, "x", BF16, 2)
+    out = torch.empty(x.shape[0], dtype=BF16, device=x.device)
+    capi.check(capi.load().praxis_b200_row_amax(_p(x), x.shape[0], x.shape[1], _p(out), _dev(x), _stream(x)))
+    return out
+
+
+def dispatch(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | None = None,
+             full: bool = True) -> Routing:
+    """``_dispatch_rows`` + inverse + padded CSR + tile table (+ activation
+    global scales from ``amax``) on the device."""
+    _need(top_idx, "top_idx", torch.int64, 2)
+    _need(gate, "gate", BF16, 2, top_idx.device)
+    if gate.shape != top_idx.shape:
+        raise ValueError("gate / top_idx shape mismatch")
+    t, k = top_idx.shape
+    dev = top_idx.device
+    r = t * k
+    e = num_experts
+    max_tiles = padded_rows(r, e) // 128
+    lib = capi.load()
+    ws = torch.empty(int(lib.praxis_b200_dispatch_workspace_size(t, k, e)), dtype=torch.uint8, device=dev)
+    i64 = dict(dtype=torch.int64, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    order = torch.empty(r, **i64) if full else None
+    inverse = torch.empty(r, **i64)
+    tokens = torch.empty(r, **i64) if full else None
+    tokens32 = torch.empty(r, **i32) if full else None
+    sorted_gate = torch.empty(r, dtype=BF16, device=dev) if full else None
+    offsets = torch.empty(e, **i32)
+    csr = torch.empty(e + 1, **i32)
+    pcsr = torch.empty(e + 1, **i32)
+    tiles = torch.empty(max(max_tiles, 1), 4, **i32)
+    num_tiles = torch.empty(1, **i32)
+    act_global = act_amax = None
+    if amax is not None:
+        _need(amax, "row amax", BF16, 1, dev)
+        act_global = torch.empty(e, dtype=torch.float32, device=dev)
+        act_amax = torch.empty(e, dtype=torch.int32, device=dev)
+    capi.check(lib.praxis_b200_dispatch(
+        _p(top_idx), _p(gate), _p(amax), t, k, e, _p(ws), ws.numel(), _p(order), _p(inverse), _p(tokens),
+        _p(tokens32), _p(sorted_gate), _p(offsets), _p(csr), _p(pcsr), _p(tiles), max_tiles, _p(num_tiles),
+        _p(act_global), _p(act_amax), _dev(top_idx), _stream(top_idx)))
+    return Routing(top_idx, gate, order, inverse, sorted_gate, tokens, tokens32, csr, offsets, (t,), csr, pcsr,
+                   tiles, num_tiles, act_global, act_amax)
+
+
+def route_dispatch(logits: Tensor, bias: Tensor, rows: tuple, top_k: int = 8,
+                   activation: str = "sigmoid") -> Routing:
+    """``router_fused.route_dispatch`` (praxis/kernels/router_fused.py:738)
+    for one input (P = 1), any E <= 256 and k <= 8."""
+    if len(rows) != 1 or rows[0] != logits.shape[0]:
+        raise ValueError("route_dispatch here takes one input (rows == (T,))")
+    top_idx, gate = route(logits, bias, top_k, activation)
+    return dispatch(top_idx, gate, logits.shape[1])
+
+
+def quantize_gather(x: Tensor, routing: Routing, act_global: Tensor) -> tuple[Tensor, Tensor]:
+    """``quantize_activations(x, csr, row_indices=tokens, alignment=128,
+    grouped_scales=False)`` (praxis/kernels/nvfp4.py:197-254) into the
+    padded layout; padding rows of partly filled tiles are zero."""
+    _need(x, "x", BF16, 2)
+    t, c = x.shape
+    k = routing.top_idx.shape[1]
+    e = routing.csr.numel() - 1
+    rp = padded_rows(t * k, e)
+    q = torch.empty(rp, c // 2, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(rp, c // 16, dtype=torch.uint8, device=x.device)
+    capi.check(capi.load().praxis_b200_quantize_gather(
+        _p(x), t, c, _p(routing.top_idx), _p(routing.inverse), _p(routing.csr), _p(routing.pcsr), _p(act_global),
+        None, k, e, _p(routing.tiles), _p(routing.num_tiles), rp // 128, _p(q), _p(sf), _dev(x), _stream(x)))
+    return q, sf
+
+
+def quantize_rows(x: Tensor, routing: Routing, globals_: Tensor | None = None,
+                  amax_bits: Tensor | None = None) -> tuple[Tensor, Tensor]:
+    """Quantize every row of the routed tiles of a padded [Rp, K] tensor."""
+    _need(x, "x", BF16, 2)
+    rp, kdim = x.shape
+    q = torch.empty(rp, kdim // 2, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(rp, kdim // 16, dtype=torch.uint8, device=x.device)
+    capi.check(capi.load().praxis_b200_quantize_rows(
+        _p(x), kdim, _p(routing.tiles), _p(routing.num_tiles), rp // 128, _p(globals_), _p(amax_bits), _p(q),
+        _p(sf), _dev(x), _stream(x)))
+    return q, sf
+
+
+def grouped_gemm(a_q: Tensor, a_sf: Tensor, b_q: Tensor, b_sf: Tensor, routing: Routing, *,
+                 epilogue: int = capi.EPI_PLAIN, act_global: Tensor | None = None,
+                 act_amax: Tensor | None = None, w_global: Tensor | None = None,
+                 amax_out: Tensor | None = None) -> Tensor:
+    """``grouped_nvfp4_mm`` (praxis/kernels/nvfp4.py:355-419) on tcgen05 with
+    an optional fused epilogue (see include/praxis_b200_moe.h)."""
+    rp = a_q.shape[0]
+    kdim = a_q.shape[1] * 2
+    e, n = b_q.shape[0], b_q.shape[1]
+    if b_q.shape[2] * 2 != kdim:
+        raise ValueError("A / B reduction width mismatch")
+    cols = n // 2 if epilogue == capi.EPI_SWIGLU else n
+    out = torch.empty(rp, cols, dtype=BF16, device=a_q.device)
+    capi.check(capi.load().praxis_b200_grouped_gemm(
+        _p(a_q), _p(a_sf), _p(b_q), _p(b_sf), _p(routing.tiles), _p(routing.num_tiles), rp // 128, rp, n, kdim, e,
+        epilogue, _p(out), _p(act_global), _p(act_amax), _p(w_global), _p(amax_out), _dev(a_q), _stream(a_q)))
+    return out
+
+
+def combine(rows: Tensor, routing: Routing, scaling: float, *, h_global: Tensor | None = None,
+            h_amax: Tensor | None = None, w_global: Tensor | None = None, rows_rescaled: bool = False,
+            shared: Tensor | None = None) -> Tensor:
+    """``rescale_combine`` (praxis/kernels/nvfp4_moe.py:206-311)."""
+    t, k = routing.top_idx.shape
+    c = rows.shape[1]
+    e = routing.csr.numel() - 1
+    out = torch.empty(t, c, dtype=BF16, device=rows.device)
+    if shared is not None:
+        _need(shared, "shared", BF16, 2, rows.device)
+    capi.check(capi.load().praxis_b200_combine(
+        _p(rows), c, _p(routing.inverse), _p(routing.top_idx), _p(routing.gate), _p(routing.csr),
+        _p(routing.pcsr), _p(h_global), _p(h_amax), _p(w_global), int(rows_rescaled), float(scaling), _p(shared),
+        _p(out), t, k, e, _dev(rows), _stream(rows)))
+    return out
+
+
+def pack_weights(w: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """Expert-first bf16 bank [E, K, N] -> (q [E,N,K/2], sf [E,N,K/16],
+    global [E]) on the GPU, the bytes of praxis/quantization/nvfp4.py:67-146."""
+    _need(w, "weights", BF16, 3)
+    e, kdim, n = w.shape
+    q = torch.empty(e, n, kdim // 2, dtype=torch.uint8, device=w.device)
+    sf = torch.empty(e, n, kdim // 16, dtype=torch.uint8, device=w.device)
+    g = torch.empty(e, dtype=torch.float32, device=w.device)
+    scratch = torch.empty(e, dtype=torch.int32, device=w.device)
+    capi.check(capi.load().praxis_b200_pack_weights(
+        _p(w), e, kdim, n, _p(q), _p(sf), _p(g), _p(scratch), _dev(w), _stream(w)))
+    return q, sf, g
+
+
+def interleave_gate_up(q: Tensor, sf: Tensor) -> tuple[Tensor, Tensor]:
+    """The fused-SwiGLU GEMM layout of gate_up q/sf (64-row gate/up blocks)."""
+    _need(q, "gate_up_q", torch.uint8, 3)
+    _need(sf, "gate_up_sf", torch.uint8, 3, q.device)
+    e, n2, c2 = q.shape
+    qo = torch.empty_like(q)
+    so = torch.empty_like(sf)
+    capi.check(capi.load().praxis_b200_interleave_gate_up(
+        _p(q), _p(sf), e, n2 // 2, c2 * 2, _p(qo), _p(so), _dev(q), _stream(q)))
+    return qo, so
+
+
+def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_q: Tensor, gate_up_sf: Tensor,
+                gate_up_global: Tensor, down_q: Tensor, down_sf: Tensor, down_global: Tensor, scaling: float,
+                shared: Tensor | None = None, *, router_terms: Tensor | None = None,
+                router_bias: Tensor | None = None, top_k: int | None = None, activation: str = "sigmoid",
+                out: Tensor | None = None):
+    """One dispatch chunk through ``praxis_b200_moe_forward``. With
+    ``router_terms`` the router runs too and (out, top_idx, gate) is returned.
+    ``gate_up_q/sf`` are in the interleaved kernel layout."""
+    _need(x, "x", BF16, 2)
+    t, c = x.shape
+    e, c_half_f, _ = down_q.shape
+    f = down_q.shape[2] * 2
+    dev = x.device
+    if router_terms is not None:
+        k = int(top_k)
+        top_idx = torch.empty(t, k, dtype=torch.int64, device=dev)
+        gate = torch.empty(t, k, dtype=BF16, device=dev)
+    else:
+        k = top_idx.shape[1]
+    if out is None:
+        out = torch.empty_like(x)
+    lib = capi.load()
+    ws_size = int(lib.praxis_b200_moe_workspace_size(t, k, e, c, f, int(router_terms is not None)))
+    ws = torch.empty(ws_size, dtype=torch.uint8, device=dev)
+    args = capi.MoeArgs(
+        x=x.data_ptr(), router_weight=None if router_terms is None else router_terms.data_ptr(),
+        router_splits=0 if router_terms is None else router_terms.shape[0],
+        activation={"sigmoid": capi.SIGMOID, "softmax": capi.SOFTMAX}[activation],
+        router_bias=None if router_bias is None else router_bias.data_ptr(),
+        top_idx=top_idx.data_ptr(), gate=gate.data_ptr(),
+        shared=None if shared is None else shared.data_ptr(), out=out.data_ptr(),
+        gate_up_q=gate_up_q.data_ptr(), gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(),
+        down_q=down_q.data_ptr(), down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(),
+        tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
+        workspace=ws.data_ptr(), workspace_size=ws_size, device=_dev(x),
+        stream=torch.cuda.current_stream(dev).cuda_stream,
+    )
+    capi.check(lib.praxis_b200_moe_forward(C.byref(args)))
+    if router_terms is not None:
+        return out, top_idx, gate
+    return out

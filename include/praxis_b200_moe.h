@@ -90,8 +90,11 @@ int praxis_b200_row_amax(const void* x, int64_t rows, int32_t cols, void* out, i
  *      the stable expert-major order of the T*k (token, slot) rows;
  *   inverse[p]: position of flat row p in that order;
  *   offsets[e]: int32 end offsets; csr[E+1]; pcsr[E+1] (128-aligned starts);
- *   tiles [max_tiles, 4] int32 {expert, first padded row, valid rows, 0} and
- *      num_tiles[1]: the 128-row tiles holding routed rows, expert order;
+ *   tiles [2 * max_tiles, 4] int32: entries 0.. are the 128-row tiles that
+ *      hold routed rows {expert, first padded row, routed rows, 0} in expert
+ *      order; entries max_tiles.. are the 256-row pairs of the 2-CTA GEMM
+ *      {expert, first padded row, routed rows, rows of live 128-row tiles};
+ *      num_tiles[2] = {tiles, pairs};
  *   act_global[e] (fp32) and act_amax[e] (fp32 bits) from row_amax [T] (bf16)
  *      when row_amax != NULL: f32(bf16(max(amax, 1e-12))) * f32(1/2688).
  * Any output pointer except csr, pcsr, tiles, num_tiles may be NULL.
@@ -145,6 +148,17 @@ int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q,
                              int64_t rows_padded, int32_t n, int32_t k, int32_t experts, int32_t epilogue,
                              void* out, const float* act_global, const uint32_t* act_amax, const float* w_global,
                              uint32_t* amax_out, int device, void* stream);
+
+/* Rescale + SwiGLU + row max over the padded gate/up GEMM output raw
+ * [rows, 2F] (bf16, gate columns first): m = bf16(act_global[e] * w_global[e])
+ * for the expert e whose pcsr segment holds the row; hidden [rows, F] and
+ * rowmax [rows] (bf16, may be NULL). alu = 1: the arithmetic of the fused GEMM
+ * epilogue (integer roundings, refined reciprocal); alu = 0: conversion-unit
+ * roundings and IEEE division. Both give the same bits.
+ * Replaces praxis/kernels/nvfp4_moe.py:102-158 (rescale_swiglu_maximum). */
+int praxis_b200_rescale_swiglu(const void* raw, int64_t rows, int32_t hidden, const int32_t* pcsr,
+                               int32_t experts, const float* act_global, const float* w_global, void* out,
+                               void* rowmax, int32_t alu, int device, void* stream);
 
 /* Weighted combine: out[t] = bf16(((a0 + a1) + a2) + a3) with
  * a_{s%4} += v_s * (f32(gate[t, s]) * f32(scaling)), v_s the routed row

@@ -83,6 +83,7 @@ SIGNATURES: dict[str, tuple] = {
         C.c_int,
         [P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, P, P, P, P, P, C.c_int, P],
     ),
+    "praxis_b200_rescale_swiglu": (C.c_int, [P, I64, I32, P, I32, P, P, P, P, I32, C.c_int, P]),
     "praxis_b200_combine": (
         C.c_int,
         [P, I32, P, P, P, P, P, P, P, P, I32, F32, P, P, I64, I32, I32, C.c_int, P],

@@ -31,6 +31,9 @@ int run_router_logits(const uint16_t* x, const uint16_t* w, int splits, int64_t 
                       float* logits, uint16_t* row_amax, cudaStream_t stream);
 int run_route(const float* logits, const float* bias, int64_t tokens, int experts, int top_k, int activation,
               int64_t* top_idx, uint16_t* gate, cudaStream_t stream);
+int run_rescale_swiglu(const uint16_t* raw, int64_t rows, int hidden, const int32_t* pcsr, int experts,
+                       const float* act_global, const float* w_global, uint16_t* out, uint16_t* rowmax, int alu,
+                       cudaStream_t stream);
 int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx, const uint16_t* gate,
                 const int32_t* csr, const int32_t* pcsr, const float* h_global, const uint32_t* h_amax,
                 const float* w_global, int rows_rescaled, float scaling, const uint16_t* shared, uint16_t* out,
@@ -113,8 +116,8 @@ static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int
   L.csr = take((size_t)(experts + 1) * 4);
   L.pcsr = take((size_t)(experts + 1) * 4);
   L.offsets = take((size_t)experts * 4);
-  L.tiles = take((size_t)(L.max_tiles + 1) * sizeof(TileEntry));
-  L.num_tiles = take(4);
+  L.tiles = take((size_t)(2 * L.max_tiles + 1) * sizeof(TileEntry));
+  L.num_tiles = take(8);
   L.act_amax = take((size_t)experts * 4);
   L.act_global = take((size_t)experts * 4);
   L.h_amax = take((size_t)experts * 4);
@@ -242,6 +245,16 @@ int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q,
   return run_grouped_gemm(a_q, a_sf, b_q, b_sf, reinterpret_cast<const TileEntry*>(tiles), num_tiles, max_tiles,
                           rows_padded, n, k, experts, epilogue, static_cast<uint16_t*>(out), out_cols, act_global,
                           act_amax, w_global, amax_out, PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_rescale_swiglu(const void* raw, int64_t rows, int32_t hidden, const int32_t* pcsr,
+                               int32_t experts, const float* act_global, const float* w_global, void* out,
+                               void* rowmax, int32_t alu, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!raw || !pcsr || !act_global || !w_global || !out)
+    return set_error(PRAXIS_B200_EINVAL, "rescale_swiglu: null pointer");
+  return run_rescale_swiglu(static_cast<const uint16_t*>(raw), rows, hidden, pcsr, experts, act_global, w_global,
+                            static_cast<uint16_t*>(out), static_cast<uint16_t*>(rowmax), alu, PRAXIS_STREAM(stream));
 }
 
 int praxis_b200_combine(const void* rows, int32_t cols, const int64_t* inverse, const int64_t* top_idx,

@@ -43,40 +43,58 @@ __global__ void __launch_bounds__(256) combine_kernel(
     s_mult[warp][lane] = mult;
   }
   __syncwarp();
-  for (int c = lane * 8; c < cols; c += 256) {
-    float acc[4][8];
+  // Two 8-column chunks per lane per pass: every routed-row load of the pass
+  // is issued before any arithmetic (2 * top_k 16-byte loads in flight).
+  constexpr int U = 2;
+  for (int c0 = lane * 8; c0 < cols; c0 += 256 * U) {
+    uint4 v[U][8];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * 256;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[a][i] = 0.0f;
-    for (int s = 0; s < top_k; ++s) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + s_src[warp][s] * cols + c));
-      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-      const float sc = s_scale[warp][s], mult = s_mult[warp][s];
-      const int a = s & 3;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float val = bf16_to_f32((uint16_t)((wv[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu));
-        if (!rows_rescaled) val = bf16_round(mul_rn(val, mult));
-        acc[a][i] = add_rn(acc[a][i], mul_rn(val, sc));
-      }
+      for (int s = 0; s < 8; ++s)
+        if (s < top_k && c < cols) v[u][s] = ldg_stream(reinterpret_cast<const uint4*>(rows + s_src[warp][s] * cols + c));
     }
-    uint32_t packed[4];
-    uint4 sh = make_uint4(0, 0, 0, 0);
-    if (shared != nullptr) sh = __ldg(reinterpret_cast<const uint4*>(shared + t * cols + c));
-    const uint32_t shv[4] = {sh.x, sh.y, sh.z, sh.w};
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      uint32_t h2[2];
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * 256;
+      if (c >= cols) break;
+      float acc[4][8];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float y = bf16_round(add_rn(add_rn(add_rn(acc[0][i + j], acc[1][i + j]), acc[2][i + j]), acc[3][i + j]));
-        if (shared != nullptr) y = add_rn(y, bf16_to_f32((uint16_t)((shv[(i + j) >> 1] >> (((i + j) & 1) * 16)) & 0xFFFFu)));
-        h2[j] = f32_to_bf16(y);
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[a][i] = 0.0f;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < top_k) {
+          const uint32_t wv[4] = {v[u][s].x, v[u][s].y, v[u][s].z, v[u][s].w};
+          const float sc = s_scale[warp][s], mult = s_mult[warp][s];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float val = bf16_to_f32((uint16_t)((wv[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu));
+            if (!rows_rescaled) val = bf16_round_alu(__fmul_rn(val, mult));
+            acc[s & 3][i] = __fadd_rn(acc[s & 3][i], __fmul_rn(val, sc));
+          }
+        }
       }
-      packed[i >> 1] = h2[0] | (h2[1] << 16);
+      uint4 sh = make_uint4(0, 0, 0, 0);
+      if (shared != nullptr) sh = ldg_stream(reinterpret_cast<const uint4*>(shared + t * cols + c));
+      const uint32_t shv[4] = {sh.x, sh.y, sh.z, sh.w};
+      uint32_t packed[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        float y[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          y[j] = bf16_round_alu(
+              __fadd_rn(__fadd_rn(__fadd_rn(acc[0][i + j], acc[1][i + j]), acc[2][i + j]), acc[3][i + j]));
+          if (shared != nullptr)
+            y[j] = __fadd_rn(y[j], bf16_to_f32((uint16_t)((shv[(i + j) >> 1] >> (((i + j) & 1) * 16)) & 0xFFFFu)));
+        }
+        packed[i >> 1] = pack_bf16x2_alu(y[0], y[1]);
+      }
+      *reinterpret_cast<uint4*>(out + t * cols + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
-    *reinterpret_cast<uint4*>(out + t * cols + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
 }
 

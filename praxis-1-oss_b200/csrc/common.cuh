@@ -80,6 +80,15 @@ __device__ __forceinline__ uint32_t f32x2_to_e2m1_byte(float lo, float hi) {
   return out;
 }
 
+// 16-byte streaming load through the non-coherent path (read-once data).
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 // IEEE round-to-nearest division and product/sum with no contraction.
 __device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
@@ -92,6 +101,70 @@ __device__ __forceinline__ float sigmoid_triton(float x) {
   float e;
   asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t));
   return div_rn(1.0f, add_rn(1.0f, e));
+}
+
+// ---------------------------------------------------------------------------
+// ALU-only variants for the GEMM epilogues. The conversion/transcendental
+// (XU) pipe is the epilogue's bottleneck, so roundings use integer ops and
+// the sigmoid's division uses one reciprocal estimate refined on the FMA
+// pipe. Both produce the same bits as the variants above; the division's
+// equality is checked on every bf16 gate value (tests/test_gpu_parity.py).
+// ---------------------------------------------------------------------------
+// float -> bf16 (round to nearest even) in the high 16 bits; NaN -> qNaN.
+__device__ __forceinline__ uint32_t bf16_hi_bits(float x) {
+  const uint32_t u = __float_as_uint(x);
+  const uint32_t r = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  return ((u & 0x7FFFFFFFu) > 0x7F800000u) ? 0x7FC00000u : r;
+}
+__device__ __forceinline__ float bf16_round_alu(float x) { return __uint_as_float(bf16_hi_bits(x)); }
+// Two floats -> packed bf16x2 (lo in bits 0-15).
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  return __byte_perm(bf16_hi_bits(lo), bf16_hi_bits(hi), 0x7632);
+}
+
+// 1 / d rounded to nearest for d >= 1 (d = 1 + 2^t in the sigmoid).
+// Newton-Raphson refinement of the hardware reciprocal estimate, then one
+// residual correction of the quotient (Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. R&D 34(1), 1990):
+//   y1 = y0 + y0 (1 - d y0);  q0 = n y1;  q = q0 + (n - d q0) y1.
+// d > 2^64 is scaled by 2^-64 together with the numerator (exact), so the
+// estimate stays normal and a subnormal quotient is still rounded correctly.
+__device__ __forceinline__ float recip_rn_ge1(float d) {
+  const bool big = d > 1.8446744073709552e19f;
+  const float ds = big ? __fmul_rn(d, 5.421010862427522e-20f) : d;
+  const float n = big ? 5.421010862427522e-20f : 1.0f;
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(ds));
+  y = __fmaf_rn(y, __fmaf_rn(-ds, y, 1.0f), y);
+  const float q0 = __fmul_rn(n, y);
+  const float q = __fmaf_rn(__fmaf_rn(-ds, q0, n), y, q0);
+  return isinf(d) ? 0.0f : q;
+}
+
+__device__ __forceinline__ float sigmoid_triton_alu(float x) {
+  const float t = __fmul_rn(-x, 1.4426950408889634f);
+  float e;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t));
+  return recip_rn_ge1(__fadd_rn(1.0f, e));
+}
+
+// The reference's SwiGLU element (praxis/kernels/nvfp4_moe.py:125-128) on the
+// raw fp32 accumulators of gate and up: gemm output bf16(acc), rescale
+// bf16(. * mult), silu = bf16(gate * sigmoid(gate)), h = bf16(silu * up).
+// Returns h as a float (a bf16 value).
+template <bool kAlu>
+__device__ __forceinline__ float swiglu_element(float gate_acc, float up_acc, float mult) {
+  if constexpr (kAlu) {
+    const float g = bf16_round_alu(__fmul_rn(bf16_round_alu(gate_acc), mult));
+    const float u = bf16_round_alu(__fmul_rn(bf16_round_alu(up_acc), mult));
+    const float silu = bf16_round_alu(__fmul_rn(g, sigmoid_triton_alu(g)));
+    return bf16_round_alu(__fmul_rn(silu, u));
+  } else {
+    const float g = bf16_round(mul_rn(bf16_round(gate_acc), mult));
+    const float u = bf16_round(mul_rn(bf16_round(up_acc), mult));
+    const float silu = bf16_round(mul_rn(g, sigmoid_triton(g)));
+    return bf16_round(mul_rn(silu, u));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -165,7 +238,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA loads: every copy lands in the issuing CTA's own shared memory
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
@@ -260,6 +333,80 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
 }
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// CTA pairs (cluster of 2) for cta_group::2 MMAs. No multicast loads: each
+// CTA's TMA copies land in its own shared memory; only completion signals
+// and tcgen05.commit arrivals cross to the peer.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on the pair leader's mbarrier (`bar_cluster`, a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* desc, uint32_t bar_cluster, int32_t c0,
+                                                 int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrive on the mbarrier at the same offset in every CTA of `mask` once all
+// prior tcgen05 operations of this thread completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_nvf4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
 
 // Shared-memory matrix descriptor (sm_100 format): start address, leading
 // and stride byte offsets (16-byte units), version 1, layout type.

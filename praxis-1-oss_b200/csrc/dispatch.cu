@@ -136,20 +136,50 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
     int32_t* __restrict__ pcsr, TileEntry* __restrict__ tiles, int max_tiles, int32_t* __restrict__ num_tiles,
     float* __restrict__ act_global, uint32_t* __restrict__ act_amax_bits) {
   __shared__ int s_warp[32];
+  __shared__ int s_part[1024];
+  __shared__ uint32_t s_pmax[1024];
+  // Exclusive scan over segments per expert, in place (seg_count becomes the
+  // offset of the segment's first row inside its expert). Thread t handles
+  // expert t % E over one contiguous range of segments (consecutive threads
+  // read consecutive experts of a segment row).
+  const int parts = max(1, (int)blockDim.x / experts);
+  const int t = threadIdx.x;
+  const int te = t % experts, tp = t / experts;
+  const int span = (segments + parts - 1) / parts;
+  const int s0 = tp * span, s1 = min(segments, s0 + span);
+  int local = 0;
+  uint32_t lmax = 0;
+  if (tp < parts) {
+    for (int s = s0; s < s1; ++s) {
+      const int64_t i = (int64_t)s * experts + te;
+      local += seg_count[i];
+      lmax = max(lmax, seg_max[i]);
+    }
+    s_part[t] = local;
+    s_pmax[t] = lmax;
+  }
+  __syncthreads();
+  if (tp < parts) {
+    int before = 0;
+    for (int q = 0; q < tp; ++q) before += s_part[q * experts + te];
+    int run = before;
+    for (int s = s0; s < s1; ++s) {
+      const int64_t i = (int64_t)s * experts + te;
+      const int c = seg_count[i];
+      seg_count[i] = run;
+      run += c;
+    }
+  }
   const int e = threadIdx.x;
   int count = 0;
   uint32_t m = 0;
   if (e < experts) {
-    // exclusive scan over segments in place: seg_count becomes the offset of
-    // the segment's first row inside the expert.
-    for (int s = 0; s < segments; ++s) {
-      const int64_t i = (int64_t)s * experts + e;
-      const int c = seg_count[i];
-      seg_count[i] = count;
-      count += c;
-      m = max(m, seg_max[i]);
+    for (int q = 0; q < parts; ++q) {
+      count += s_part[q * experts + e];
+      m = max(m, s_pmax[q * experts + e]);
     }
   }
+  __syncthreads();
   int total = 0;
   const int start = block_exclusive_scan(e < experts ? count : 0, s_warp, &total);
   if (e < experts) {
@@ -182,7 +212,30 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
       }
     }
   }
-  if (threadIdx.x == 0) *num_tiles = min(tiles_total, max_tiles);
+  // Pair table (256-row units of the 2-CTA GEMM) after the tile table:
+  // {expert, first padded row, routed rows of the 256 (1..256), live rows
+  // (rows of the expert's 128-row tiles inside the 256)}.
+  const int npair = e < experts ? (count + 2 * kTileRows - 1) / (2 * kTileRows) : 0;
+  int pairs_total = 0;
+  const int pstart_idx = block_exclusive_scan(npair, s_warp, &pairs_total);
+  if (e < experts) {
+    const int64_t pstart = ((int64_t)start + (int64_t)(align - 1) * e) / align * align;
+    const int live_total = ntile * kTileRows;
+    for (int j = 0; j < npair; ++j) {
+      if (pstart_idx + j < max_tiles) {
+        TileEntry t;
+        t.expert = e;
+        t.row0 = (int32_t)(pstart + (int64_t)j * 2 * kTileRows);
+        t.valid = min(2 * kTileRows, count - j * 2 * kTileRows);
+        t.pad = min(2 * kTileRows, live_total - j * 2 * kTileRows);
+        tiles[max_tiles + pstart_idx + j] = t;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    num_tiles[0] = min(tiles_total, max_tiles);
+    num_tiles[1] = min(pairs_total, max_tiles);
+  }
 }
 
 // ---------------------------------------------------------------------------

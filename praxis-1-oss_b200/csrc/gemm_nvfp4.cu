@@ -208,30 +208,26 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
       const size_t grow = (size_t)t.row0 + row_in_tile;
       const uint32_t taddr = tmem + ((quad * 32u) << 16) + acc * BLOCK_N;
       if constexpr (EPI == EPI_SWIGLU) {
+        // B rows come in 64-row blocks of 32 gate rows then the matching 32
+        // up rows (praxis_b200_interleave_gate_up): tile columns [64c, 64c+32)
+        // are gate and [64c+32, 64c+64) up for hidden columns 32c.. of the tile.
         const float mult = expert_multiplier(p, t.expert);
         float rmax = 0.0f;
         constexpr int HALF = BLOCK_N / 2;
 #pragma unroll 1
         for (int c = 0; c < HALF / 32; ++c) {
           uint32_t g[32], up[32];
-          tc_ld_32x32b_x32(taddr + c * 32, g);
-          tc_ld_32x32b_x32(taddr + HALF + c * 32, up);
+          tc_ld_32x32b_x32(taddr + c * 64, g);
+          tc_ld_32x32b_x32(taddr + c * 64 + 32, up);
           tc_wait_ld();
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            uint32_t hv[2];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const float gate = bf16_round(mul_rn(bf16_round(__uint_as_float(g[j + i])), mult));
-              const float upv = bf16_round(mul_rn(bf16_round(__uint_as_float(up[j + i])), mult));
-              const float silu = bf16_round(mul_rn(gate, sigmoid_triton(gate)));
-              uint16_t h = f32_to_bf16(mul_rn(silu, upv));
-              if (!valid) h = 0;
-              rmax = fmaxf(rmax, fabsf(bf16_to_f32(h)));
-              hv[i] = h;
-            }
-            packed[j / 2] = hv[0] | (hv[1] << 16);
+            float h0 = swiglu_element<true>(__uint_as_float(g[j]), __uint_as_float(up[j]), mult);
+            float h1 = swiglu_element<true>(__uint_as_float(g[j + 1]), __uint_as_float(up[j + 1]), mult);
+            if (!valid) h0 = h1 = 0.0f;
+            rmax = fmaxf(rmax, fmaxf(fabsf(h0), fabsf(h1)));
+            packed[j / 2] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632);
           }
           store_row_chunk(p.out + grow * p.out_cols + (size_t)n * HALF + c * 32, packed);
         }
@@ -249,13 +245,13 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
             uint32_t packed[16];
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-              float v0 = bf16_round(__uint_as_float(r[j]));
-              float v1 = bf16_round(__uint_as_float(r[j + 1]));
+              float v0 = __uint_as_float(r[j]);
+              float v1 = __uint_as_float(r[j + 1]);
               if constexpr (EPI == EPI_RESCALE) {
-                v0 = mul_rn(v0, mult);
-                v1 = mul_rn(v1, mult);
+                v0 = __fmul_rn(bf16_round_alu(v0), mult);
+                v1 = __fmul_rn(bf16_round_alu(v1), mult);
               }
-              packed[j / 2] = (uint32_t)f32_to_bf16(v0) | ((uint32_t)f32_to_bf16(v1) << 16);
+              packed[j / 2] = pack_bf16x2_alu(v0, v1);
             }
             store_row_chunk(p.out + grow * p.out_cols + (size_t)n * BLOCK_N + c * 32, packed);
           }
@@ -274,6 +270,271 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair kernel: M = 256 (128 rows per CTA), N = 256, cta_group::2.
+//
+// Each CTA loads its own 128 A rows and its own half (128 rows) of the B
+// tile; the pair's MMA reads B from both CTAs' shared memory, so per SM the
+// operand traffic per FLOP is half that of the 1-CTA 128x128 tile. Each CTA
+// also holds the scales of its A rows and of all 256 B rows (the MMA reads
+// SFB of every N column in each CTA's tensor memory).
+//
+// Tensor memory (512 columns per CTA): the accumulator of tile i starts at
+// column 0 for even i and 192 for odd i; the two overlap in 64 columns, which
+// the epilogue drains first and then releases, so the next tile's MMAs run
+// while the remaining 192 columns drain. Scales live in columns 448..495.
+//
+// Roles: warp 0 TMA (both CTAs; completion counted on the leader's barrier),
+// warp 1 tcgen05 issuer (leader CTA only), warps 2..9 epilogue (both CTAs,
+// two warps per TMEM lane quadrant, 128 columns each).
+// ---------------------------------------------------------------------------
+struct PairShape {
+  static constexpr int BN = 256;
+  static constexpr int BK_BYTES = 128;
+  static constexpr int STAGES = 5;
+  static constexpr int A_BYTES = 128 * BK_BYTES;
+  static constexpr int B_BYTES = 128 * BK_BYTES;
+  static constexpr int SFA_BYTES = 4 * 512;
+  static constexpr int SFB_BYTES = 2 * 4 * 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int ACC_ALT_COL = 192;  // start of every other accumulator
+  static constexpr int OVERLAP = 64;       // columns shared by consecutive accumulators
+  static constexpr int SFA_COL = 448;
+  static constexpr int SFB_COL = 464;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 1)
+    gemm_nvfp4_pair_kernel(const __grid_constant__ GemmParams p) {
+  using S = PairShape;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + S::STAGES * S::A_BYTES;
+  uint8_t* sSFA = sB + S::STAGES * S::B_BYTES;
+  uint8_t* sSFB = sSFA + S::STAGES * S::SFA_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + S::STAGES * S::SFB_BYTES);
+  uint64_t* full = bars;                   // leader: both CTAs' loads of a stage
+  uint64_t* empty = bars + S::STAGES;      // each CTA: stage free again
+  uint64_t* acc_full = bars + 2 * S::STAGES;
+  uint64_t* acc_empty = acc_full + 1;      // leader: 16 epilogue warps of the pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * S::EPI_WARPS);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_a);
+    tma_prefetch_desc(&p.tmap_b);
+    tma_prefetch_desc(&p.tmap_sfa);
+    tma_prefetch_desc(&p.tmap_sfb);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const TileEntry* pairs = p.tiles + p.max_tiles;
+  const int n_tiles = p.N / S::BN;
+  const int num_pairs = p.num_tiles[1];
+  const int total = num_pairs * n_tiles;
+  const int k_tiles = (p.K + 255) / 256;
+  const int kb_total = p.K / 64;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int u = cluster; u < total && ok; u += nclusters) {
+        const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
+        const TileEntry t = pairs[m];
+        const int a_row = t.row0 + 128 * (int)rank;
+        const int b_row = t.expert * p.N + n * S::BN + 128 * (int)rank;
+        // scale atoms as 256-byte rows: 8 rows per k-tile of a 128-row tile
+        const int sfa_row = ((t.row0 / 128 + (int)rank) * kb_total) * 2;
+        const int sfb_row0 = ((t.expert * (p.N / 128) + n * 2) * kb_total) * 2;
+        const int sfb_row1 = sfb_row0 + kb_total * 2;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_leader + stage * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+          tma_load_2d_pair(sA + stage * S::A_BYTES, &p.tmap_a, fb, kt * S::BK_BYTES, a_row);
+          tma_load_2d_pair(sB + stage * S::B_BYTES, &p.tmap_b, fb, kt * S::BK_BYTES, b_row);
+          tma_load_2d_pair(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, fb, 0, sfa_row + kt * 8);
+          tma_load_2d_pair(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, fb, 0, sfb_row0 + kt * 8);
+          tma_load_2d_pair(sSFB + stage * S::SFB_BYTES + 2048, &p.tmap_sfb, fb, 0, sfb_row1 + kt * 8);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- tcgen05 issuer (leader) ----------------
+      constexpr uint32_t idesc = idesc_nvf4(256, S::BN);
+      const uint32_t sfa_t = tmem + S::SFA_COL;
+      const uint32_t sfb_t = tmem + S::SFB_COL;
+      uint32_t stage = 0, phase = 0, it = 0;
+      bool ok = true;
+      for (int u = cluster; u < total && ok; u += nclusters, ++it) {
+        if (!mbar_wait(acc_empty, (it & 1u) ^ 1u, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + ((it & 1u) ? S::ACC_ALT_COL : 0u);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int kb_n = min(4, kb_total - kt * 4);
+          const uint32_t a_base = smem_u32(sA + stage * S::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
+          const uint32_t sfa_s = smem_u32(sSFA + stage * S::SFA_BYTES);
+          const uint32_t sfb_s = smem_u32(sSFB + stage * S::SFB_BYTES);
+          for (int kb = 0; kb < kb_n; ++kb) {
+            tc_cp_32x128b_warpx4_pair(sfa_t + kb * 4, smem_desc(sfa_s + kb * 512, 0, 128, kLayoutSwizzleNone));
+            tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8, smem_desc(sfb_s + kb * 512, 0, 128, kLayoutSwizzleNone));
+            tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8 + 4,
+                                      smem_desc(sfb_s + 2048 + kb * 512, 0, 128, kLayoutSwizzleNone));
+          }
+          for (int kb = 0; kb < kb_n; ++kb) {
+            const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+            const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+            tc_mma_nvf4_pair(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * 8, (kt | kb) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(acc_full, 0x3);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const uint32_t quad = (uint32_t)(warp & 3);
+    const int half = (warp - 2) >> 2;  // columns [128*half, 128*half + 128)
+    const int row_in_tile = (int)(quad * 32 + lane);
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(acc_empty), 0);
+    uint32_t it = 0;
+    for (int u = cluster; u < total; u += nclusters, ++it) {
+      const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
+      const TileEntry t = pairs[m];
+      if (!mbar_wait(acc_full, it & 1u, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const bool odd = (it & 1u) != 0;
+      // The 64 columns this tile shares with the next accumulator: the last
+      // block of an even tile (half 1), the first block of an odd tile (half 0).
+      const bool owns_overlap = odd ? (half == 0) : (half == 1);
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(acc_empty);
+          else mbar_arrive_cluster(acc_empty_leader);
+        }
+      };
+      if (!owns_overlap) release();
+      const int here_valid = min(max(t.valid - 128 * (int)rank, 0), 128);
+      const int here_live = min(max(t.pad - 128 * (int)rank, 0), 128);
+      const bool valid = row_in_tile < here_valid;
+      const bool live = row_in_tile < here_live;
+      const size_t grow = (size_t)t.row0 + 128 * rank + row_in_tile;
+      const uint32_t tbase = tmem + ((quad * 32u) << 16) + (odd ? S::ACC_ALT_COL : 0u);
+      const float mult = (EPI == EPI_PLAIN) ? 1.0f : expert_multiplier(p, t.expert);
+      float rmax = 0.0f;
+#pragma unroll 1
+      for (int i = 0; i < 2; ++i) {
+        // 64-column blocks of this warp; the overlapping block goes first
+        const int blk = 2 * half + ((owns_overlap && !odd) ? 1 - i : i);
+        uint32_t r0[32], r1[32];
+        tc_ld_32x32b_x32(tbase + blk * 64, r0);
+        tc_ld_32x32b_x32(tbase + blk * 64 + 32, r1);
+        tc_wait_ld();
+        if (owns_overlap && i == 0) release();
+        uint32_t packed[16];
+        if constexpr (EPI == EPI_SWIGLU) {
+          // block = 32 gate columns then the matching 32 up columns
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float h0 = swiglu_element<true>(__uint_as_float(r0[j]), __uint_as_float(r1[j]), mult);
+            float h1 = swiglu_element<true>(__uint_as_float(r0[j + 1]), __uint_as_float(r1[j + 1]), mult);
+            if (!valid) h0 = h1 = 0.0f;
+            rmax = fmaxf(rmax, fmaxf(fabsf(h0), fabsf(h1)));
+            packed[j / 2] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632);
+          }
+          if (live) store_row_chunk(p.out + grow * p.out_cols + (size_t)n * (S::BN / 2) + blk * 32, packed);
+        } else {
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float v0 = __uint_as_float(r0[j]), v1 = __uint_as_float(r0[j + 1]);
+              if constexpr (EPI == EPI_RESCALE) {
+                v0 = __fmul_rn(bf16_round_alu(v0), mult);
+                v1 = __fmul_rn(bf16_round_alu(v1), mult);
+              }
+              packed[j / 2] = pack_bf16x2_alu(v0, v1);
+            }
+            store_row_chunk(p.out + grow * p.out_cols + (size_t)n * S::BN + blk * 64, packed);
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float v0 = __uint_as_float(r1[j]), v1 = __uint_as_float(r1[j + 1]);
+              if constexpr (EPI == EPI_RESCALE) {
+                v0 = __fmul_rn(bf16_round_alu(v0), mult);
+                v1 = __fmul_rn(bf16_round_alu(v1), mult);
+              }
+              packed[j / 2] = pack_bf16x2_alu(v0, v1);
+            }
+            store_row_chunk(p.out + grow * p.out_cols + (size_t)n * S::BN + blk * 64 + 32, packed);
+          }
+        }
+      }
+      if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+        if (lane == 0) atomicMax(p.amax_out + t.expert, __float_as_uint(rmax));
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // all tensor-memory reads and cross-CTA signals of the pair done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, S::TMEM_COLS);
   }
 }
 
@@ -330,6 +591,64 @@ static int launch_gemm(const GemmParams& p, int max_tiles, cudaStream_t stream) 
   return check_launch("gemm_nvfp4");
 }
 
+// Scale-factor atoms viewed as rows of 256 bytes (8 rows = the 4 atoms of
+// one k-tile of a 128-row tile), box {256 B, 8 rows}, no swizzle.
+static int make_bytes_map(CUtensorMap* map, const void* base, size_t bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (bytes % 256 != 0 || bytes == 0) return set_error(PRAXIS_B200_EINVAL, "scale buffer size %zu", bytes);
+  cuuint64_t gdim[2] = {256u, (cuuint64_t)(bytes / 256)};
+  cuuint64_t gstride[1] = {256u};
+  cuuint32_t box[2] = {256u, 8u};
+  cuuint32_t estride[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", (int)r);
+  return PRAXIS_B200_OK;
+}
+
+// 0: CTA-pair kernel where N % 256 == 0 (default); 1: the 1-CTA kernel
+// (PRAXIS_B200_GEMM=single).
+static int gemm_variant() {
+  const char* s = getenv("PRAXIS_B200_GEMM");
+  return (s != nullptr && strcmp(s, "single") == 0) ? 1 : 0;
+}
+
+template <int EPI>
+static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t stream) {
+  using S = PairShape;
+  auto kernel = gemm_nvfp4_pair_kernel<EPI>;
+  static int max_clusters[8] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 8) return set_error(PRAXIS_B200_EINVAL, "device index %d", dev);
+  if (max_clusters[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "pair gemm smem attribute: %s", cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    cfg.blockDim = dim3(S::THREADS);
+    cfg.dynamicSmemBytes = S::SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    if (e != cudaSuccess || n <= 0) n = sm_count() / 2;
+    max_clusters[dev] = n;
+  }
+  const int units = max_tiles * (p.N / S::BN);
+  if (units <= 0) return PRAXIS_B200_OK;
+  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  kernel<<<2 * clusters, S::THREADS, S::SMEM_BYTES, stream>>>(p);
+  return check_launch("gemm_nvfp4_pair");
+}
+
 int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, const TileEntry* tiles,
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
@@ -367,6 +686,21 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.act_amax = act_amax;
   p.w_global = w_global;
   p.amax_out = amax_out;
+  p.max_tiles = max_tiles;
+  if (n % PairShape::BN == 0 && gemm_variant() == 0) {
+    rc = make_bytes_map(&p.tmap_sfa, a_sf, (size_t)rows_padded * (k / 16));
+    if (rc) return rc;
+    rc = make_bytes_map(&p.tmap_sfb, b_sf, (size_t)experts * n * (k / 16));
+    if (rc) return rc;
+    switch (epilogue) {
+      case EPI_SWIGLU:
+        return launch_gemm_pair<EPI_SWIGLU>(p, max_tiles, stream);
+      case EPI_RESCALE:
+        return launch_gemm_pair<EPI_RESCALE>(p, max_tiles, stream);
+      default:
+        return launch_gemm_pair<EPI_PLAIN>(p, max_tiles, stream);
+    }
+  }
   switch (epilogue) {
     case EPI_SWIGLU:
       return launch_gemm<128, EPI_SWIGLU>(p, max_tiles, stream);

@@ -14,12 +14,15 @@ namespace praxis {
 enum Epilogue : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESCALE = 2 };
 
 struct GemmParams {
-  CUtensorMap tmap_a;  // packed FP4 activation rows (padded, expert-grouped)
-  CUtensorMap tmap_b;  // packed FP4 weights, E*N rows
+  CUtensorMap tmap_a;    // packed FP4 activation rows (padded, expert-grouped)
+  CUtensorMap tmap_b;    // packed FP4 weights, E*N rows
+  CUtensorMap tmap_sfa;  // A scales as 256-byte rows (2-CTA kernel)
+  CUtensorMap tmap_sfb;  // B scales as 256-byte rows (2-CTA kernel)
   const uint8_t* sfa;  // swizzled UE4M3 scales of A
   const uint8_t* sfb;  // swizzled UE4M3 scales of B, per expert
-  const TileEntry* tiles;
-  const int32_t* num_tiles;
+  const TileEntry* tiles;   // 128-row tiles; the 256-row pairs follow at tiles + max_tiles
+  const int32_t* num_tiles; // {tiles, pairs}
+  int32_t max_tiles;
   int32_t N;
   int32_t K;
   uint16_t* out;

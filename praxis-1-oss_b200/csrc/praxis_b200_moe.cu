@@ -8,4 +8,5 @@
 #include "quantize.cu"
 #include "gemm_nvfp4.cu"
 #include "combine.cu"
+#include "swiglu.cu"
 #include "capi.cu"

@@ -215,14 +215,14 @@ __global__ void pack_quant_kernel(const uint16_t* __restrict__ w, int k_dim, int
 
 // ---------------------------------------------------------------------------
 // Gate/up interleave: kernel-layout row r of an expert's [2F, C] gate_up
-// matrix is gate row 64*(r/128) + r%128 for r%128 < 64, else up row
-// F + 64*(r/128) + r%128 - 64. One CTA per (row, expert).
+// matrix is gate row 32*(r/64) + r%64 for r%64 < 32, else up row
+// F + 32*(r/64) + r%64 - 32. One CTA per (row, expert).
 // ---------------------------------------------------------------------------
 __global__ void interleave_gate_up_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sf, int f_dim,
                                           int c_dim, uint8_t* __restrict__ q_out, uint8_t* __restrict__ sf_out) {
   const int r = blockIdx.x, e = blockIdx.y;
-  const int blk = r / 128, w = r % 128;
-  const int src = w < 64 ? 64 * blk + w : f_dim + 64 * blk + (w - 64);
+  const int blk = r / 64, w = r % 64;
+  const int src = w < 32 ? 32 * blk + w : f_dim + 32 * blk + (w - 32);
   const int64_t rows = 2 * (int64_t)f_dim;
   const uint4* qs = reinterpret_cast<const uint4*>(q + ((int64_t)e * rows + src) * (c_dim / 2));
   uint4* qd = reinterpret_cast<uint4*>(q_out + ((int64_t)e * rows + r) * (c_dim / 2));

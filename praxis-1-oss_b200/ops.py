@@ -146,8 +146,8 @@ def dispatch(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | Non
     offsets = torch.empty(e, **i32)
     csr = torch.empty(e + 1, **i32)
     pcsr = torch.empty(e + 1, **i32)
-    tiles = torch.empty(max(max_tiles, 1), 4, **i32)
-    num_tiles = torch.empty(1, **i32)
+    tiles = torch.empty(2 * max(max_tiles, 1), 4, **i32)  # 128-row tiles, then 256-row pairs
+    num_tiles = torch.empty(2, **i32)
     act_global = act_amax = None
     if amax is not None:
         _need(amax, "row amax", BF16, 1, dev)
@@ -218,6 +218,20 @@ def grouped_gemm(a_q: Tensor, a_sf: Tensor, b_q: Tensor, b_sf: Tensor, routing: 
         _p(a_q), _p(a_sf), _p(b_q), _p(b_sf), _p(routing.tiles), _p(routing.num_tiles), rp // 128, rp, n, kdim, e,
         epilogue, _p(out), _p(act_global), _p(act_amax), _p(w_global), _p(amax_out), _dev(a_q), _stream(a_q)))
     return out
+
+
+def rescale_swiglu(raw: Tensor, pcsr: Tensor, act_global: Tensor, w_global: Tensor, *, alu: bool = True
+                   ) -> tuple[Tensor, Tensor]:
+    """``rescale_swiglu_maximum`` (praxis/kernels/nvfp4_moe.py:136-158) on the
+    padded gate/up GEMM output; ``alu`` picks the fused epilogue's arithmetic."""
+    _need(raw, "raw", BF16, 2)
+    rows, h2 = raw.shape
+    out = torch.empty(rows, h2 // 2, dtype=BF16, device=raw.device)
+    rowmax = torch.empty(rows, dtype=BF16, device=raw.device)
+    capi.check(capi.load().praxis_b200_rescale_swiglu(
+        _p(raw), rows, h2 // 2, _p(pcsr), pcsr.numel() - 1, _p(act_global), _p(w_global), _p(out), _p(rowmax),
+        int(alu), _dev(raw), _stream(raw)))
+    return out, rowmax
 
 
 def combine(rows: Tensor, routing: Routing, scaling: float, *, h_global: Tensor | None = None,

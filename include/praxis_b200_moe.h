@@ -139,7 +139,8 @@ int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, co
  * blocks (praxis_b200_interleave_gate_up), out = hidden [Rp, N/2], amax_out[e]
  * atomically maxed with the bits of max |hidden|. EPI_RESCALE: out [Rp, N].
  * act_global (or act_amax) and w_global give bf16(g_act * g_w).
- * Rows of a tile past its valid count are not stored (EPI_SWIGLU stores 0).
+ * Rows of a tile past its valid count hold the products of the padding rows
+ * (zero for padding written by the quantize entry points; EPI_SWIGLU stores 0).
  * Replaces praxis/kernels/nvfp4.py:355-419 (grouped_nvfp4_mm) with
  * praxis/kernels/nvfp4_moe.py:102-158 (EPI_SWIGLU) or the rescale of
  * praxis/kernels/nvfp4_moe.py:236-247 (EPI_RESCALE) fused. N, K % 128 == 0. */

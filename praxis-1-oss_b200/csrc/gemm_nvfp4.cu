@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
 struct PairShape {
   static constexpr int BN = 256;
   static constexpr int BK_BYTES = 128;
-  static constexpr int STAGES = 5;
+  static constexpr int STAGES = 4;
   static constexpr int A_BYTES = 128 * BK_BYTES;
   static constexpr int B_BYTES = 128 * BK_BYTES;
   static constexpr int SFA_BYTES = 4 * 512;
@@ -307,8 +307,18 @@ struct PairShape {
   static constexpr int TMEM_COLS = 512;
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  // Output staging per epilogue warp: 32 rows x up to 128 bf16 columns as two
+  // 32 x 64 boxes of 4 KB in the TMA 128-byte swizzle.
+  static constexpr int OUT_STAGE_BYTES = 2 * 4096;
+  static constexpr size_t SMEM_BYTES =
+      1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EPI_WARPS * OUT_STAGE_BYTES + 256;
 };
+
+// Writes 8 bf16 (16 bytes) of row `row` (0..31), 16-byte chunk `chunk` (0..7)
+// of a 32 x 64 box staged in the TMA 128-byte swizzle (chunk ^ row % 8).
+__device__ __forceinline__ void stage_chunk(uint8_t* box, int row, int chunk, uint4 v) {
+  *reinterpret_cast<uint4*>(box + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
+}
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 1)
@@ -320,7 +330,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
   uint8_t* sB = sA + S::STAGES * S::A_BYTES;
   uint8_t* sSFA = sB + S::STAGES * S::B_BYTES;
   uint8_t* sSFB = sSFA + S::STAGES * S::SFA_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + S::STAGES * S::SFB_BYTES);
+  uint8_t* sOut = sSFB + S::STAGES * S::SFB_BYTES;  // 1 KB aligned (stage sizes are multiples of 1 KB)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + S::EPI_WARPS * S::OUT_STAGE_BYTES);
   uint64_t* full = bars;                   // leader: both CTAs' loads of a stage
   uint64_t* empty = bars + S::STAGES;      // each CTA: stage free again
   uint64_t* acc_full = bars + 2 * S::STAGES;
@@ -448,6 +459,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
     const int half = (warp - 2) >> 2;  // columns [128*half, 128*half + 128)
     const int row_in_tile = (int)(quad * 32 + lane);
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(acc_empty), 0);
+    uint8_t* stg = sOut + (warp - 2) * S::OUT_STAGE_BYTES;
     uint32_t it = 0;
     for (int u = cluster; u < total; u += nclusters, ++it) {
       const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
@@ -468,58 +480,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
       };
       if (!owns_overlap) release();
       const int here_valid = min(max(t.valid - 128 * (int)rank, 0), 128);
-      const int here_live = min(max(t.pad - 128 * (int)rank, 0), 128);
+      const bool live = t.pad - 128 * (int)rank > 0;  // this CTA's 128 rows are in live tiles
       const bool valid = row_in_tile < here_valid;
-      const bool live = row_in_tile < here_live;
-      const size_t grow = (size_t)t.row0 + 128 * rank + row_in_tile;
       const uint32_t tbase = tmem + ((quad * 32u) << 16) + (odd ? S::ACC_ALT_COL : 0u);
       const float mult = (EPI == EPI_PLAIN) ? 1.0f : expert_multiplier(p, t.expert);
       float rmax = 0.0f;
+      // the staging boxes are free once this warp's previous stores read them
+      if (lane == 0) bulk_wait_group_read0();
+      __syncwarp();
 #pragma unroll 1
       for (int i = 0; i < 2; ++i) {
         // 64-column blocks of this warp; the overlapping block goes first
-        const int blk = 2 * half + ((owns_overlap && !odd) ? 1 - i : i);
+        const int bl = (owns_overlap && !odd) ? 1 - i : i;
+        const int blk = 2 * half + bl;
         uint32_t r0[32], r1[32];
         tc_ld_32x32b_x32(tbase + blk * 64, r0);
         tc_ld_32x32b_x32(tbase + blk * 64 + 32, r1);
         tc_wait_ld();
         if (owns_overlap && i == 0) release();
-        uint32_t packed[16];
         if constexpr (EPI == EPI_SWIGLU) {
-          // block = 32 gate columns then the matching 32 up columns
+          // block = 32 gate columns then the matching 32 up columns -> 32
+          // hidden columns: chunks 4*bl .. 4*bl+3 of the warp's 64-column box
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float h0 = swiglu_element<true>(__uint_as_float(r0[j]), __uint_as_float(r1[j]), mult);
-            float h1 = swiglu_element<true>(__uint_as_float(r0[j + 1]), __uint_as_float(r1[j + 1]), mult);
-            if (!valid) h0 = h1 = 0.0f;
-            rmax = fmaxf(rmax, fmaxf(fabsf(h0), fabsf(h1)));
-            packed[j / 2] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632);
+          for (int c = 0; c < 4; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int e0 = c * 8 + 2 * j;
+              float h0 = swiglu_element<true>(__uint_as_float(r0[e0]), __uint_as_float(r1[e0]), mult);
+              float h1 = swiglu_element<true>(__uint_as_float(r0[e0 + 1]), __uint_as_float(r1[e0 + 1]), mult);
+              if (!valid) h0 = h1 = 0.0f;
+              rmax = fmaxf(rmax, fmaxf(fabsf(h0), fabsf(h1)));
+              w[j] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632);
+            }
+            stage_chunk(stg, (int)lane, 4 * bl + c, make_uint4(w[0], w[1], w[2], w[3]));
           }
-          if (live) store_row_chunk(p.out + grow * p.out_cols + (size_t)n * (S::BN / 2) + blk * 32, packed);
         } else {
-          if (valid) {
+          uint8_t* box = stg + bl * 4096;
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              float v0 = __uint_as_float(r0[j]), v1 = __uint_as_float(r0[j + 1]);
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t* r = c < 4 ? r0 : r1;
+            const int b0 = (c & 3) * 8;
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float v0 = __uint_as_float(r[b0 + 2 * j]), v1 = __uint_as_float(r[b0 + 2 * j + 1]);
               if constexpr (EPI == EPI_RESCALE) {
                 v0 = __fmul_rn(bf16_round_alu(v0), mult);
                 v1 = __fmul_rn(bf16_round_alu(v1), mult);
               }
-              packed[j / 2] = pack_bf16x2_alu(v0, v1);
+              w[j] = pack_bf16x2_alu(v0, v1);
             }
-            store_row_chunk(p.out + grow * p.out_cols + (size_t)n * S::BN + blk * 64, packed);
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              float v0 = __uint_as_float(r1[j]), v1 = __uint_as_float(r1[j + 1]);
-              if constexpr (EPI == EPI_RESCALE) {
-                v0 = __fmul_rn(bf16_round_alu(v0), mult);
-                v1 = __fmul_rn(bf16_round_alu(v1), mult);
-              }
-              packed[j / 2] = pack_bf16x2_alu(v0, v1);
-            }
-            store_row_chunk(p.out + grow * p.out_cols + (size_t)n * S::BN + blk * 64 + 32, packed);
+            stage_chunk(box, (int)lane, c, make_uint4(w[0], w[1], w[2], w[3]));
           }
         }
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0 && live) {
+        const int row = t.row0 + 128 * (int)rank + (int)quad * 32;
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_store_2d(&p.tmap_out, stg, n * (S::BN / 2) + 64 * half, row);
+        } else {
+          tma_store_2d(&p.tmap_out, stg, n * S::BN + 128 * half, row);
+          tma_store_2d(&p.tmap_out, stg + 4096, n * S::BN + 128 * half + 64, row);
+        }
+        bulk_commit_group();
       }
       if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll
@@ -527,6 +553,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
         if (lane == 0) atomicMax(p.amax_out + t.expert, __float_as_uint(rmax));
       }
     }
+    if (lane == 0) bulk_wait_group0();
   }
 
   __syncwarp();
@@ -605,6 +632,22 @@ static int make_bytes_map(CUtensorMap* map, const void* base, size_t bytes) {
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", (int)r);
+  return PRAXIS_B200_OK;
+}
+
+// bf16 output rows [rows, cols]: box {64 columns (128 B), 32 rows}, the TMA
+// 128-byte swizzle (the epilogue stages each 32-row slab in that layout).
+static int make_out_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64u, 32u};
+  cuuint32_t estride[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
   return PRAXIS_B200_OK;
 }
 
@@ -691,6 +734,8 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
     rc = make_bytes_map(&p.tmap_sfa, a_sf, (size_t)rows_padded * (k / 16));
     if (rc) return rc;
     rc = make_bytes_map(&p.tmap_sfb, b_sf, (size_t)experts * n * (k / 16));
+    if (rc) return rc;
+    rc = make_out_map(&p.tmap_out, out, rows_padded, out_cols);
     if (rc) return rc;
     switch (epilogue) {
       case EPI_SWIGLU:

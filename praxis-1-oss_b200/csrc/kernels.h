@@ -18,6 +18,7 @@ struct GemmParams {
   CUtensorMap tmap_b;    // packed FP4 weights, E*N rows
   CUtensorMap tmap_sfa;  // A scales as 256-byte rows (2-CTA kernel)
   CUtensorMap tmap_sfb;  // B scales as 256-byte rows (2-CTA kernel)
+  CUtensorMap tmap_out;  // bf16 output rows, 64-column x 32-row boxes (2-CTA kernel)
   const uint8_t* sfa;  // swizzled UE4M3 scales of A
   const uint8_t* sfb;  // swizzled UE4M3 scales of B, per expert
   const TileEntry* tiles;   // 128-row tiles; the 256-row pairs follow at tiles + max_tiles

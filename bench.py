@@ -250,15 +250,15 @@ def run_b200(args, cfg):
     bank = mod.routed
     bank.prepare()
     terms = mod.router_terms()
-    gq, gsf = bank._kernel_gate_up
+    kw = bank.kernel_weights()
     x = x_cpu.to(dev)
     out = torch.empty_like(x)
     ops = pkg.ops
 
     def step():
-        return ops.moe_forward(x, None, None, gq, gsf, bank.gate_up_global, bank.down_q, bank.down_sf,
-                               bank.down_global, 2.5, router_terms=terms, router_bias=mod.expert_bias, top_k=k,
-                               out=out)
+        return ops.moe_forward(x, None, None, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
+                               kw.down_sf, bank.down_global, 2.5, router_terms=terms, router_bias=mod.expert_bias,
+                               top_k=k, out=out, weight_sf_layout=kw.sf_layout)
 
     # correctness guard of the measured path: routing and output vs the
     # stage-by-stage ops path (same kernels, separate launches)
@@ -290,12 +290,12 @@ def run_b200(args, cfg):
 
     # per-stage timing (same kernels launched stage by stage, events on the
     # launching stream) for the roofline of the dominant kernel
-    stages = time_stages(pkg, x, terms, mod, bank, gq, gsf, cfg, reps=max(3, min(args.steps, 10)))
+    stages = time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=max(3, min(args.steps, 10)))
     gemm1_ms = stages["gemm1_swiglu"]
     flops1 = 2.0 * t * k * c * 2 * f
     bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
     fp4_peak = 4.0 * bf16_peak
-    roofline = {"bound": "tensor", "kernel": "gemm_nvfp4_kernel<128, EPI_SWIGLU> (gate/up)",
+    roofline = {"bound": "tensor", "kernel": "gemm_nvfp4_pair_kernel<EPI_SWIGLU> (gate/up)",
                 "achieved": flops1 / (gemm1_ms / 1e3) / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
                 "frac": flops1 / (gemm1_ms / 1e3) / 1e12 / fp4_peak, "traffic": None,
                 "peak_note": ("dense FP4 peak = 4 x measured cuBLAS bf16 burst "
@@ -328,7 +328,7 @@ def run_b200(args, cfg):
         dist.destroy_process_group()
 
 
-def time_stages(pkg, x, terms, mod, bank, gq, gsf, cfg, reps=5):
+def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
     import torch
 
     ops, capi = pkg.ops, pkg.capi
@@ -346,18 +346,19 @@ def time_stages(pkg, x, terms, mod, bank, gq, gsf, cfg, reps=5):
         evs[2].record(stream)
         r = ops.dispatch(top, gate, cfg["experts"], amax, full=False)
         evs[3].record(stream)
-        aq, asf = ops.quantize_gather(x, r, r.act_global)
+        aq, asf = ops.quantize_gather(x, r, r.act_global, sf_layout=kw.sf_layout)
         evs[4].record(stream)
         hamax = torch.zeros(cfg["experts"], dtype=torch.int32, device=x.device)
         e_g0 = torch.cuda.Event(enable_timing=True)
         e_g0.record(stream)
-        hidden = ops.grouped_gemm(aq, asf, gq, gsf, r, epilogue=capi.EPI_SWIGLU, act_global=r.act_global,
-                                  w_global=bank.gate_up_global, amax_out=hamax)
+        hidden = ops.grouped_gemm(aq, asf, kw.gate_up_q, kw.gate_up_sf, r, epilogue=capi.EPI_SWIGLU,
+                                  act_global=r.act_global, w_global=bank.gate_up_global, amax_out=hamax,
+                                  sf_layout=kw.sf_layout)
         evs[5].record(stream)
-        hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
+        hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax, sf_layout=kw.sf_layout)
         evs[6].record(stream)
-        rows = ops.grouped_gemm(hq, hsf, bank.down_q, bank.down_sf, r, epilogue=capi.EPI_RESCALE, act_amax=hamax,
-                                w_global=bank.down_global)
+        rows = ops.grouped_gemm(hq, hsf, bank.down_q, kw.down_sf, r, epilogue=capi.EPI_RESCALE, act_amax=hamax,
+                                w_global=bank.down_global, sf_layout=kw.sf_layout)
         evs[7].record(stream)
         ops.combine(rows, r, 2.5, rows_rescaled=True)
         evs[8].record(stream)

@@ -52,6 +52,18 @@ enum {
   PRAXIS_B200_EPI_RESCALE = 2  /* out = bf16(bf16(acc) * bf16(g_act * g_w)) */
 };
 
+/* Layouts of the UE4M3 block-scale ("sf") buffers.
+ * COMPACT     the reference's layout (praxis/kernels/nvfp4.py:114-119):
+ *             per 128-row tile and 64-element k-block one 512-byte atom,
+ *             byte (r%32)*16 + ((r%128)/32)*4 + j%4 for row r, scale j.
+ * REPLICATED  this library's GEMM layout: every atom stored 4 times in a row
+ *             (the four tensor-memory lane quadrants each get a copy with one
+ *             128x256b tcgen05 copy). Activations: [tile][k-block][4][512 B];
+ *             weights: [expert][256-row tile][k-block][2 x 128-row][4][512 B].
+ *             Produced by the quantize entry points and
+ *             praxis_b200_replicate_scales. */
+enum { PRAXIS_B200_SF_COMPACT = 0, PRAXIS_B200_SF_REPLICATED = 1 };
+
 int praxis_b200_abi_version(void);
 const char* praxis_b200_last_error(void);
 /* Number of SMs of `device`; 0 if it is not an sm_100 device. */
@@ -114,7 +126,8 @@ int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* r
 /* NVFP4 quantization of the routed rows (gathered from x [T, C] bf16 through
  * inverse/top_idx) into the padded expert-grouped layout: q [Rp, C/2] (two
  * E2M1 codes per byte, even element low), sf [Rp, C/16] (UE4M3, 128x4
- * swizzled atoms); padding rows of the listed tiles are zeroed. Global scale
+ * swizzled atoms; 4x that size for sf_layout PRAXIS_B200_SF_REPLICATED);
+ * padding rows of the listed tiles are zeroed. Global scale
  * per expert from act_global, or from act_amax when act_global is NULL.
  * Replaces praxis/kernels/nvfp4.py:197-254 + :44-124 (quantize_activations
  * with row_indices, alignment=128, grouped_scales=False). C % 64 == 0. */
@@ -122,15 +135,17 @@ int praxis_b200_quantize_gather(const void* x, int64_t tokens, int32_t dim, cons
                                 const int64_t* inverse, const int32_t* csr, const int32_t* pcsr,
                                 const float* act_global, const uint32_t* act_amax, int32_t top_k,
                                 int32_t experts, const int32_t* tiles, const int32_t* num_tiles,
-                                int32_t max_tiles, void* q, void* sf, int device, void* stream);
+                                int32_t max_tiles, void* q, void* sf, int32_t sf_layout, int device,
+                                void* stream);
 
 /* NVFP4 quantization of every row of the listed tiles of x [Rp, K] (bf16),
- * global per expert from globals, or from amax (fp32 bits) when NULL.
+ * global per expert from globals, or from amax (fp32 bits) when NULL;
+ * sf in sf_layout (as praxis_b200_quantize_gather).
  * Replaces praxis/kernels/nvfp4.py:197-254 for the hidden activations
  * (praxis/quantization/nvfp4.py:365-372). K % 64 == 0. */
 int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, const int32_t* num_tiles,
                               int32_t max_tiles, const float* globals, const uint32_t* amax, void* q, void* sf,
-                              int device, void* stream);
+                              int32_t sf_layout, int device, void* stream);
 
 /* Grouped NVFP4 GEMM on tcgen05: for each listed tile (expert e, rows r),
  * acc[r, n] = sum_k dq(a[r, k]) * dq(b[e, n, k]) (alpha = 1), then the
@@ -139,6 +154,9 @@ int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, co
  * blocks (praxis_b200_interleave_gate_up), out = hidden [Rp, N/2], amax_out[e]
  * atomically maxed with the bits of max |hidden|. EPI_RESCALE: out [Rp, N].
  * act_global (or act_amax) and w_global give bf16(g_act * g_w).
+ * sf_layout PRAXIS_B200_SF_COMPACT: both scale buffers in the reference's
+ * layout; PRAXIS_B200_SF_REPLICATED: a_sf replicated in 128-row groups and
+ * b_sf in 256-row groups (praxis_b200_replicate_scales), N % 256 == 0.
  * Rows of a tile past its valid count hold the products of the padding rows
  * (zero for padding written by the quantize entry points; EPI_SWIGLU stores 0).
  * Replaces praxis/kernels/nvfp4.py:355-419 (grouped_nvfp4_mm) with
@@ -148,7 +166,14 @@ int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q,
                              const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles,
                              int64_t rows_padded, int32_t n, int32_t k, int32_t experts, int32_t epilogue,
                              void* out, const float* act_global, const uint32_t* act_amax, const float* w_global,
-                             uint32_t* amax_out, int device, void* stream);
+                             uint32_t* amax_out, int32_t sf_layout, int device, void* stream);
+
+/* Copies compact scales sf [rows, k/16] (the reference's swizzled layout)
+ * into the replicated GEMM layout out [4 * rows * k/16]: group_rows = 128 for
+ * activations, 256 for weights (rows = E * N, N % 256 == 0). rows % group_rows
+ * == 0, k % 64 == 0. Kernel-side layout only: no reference counterpart. */
+int praxis_b200_replicate_scales(const void* sf, int64_t rows, int32_t k, int32_t group_rows, void* out,
+                                 int device, void* stream);
 
 /* Rescale + SwiGLU + row max over the padded gate/up GEMM output raw
  * [rows, 2F] (bf16, gate columns first): m = bf16(act_global[e] * w_global[e])
@@ -181,7 +206,7 @@ int praxis_b200_pack_weights(const void* w, int32_t experts, int32_t k, int32_t 
                              float* global_out, uint32_t* scratch, int device, void* stream);
 
 /* Copies gate_up q [E, 2F, C/2] / sf [E, 2F, C/16] into the fused-SwiGLU
- * GEMM layout: 128-row blocks of 64 gate rows then the matching 64 up rows.
+ * GEMM layout: 64-row blocks of 32 gate rows then the matching 32 up rows.
  * Kernel-side layout only (the reference keeps gate rows 0..F-1, up rows
  * F..2F-1: praxis/quantization/nvfp4.py:132-144). */
 int praxis_b200_interleave_gate_up(const void* q, const void* sf, int32_t experts, int32_t hidden, int32_t dim,
@@ -206,6 +231,7 @@ typedef struct praxis_b200_moe_args {
   const void* down_q;        /* [E, C, F/2] */
   const void* down_sf;       /* [E, C, F/16] */
   const float* down_global;
+  int32_t weight_sf_layout;  /* layout of gate_up_sf and down_sf (PRAXIS_B200_SF_*) */
   int64_t tokens;
   int32_t dim;               /* C */
   int32_t hidden;            /* F */

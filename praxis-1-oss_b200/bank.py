@@ -18,16 +18,26 @@ from __future__ import annotations
 
 import math
 from collections.abc import Mapping
+from typing import NamedTuple
 
 import torch
 from torch import Tensor, nn
 
-from . import ops
+from . import capi, ops
 
 PACKING_RECIPE = "qat-reciprocal-v1"
 _BUFFER_NAMES = frozenset(
     ("gate_up_q", "gate_up_sf", "gate_up_global", "down_q", "down_sf", "down_global", "_unit_alpha")
 )
+
+
+class KernelWeights(NamedTuple):
+    """Device copies in the kernels' layouts (built by ``prepare()``)."""
+
+    gate_up_q: Tensor   # rows interleaved in 64-row blocks (32 gate, 32 up)
+    gate_up_sf: Tensor  # same row order; replicated or compact scales
+    down_sf: Tensor     # replicated or compact scales of down_q
+    sf_layout: int      # capi.SF_REPLICATED or capi.SF_COMPACT
 
 
 def _validate(state: Mapping[str, Tensor]) -> tuple[int, int, int]:
@@ -76,9 +86,10 @@ class B200NVFP4RoutedExperts(nn.Module):
 
     Device moves are supported; dtype casts, training and gradients are not
     (praxis/quantization/nvfp4.py:229-290). The fused SwiGLU GEMM reads the
-    gate/up weight in 64-row gate/up blocks: that copy is built on the device
-    by ``prepare()`` (called by the first forward; call it before capturing a
-    CUDA graph) and is not part of the state dict.
+    gate/up weight in 64-row gate/up blocks and both GEMMs read replicated
+    block scales: those copies are built on the device by ``prepare()``
+    (called by the first forward; call it before capturing a CUDA graph) and
+    are not part of the state dict.
     """
 
     format = "nvfp4"
@@ -91,7 +102,7 @@ class B200NVFP4RoutedExperts(nn.Module):
         self.num_experts, self.in_features, self.hidden_features = e, c, h
         for name in sorted(_BUFFER_NAMES):
             self.register_buffer(name, state[name].detach())
-        self._kernel_gate_up: tuple[Tensor, Tensor] | None = None
+        self._kernel: KernelWeights | None = None
         super().train(False)
 
     @classmethod
@@ -111,25 +122,36 @@ class B200NVFP4RoutedExperts(nn.Module):
             if other.dtype != value.dtype or other.shape != value.shape:
                 raise TypeError("NVFP4 buffers support device moves, not dtype/shape casts")
         self._buffers.update(moved)
-        self._kernel_gate_up = None
+        self._kernel = None
         return self
 
     def _load_from_state_dict(self, *args, **kwargs):
-        self._kernel_gate_up = None
+        self._kernel = None
         super()._load_from_state_dict(*args, **kwargs)
 
     def prepare(self) -> None:
-        """Build the kernel-layout gate/up copy on the buffers' device."""
+        """Build the kernel-layout weights on the buffers' device: gate/up
+        rows interleaved for the fused SwiGLU epilogue and, when C % 256 ==
+        0, both scale tensors in the GEMM's replicated layout (the packed
+        buffers themselves stay in the reference's layout)."""
         if self.gate_up_q.device.type != "cuda":
             raise RuntimeError("prepare() needs the bank on a CUDA device")
-        self._kernel_gate_up = ops.interleave_gate_up(self.gate_up_q, self.gate_up_sf)
+        gu_q, gu_sf = ops.interleave_gate_up(self.gate_up_q, self.gate_up_sf)
+        down_sf = self.down_sf
+        layout = capi.SF_COMPACT
+        if self.in_features % 256 == 0:
+            gu_sf = ops.replicate_scales(gu_sf, 256)
+            down_sf = ops.replicate_scales(down_sf, 256)
+            layout = capi.SF_REPLICATED
+        self._kernel = KernelWeights(gu_q, gu_sf, down_sf, layout)
 
-    def _kernel_weights(self) -> tuple[Tensor, Tensor]:
-        if self._kernel_gate_up is None:
+    def kernel_weights(self) -> KernelWeights:
+        """The kernel-layout weights (prepare() on first use)."""
+        if self._kernel is None:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("Call prepare() on the NVFP4 bank before CUDA Graph capture")
             self.prepare()
-        return self._kernel_gate_up
+        return self._kernel
 
     # -- the routed-bank protocol -------------------------------------------
     def routed_forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int,
@@ -194,14 +216,14 @@ class B200NVFP4RoutedExperts(nn.Module):
         """The dispatch-chunk loop of praxis/quantization/nvfp4.py:683-747;
         each chunk is one praxis_b200_moe_forward call."""
         self._check(x, top_idx, gate, scaling, chunk_size)
-        gu_q, gu_sf = self._kernel_weights()
+        kw = self.kernel_weights()
         out = torch.empty_like(x)
         for start in range(0, x.shape[0], chunk_size):
             end = min(start + chunk_size, x.shape[0])
             ops.moe_forward(
-                x[start:end], top_idx[start:end], gate[start:end], gu_q, gu_sf, self.gate_up_global,
-                self.down_q, self.down_sf, self.down_global, float(scaling),
-                None if shared is None else shared[start:end], out=out[start:end],
+                x[start:end], top_idx[start:end], gate[start:end], kw.gate_up_q, kw.gate_up_sf, self.gate_up_global,
+                self.down_q, kw.down_sf, self.down_global, float(scaling),
+                None if shared is None else shared[start:end], out=out[start:end], weight_sf_layout=kw.sf_layout,
             )
         return out
 

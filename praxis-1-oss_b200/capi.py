@@ -25,6 +25,7 @@ SZ = C.c_size_t
 OK, EINVAL, ECUDA, EUNSUPPORTED = 0, 1, 2, 3
 SIGMOID, SOFTMAX = 0, 1
 EPI_PLAIN, EPI_SWIGLU, EPI_RESCALE = 0, 1, 2
+SF_COMPACT, SF_REPLICATED = 0, 1
 
 
 class MoeArgs(C.Structure):
@@ -46,6 +47,7 @@ class MoeArgs(C.Structure):
         ("down_q", P),
         ("down_sf", P),
         ("down_global", P),
+        ("weight_sf_layout", I32),
         ("tokens", I64),
         ("dim", I32),
         ("hidden", I32),
@@ -76,13 +78,14 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "praxis_b200_quantize_gather": (
         C.c_int,
-        [P, I64, I32, P, P, P, P, P, P, I32, I32, P, P, I32, P, P, C.c_int, P],
+        [P, I64, I32, P, P, P, P, P, P, I32, I32, P, P, I32, P, P, I32, C.c_int, P],
     ),
-    "praxis_b200_quantize_rows": (C.c_int, [P, I32, P, P, I32, P, P, P, P, C.c_int, P]),
+    "praxis_b200_quantize_rows": (C.c_int, [P, I32, P, P, I32, P, P, P, P, I32, C.c_int, P]),
     "praxis_b200_grouped_gemm": (
         C.c_int,
-        [P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, P, P, P, P, P, C.c_int, P],
+        [P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, P, P, P, P, P, I32, C.c_int, P],
     ),
+    "praxis_b200_replicate_scales": (C.c_int, [P, I64, I32, I32, P, C.c_int, P]),
     "praxis_b200_rescale_swiglu": (C.c_int, [P, I64, I32, P, I32, P, P, P, P, I32, C.c_int, P]),
     "praxis_b200_combine": (
         C.c_int,

@@ -20,9 +20,11 @@ int run_row_amax(const uint16_t* x, int64_t rows, int cols, uint16_t* out, cudaS
 int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int64_t* top_idx, const int64_t* inverse,
                         const int32_t* csr, const int32_t* pcsr, const float* globals, const uint32_t* amax_bits,
                         int top_k, int experts, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
-                        uint8_t* q, uint8_t* sf, cudaStream_t stream);
+                        uint8_t* q, uint8_t* sf, int sf_layout, cudaStream_t stream);
 int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
-                      const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, cudaStream_t stream);
+                      const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, int sf_layout,
+                      cudaStream_t stream);
+int run_replicate_scales(const uint8_t* sf, int64_t rows, int k_dim, int group_rows, uint8_t* out, cudaStream_t stream);
 int run_pack_weights(const uint16_t* w, int experts, int k_dim, int n_dim, uint8_t* q, uint8_t* sf, float* global_out,
                      uint32_t* amax_scratch, cudaStream_t stream);
 int run_interleave_gate_up(const uint8_t* q, const uint8_t* sf, int experts, int f_dim, int c_dim, uint8_t* q_out,
@@ -122,10 +124,10 @@ static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int
   L.act_global = take((size_t)experts * 4);
   L.h_amax = take((size_t)experts * 4);
   L.aq = take((size_t)L.rp * dim / 2);
-  L.asf = take((size_t)L.rp * dim / 16);
+  L.asf = take((size_t)L.rp * dim / 16 * 4);  // room for the replicated layout
   L.hidden = take((size_t)L.rp * hidden * 2);
   L.hq = take((size_t)L.rp * hidden / 2);
-  L.hsf = take((size_t)L.rp * hidden / 16);
+  L.hsf = take((size_t)L.rp * hidden / 16 * 4);
   L.rows = take((size_t)L.rp * dim * 2);
   L.total = off;
   return L;
@@ -214,22 +216,23 @@ int praxis_b200_quantize_gather(const void* x, int64_t tokens, int32_t dim, cons
                                 const int64_t* inverse, const int32_t* csr, const int32_t* pcsr,
                                 const float* act_global, const uint32_t* act_amax, int32_t top_k, int32_t experts,
                                 const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles, void* q, void* sf,
-                                int device, void* stream) {
+                                int32_t sf_layout, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
   if (!x || !top_idx || !inverse || !csr || !pcsr || !tiles || !num_tiles || !q || !sf)
     return set_error(PRAXIS_B200_EINVAL, "quantize_gather: null pointer");
   return run_quantize_gather(static_cast<const uint16_t*>(x), tokens, dim, top_idx, inverse, csr, pcsr, act_global,
                              act_amax, top_k, experts, reinterpret_cast<const TileEntry*>(tiles), num_tiles,
-                             max_tiles, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), PRAXIS_STREAM(stream));
+                             max_tiles, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), sf_layout,
+                             PRAXIS_STREAM(stream));
 }
 
 int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, const int32_t* num_tiles,
                               int32_t max_tiles, const float* globals, const uint32_t* amax, void* q, void* sf,
-                              int device, void* stream) {
+                              int32_t sf_layout, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
   if (!x || !tiles || !num_tiles || !q || !sf) return set_error(PRAXIS_B200_EINVAL, "quantize_rows: null pointer");
   return run_quantize_rows(static_cast<const uint16_t*>(x), k, reinterpret_cast<const TileEntry*>(tiles), num_tiles,
-                           max_tiles, globals, amax, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf),
+                           max_tiles, globals, amax, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), sf_layout,
                            PRAXIS_STREAM(stream));
 }
 
@@ -237,14 +240,22 @@ int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q,
                              const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles, int64_t rows_padded,
                              int32_t n, int32_t k, int32_t experts, int32_t epilogue, void* out,
                              const float* act_global, const uint32_t* act_amax, const float* w_global,
-                             uint32_t* amax_out, int device, void* stream) {
+                             uint32_t* amax_out, int32_t sf_layout, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
   if (!a_q || !a_sf || !b_q || !b_sf || !tiles || !num_tiles || !out)
     return set_error(PRAXIS_B200_EINVAL, "grouped_gemm: null pointer");
   const int out_cols = epilogue == PRAXIS_B200_EPI_SWIGLU ? n / 2 : n;
   return run_grouped_gemm(a_q, a_sf, b_q, b_sf, reinterpret_cast<const TileEntry*>(tiles), num_tiles, max_tiles,
                           rows_padded, n, k, experts, epilogue, static_cast<uint16_t*>(out), out_cols, act_global,
-                          act_amax, w_global, amax_out, PRAXIS_STREAM(stream));
+                          act_amax, w_global, amax_out, sf_layout, PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_replicate_scales(const void* sf, int64_t rows, int32_t k, int32_t group_rows, void* out, int device,
+                                 void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!sf || !out) return set_error(PRAXIS_B200_EINVAL, "replicate_scales: null pointer");
+  return run_replicate_scales(static_cast<const uint8_t*>(sf), rows, k, group_rows, static_cast<uint8_t*>(out),
+                              PRAXIS_STREAM(stream));
 }
 
 int praxis_b200_rescale_swiglu(const void* raw, int64_t rows, int32_t hidden, const int32_t* pcsr,
@@ -299,6 +310,11 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   if (!a->x || !a->top_idx || !a->gate || !a->out || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
       !a->down_q || !a->down_sf || !a->down_global || !a->workspace)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: null pointer");
+  const int sf_layout = a->weight_sf_layout;
+  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: unknown weight scale layout %d", sf_layout);
+  if (sf_layout == PRAXIS_B200_SF_REPLICATED && a->dim % 256 != 0)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: replicated scales need C % 256 == 0");
   if (a->tokens < 0 || a->dim <= 0 || a->hidden <= 0 || a->experts <= 0 || a->top_k < 1 || a->top_k > 8 ||
       a->top_k > a->experts)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: bad sizes");
@@ -346,18 +362,18 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
                     L.max_tiles, num_tiles, act_global, act_amax, s);
   if (rc) return rc;
   rc = run_quantize_gather(x, a->tokens, a->dim, a->top_idx, inverse, csr, pcsr, act_global, nullptr, a->top_k,
-                           a->experts, tiles, num_tiles, L.max_tiles, aq, asf, s);
+                           a->experts, tiles, num_tiles, L.max_tiles, aq, asf, sf_layout, s);
   if (rc) return rc;
   cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * a->experts, s);
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
                         a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
-                        h_amax, s);
+                        h_amax, sf_layout, s);
   if (rc) return rc;
-  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq, hsf, s);
+  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq, hsf, sf_layout, s);
   if (rc) return rc;
   rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
-                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, s);
+                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, sf_layout, s);
   if (rc) return rc;
   return run_combine(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
                      a->scaling, static_cast<const uint16_t*>(a->shared), static_cast<uint16_t*>(a->out), a->tokens,

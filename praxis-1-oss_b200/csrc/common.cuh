@@ -419,6 +419,10 @@ __device__ __forceinline__ void tc_mma_nvf4_pair(uint32_t d_tmem, uint64_t a_des
       : "memory");
 }
 
+__device__ __forceinline__ void tc_cp_128x256b_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }

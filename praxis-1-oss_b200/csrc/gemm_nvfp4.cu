@@ -290,15 +290,27 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
 // Roles: warp 0 TMA (both CTAs; completion counted on the leader's barrier),
 // warp 1 tcgen05 issuer (leader CTA only), warps 2..9 epilogue (both CTAs,
 // two warps per TMEM lane quadrant, 128 columns each).
+//
+// Scale factors reach tensor memory in one of two ways:
+//  REP = false  the reference's compact layout (512-byte atom = 128 rows x 4
+//               scales); one tcgen05.cp 32x128b.warpx4 per atom replicates it
+//               into the four lane quadrants (12 copies per k-tile).
+//  REP = true   atoms stored four times in a row in global memory ("replicated
+//               layout", produced by this library's quantize kernels and
+//               praxis_b200_replicate_scales); one tcgen05.cp 128x256b moves
+//               two replicated atoms (6 copies per k-tile, ~5x less copy time
+//               for the same tensor-memory contents).
 // ---------------------------------------------------------------------------
+template <bool REP>
 struct PairShape {
   static constexpr int BN = 256;
   static constexpr int BK_BYTES = 128;
-  static constexpr int STAGES = 4;
+  static constexpr int STAGES = REP ? 3 : 4;
   static constexpr int A_BYTES = 128 * BK_BYTES;
   static constexpr int B_BYTES = 128 * BK_BYTES;
-  static constexpr int SFA_BYTES = 4 * 512;
-  static constexpr int SFB_BYTES = 2 * 4 * 512;
+  static constexpr int SF_COPIES = REP ? 4 : 1;
+  static constexpr int SFA_BYTES = 4 * 512 * SF_COPIES;      // 4 k-blocks
+  static constexpr int SFB_BYTES = 2 * 4 * 512 * SF_COPIES;  // 2 row-tiles x 4 k-blocks
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
   static constexpr int ACC_ALT_COL = 192;  // start of every other accumulator
   static constexpr int OVERLAP = 64;       // columns shared by consecutive accumulators
@@ -307,11 +319,12 @@ struct PairShape {
   static constexpr int TMEM_COLS = 512;
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  // Output staging per epilogue warp: 32 rows x up to 128 bf16 columns as two
-  // 32 x 64 boxes of 4 KB in the TMA 128-byte swizzle.
-  static constexpr int OUT_STAGE_BYTES = 2 * 4096;
+  // Output staging per epilogue warp: one 32 x 64 bf16 box (4 KB) in the TMA
+  // 128-byte swizzle.
+  static constexpr int OUT_STAGE_BYTES = 4096;
   static constexpr size_t SMEM_BYTES =
       1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EPI_WARPS * OUT_STAGE_BYTES + 256;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 // Writes 8 bf16 (16 bytes) of row `row` (0..31), 16-byte chunk `chunk` (0..7)
@@ -320,10 +333,10 @@ __device__ __forceinline__ void stage_chunk(uint8_t* box, int row, int chunk, ui
   *reinterpret_cast<uint4*>(box + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
 }
 
-template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 1)
+template <int EPI, bool REP>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THREADS, 1)
     gemm_nvfp4_pair_kernel(const __grid_constant__ GemmParams p) {
-  using S = PairShape;
+  using S = PairShape<REP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -386,9 +399,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
         const TileEntry t = pairs[m];
         const int a_row = t.row0 + 128 * (int)rank;
         const int b_row = t.expert * p.N + n * S::BN + 128 * (int)rank;
-        // scale atoms as 256-byte rows: 8 rows per k-tile of a 128-row tile
-        const int sfa_row = ((t.row0 / 128 + (int)rank) * kb_total) * 2;
-        const int sfb_row0 = ((t.expert * (p.N / 128) + n * 2) * kb_total) * 2;
+        // scale atoms as 256-byte rows (2 per 512-byte atom)
+        const int sfa_row = ((t.row0 / 128 + (int)rank) * kb_total) * 2 * S::SF_COPIES;
+        const int sfb_row0 =
+            REP ? ((t.expert * (p.N / 256) + n) * kb_total) * 16 : ((t.expert * (p.N / 128) + n * 2) * kb_total) * 2;
         const int sfb_row1 = sfb_row0 + kb_total * 2;
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) {
@@ -399,9 +413,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
           tma_load_2d_pair(sA + stage * S::A_BYTES, &p.tmap_a, fb, kt * S::BK_BYTES, a_row);
           tma_load_2d_pair(sB + stage * S::B_BYTES, &p.tmap_b, fb, kt * S::BK_BYTES, b_row);
-          tma_load_2d_pair(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, fb, 0, sfa_row + kt * 8);
-          tma_load_2d_pair(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, fb, 0, sfb_row0 + kt * 8);
-          tma_load_2d_pair(sSFB + stage * S::SFB_BYTES + 2048, &p.tmap_sfb, fb, 0, sfb_row1 + kt * 8);
+          if constexpr (REP) {
+            // [k-block][4 copies][512 B] for A; [k-block][row-tile][4 copies][512 B] for B
+            tma_load_2d_pair(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, fb, 0, sfa_row + kt * 32);
+            tma_load_2d_pair(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, fb, 0, sfb_row0 + kt * 64);
+          } else {
+            tma_load_2d_pair(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, fb, 0, sfa_row + kt * 8);
+            tma_load_2d_pair(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, fb, 0, sfb_row0 + kt * 8);
+            tma_load_2d_pair(sSFB + stage * S::SFB_BYTES + 2048, &p.tmap_sfb, fb, 0, sfb_row1 + kt * 8);
+          }
           if (++stage == S::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -432,11 +452,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
           const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
           const uint32_t sfa_s = smem_u32(sSFA + stage * S::SFA_BYTES);
           const uint32_t sfb_s = smem_u32(sSFB + stage * S::SFB_BYTES);
-          for (int kb = 0; kb < kb_n; ++kb) {
-            tc_cp_32x128b_warpx4_pair(sfa_t + kb * 4, smem_desc(sfa_s + kb * 512, 0, 128, kLayoutSwizzleNone));
-            tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8, smem_desc(sfb_s + kb * 512, 0, 128, kLayoutSwizzleNone));
-            tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8 + 4,
-                                      smem_desc(sfb_s + 2048 + kb * 512, 0, 128, kLayoutSwizzleNone));
+          if constexpr (REP) {
+            // 128 lanes x 32 bytes per copy: lane l reads line l of two
+            // replicated atoms (the two 16-byte halves are 2 KB apart).
+            for (int j = 0; j < (kb_n + 1) / 2; ++j)
+              tc_cp_128x256b_pair(sfa_t + 8 * j, smem_desc(sfa_s + j * 4096, 2048, 128, kLayoutSwizzleNone));
+            for (int kb = 0; kb < kb_n; ++kb)
+              tc_cp_128x256b_pair(sfb_t + 8 * kb, smem_desc(sfb_s + kb * 4096, 2048, 128, kLayoutSwizzleNone));
+          } else {
+            for (int kb = 0; kb < kb_n; ++kb) {
+              tc_cp_32x128b_warpx4_pair(sfa_t + kb * 4, smem_desc(sfa_s + kb * 512, 0, 128, kLayoutSwizzleNone));
+              tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8, smem_desc(sfb_s + kb * 512, 0, 128, kLayoutSwizzleNone));
+              tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8 + 4,
+                                        smem_desc(sfb_s + 2048 + kb * 512, 0, 128, kLayoutSwizzleNone));
+            }
           }
           for (int kb = 0; kb < kb_n; ++kb) {
             const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
@@ -516,7 +545,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
             stage_chunk(stg, (int)lane, 4 * bl + c, make_uint4(w[0], w[1], w[2], w[3]));
           }
         } else {
-          uint8_t* box = stg + bl * 4096;
+          // one 32 x 64 box per block: reuse the staging box once the
+          // previous block's store has read it
+          if (i == 1) {
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint32_t* r = c < 4 ? r0 : r1;
@@ -531,21 +565,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape::THREADS, 
               }
               w[j] = pack_bf16x2_alu(v0, v1);
             }
-            stage_chunk(box, (int)lane, c, make_uint4(w[0], w[1], w[2], w[3]));
+            stage_chunk(stg, (int)lane, c, make_uint4(w[0], w[1], w[2], w[3]));
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0 && live) {
+            tma_store_2d(&p.tmap_out, stg, n * S::BN + 64 * blk, t.row0 + 128 * (int)rank + (int)quad * 32);
+            bulk_commit_group();
           }
         }
       }
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0 && live) {
-        const int row = t.row0 + 128 * (int)rank + (int)quad * 32;
-        if constexpr (EPI == EPI_SWIGLU) {
-          tma_store_2d(&p.tmap_out, stg, n * (S::BN / 2) + 64 * half, row);
-        } else {
-          tma_store_2d(&p.tmap_out, stg, n * S::BN + 128 * half, row);
-          tma_store_2d(&p.tmap_out, stg + 4096, n * S::BN + 128 * half + 64, row);
+      if constexpr (EPI == EPI_SWIGLU) {
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0 && live) {
+          tma_store_2d(&p.tmap_out, stg, n * (S::BN / 2) + 64 * half, t.row0 + 128 * (int)rank + (int)quad * 32);
+          bulk_commit_group();
         }
-        bulk_commit_group();
       }
       if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll
@@ -618,15 +654,15 @@ static int launch_gemm(const GemmParams& p, int max_tiles, cudaStream_t stream) 
   return check_launch("gemm_nvfp4");
 }
 
-// Scale-factor atoms viewed as rows of 256 bytes (8 rows = the 4 atoms of
-// one k-tile of a 128-row tile), box {256 B, 8 rows}, no swizzle.
-static int make_bytes_map(CUtensorMap* map, const void* base, size_t bytes) {
+// Scale-factor atoms viewed as rows of 256 bytes, box {256 B, box_rows},
+// no swizzle (8 rows = the 4 compact atoms of one k-tile of a 128-row tile).
+static int make_bytes_map(CUtensorMap* map, const void* base, size_t bytes, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled is unavailable");
   if (bytes % 256 != 0 || bytes == 0) return set_error(PRAXIS_B200_EINVAL, "scale buffer size %zu", bytes);
   cuuint64_t gdim[2] = {256u, (cuuint64_t)(bytes / 256)};
   cuuint64_t gstride[1] = {256u};
-  cuuint32_t box[2] = {256u, 8u};
+  cuuint32_t box[2] = {256u, (cuuint32_t)box_rows};
   cuuint32_t estride[2] = {1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -651,17 +687,17 @@ static int make_out_map(CUtensorMap* map, const void* base, int64_t rows, int64_
   return PRAXIS_B200_OK;
 }
 
-// 0: CTA-pair kernel where N % 256 == 0 (default); 1: the 1-CTA kernel
-// (PRAXIS_B200_GEMM=single).
+// Compact scale layout: 0 = CTA-pair kernel where N % 256 == 0 (default),
+// 1 = the 1-CTA kernel (PRAXIS_B200_GEMM=single).
 static int gemm_variant() {
   const char* s = getenv("PRAXIS_B200_GEMM");
   return (s != nullptr && strcmp(s, "single") == 0) ? 1 : 0;
 }
 
-template <int EPI>
+template <int EPI, bool REP>
 static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t stream) {
-  using S = PairShape;
-  auto kernel = gemm_nvfp4_pair_kernel<EPI>;
+  using S = PairShape<REP>;
+  auto kernel = gemm_nvfp4_pair_kernel<EPI, REP>;
   static int max_clusters[8] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -692,10 +728,23 @@ static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t str
   return check_launch("gemm_nvfp4_pair");
 }
 
+template <bool REP>
+static int launch_pair_epi(const GemmParams& p, int epilogue, int max_tiles, cudaStream_t stream) {
+  switch (epilogue) {
+    case EPI_SWIGLU:
+      return launch_gemm_pair<EPI_SWIGLU, REP>(p, max_tiles, stream);
+    case EPI_RESCALE:
+      return launch_gemm_pair<EPI_RESCALE, REP>(p, max_tiles, stream);
+    default:
+      return launch_gemm_pair<EPI_PLAIN, REP>(p, max_tiles, stream);
+  }
+}
+
 int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, const TileEntry* tiles,
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
-                     const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, cudaStream_t stream) {
+                     const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
+                     cudaStream_t stream) {
   if (n % 128 != 0 || k % 128 != 0 || n <= 0 || k <= 0)
     return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs N and K multiples of 128 (N=%d K=%d)", n, k);
   if (max_tiles < 0 || rows_padded < (int64_t)max_tiles * 128)
@@ -708,6 +757,10 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
     return set_error(PRAXIS_B200_EINVAL, "rescale epilogue needs global scales");
   if (epilogue != EPI_PLAIN && epilogue != EPI_SWIGLU && epilogue != EPI_RESCALE)
     return set_error(PRAXIS_B200_EINVAL, "unknown epilogue %d", epilogue);
+  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
+    return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
+  if (sf_layout == PRAXIS_B200_SF_REPLICATED && n % 256 != 0)
+    return set_error(PRAXIS_B200_EINVAL, "the replicated scale layout needs N %% 256 == 0");
   if (((uintptr_t)a_sf | (uintptr_t)b_sf | (uintptr_t)out) & 15)
     return set_error(PRAXIS_B200_EINVAL, "scale and output buffers must be 16-byte aligned");
   if (rows_padded == 0 || max_tiles == 0) return PRAXIS_B200_OK;
@@ -730,21 +783,17 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.w_global = w_global;
   p.amax_out = amax_out;
   p.max_tiles = max_tiles;
-  if (n % PairShape::BN == 0 && gemm_variant() == 0) {
-    rc = make_bytes_map(&p.tmap_sfa, a_sf, (size_t)rows_padded * (k / 16));
+  const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
+  if (n % 256 == 0 && (rep || gemm_variant() == 0)) {
+    const size_t copies = rep ? 4 : 1;
+    rc = make_bytes_map(&p.tmap_sfa, a_sf, (size_t)rows_padded * (k / 16) * copies, rep ? 32 : 8);
     if (rc) return rc;
-    rc = make_bytes_map(&p.tmap_sfb, b_sf, (size_t)experts * n * (k / 16));
+    rc = make_bytes_map(&p.tmap_sfb, b_sf, (size_t)experts * n * (k / 16) * copies, rep ? 64 : 8);
     if (rc) return rc;
     rc = make_out_map(&p.tmap_out, out, rows_padded, out_cols);
     if (rc) return rc;
-    switch (epilogue) {
-      case EPI_SWIGLU:
-        return launch_gemm_pair<EPI_SWIGLU>(p, max_tiles, stream);
-      case EPI_RESCALE:
-        return launch_gemm_pair<EPI_RESCALE>(p, max_tiles, stream);
-      default:
-        return launch_gemm_pair<EPI_PLAIN>(p, max_tiles, stream);
-    }
+    return rep ? launch_pair_epi<true>(p, epilogue, max_tiles, stream)
+               : launch_pair_epi<false>(p, epilogue, max_tiles, stream);
   }
   switch (epilogue) {
     case EPI_SWIGLU:

@@ -58,6 +58,7 @@ __host__ __device__ __forceinline__ float global_from_amax_bits(uint32_t bits) {
 int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, const TileEntry* tiles,
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
-                     const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, cudaStream_t stream);
+                     const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
+                     cudaStream_t stream);
 
 }  // namespace praxis

@@ -30,6 +30,16 @@ __device__ __forceinline__ uint32_t sf_offset(int64_t row, int col, int kb) {
                     (col & 3));
 }
 
+// Replicated layout (PRAXIS_B200_SF_REPLICATED): the atom of (row group,
+// k-block) is stored four times in a row; a group is 128 rows (activations)
+// or 256 rows = two atoms (weights, [group][k-block][half][copy][512 B]).
+__device__ __forceinline__ uint32_t sf_offset_rep(int64_t row, int col, int kb, int group_rows, int copy) {
+  const int64_t g = group_rows == 256 ? row >> 8 : row >> 7;
+  const int half = group_rows == 256 ? (int)((row >> 7) & 1) : 0;
+  return (uint32_t)((g * (kb >> 2) + (col >> 2)) * (group_rows * 16) + half * 2048 + copy * 512 + (row & 31) * 16 +
+                    ((row & 127) >> 5) * 4 + (col & 3));
+}
+
 __device__ __forceinline__ float clamp6(float x) { return fminf(fmaxf(x, -6.0f), 6.0f); }
 
 // Quantize 16 values with global g (inv_g = div_rn(1, g)); returns the 8
@@ -63,16 +73,21 @@ __device__ __forceinline__ void load16_bf16(const uint16_t* src, float (&v)[16],
   }
 }
 
-// Gather the four scale bytes of lanes 4i..4i+3 into lane 4i and store them
-// as one word (the 4 scales of a 64-element group are adjacent in the atom).
+// Gather the four scale bytes of lanes 4i..4i+3 into one word (the 4 scales
+// of a 64-element group are adjacent in the atom) and store it: lane 4i in
+// the compact layout; lane 4i+c writes copy c in the replicated one.
 __device__ __forceinline__ void store_sf_group(uint8_t* sf_base, int64_t row, int col, int kb, uint32_t byte,
-                                               bool active) {
+                                               bool active, bool rep) {
   const uint32_t lane = threadIdx.x & 31;
   uint32_t b1 = __shfl_down_sync(0xffffffffu, byte, 1);
   uint32_t b2 = __shfl_down_sync(0xffffffffu, byte, 2);
   uint32_t b3 = __shfl_down_sync(0xffffffffu, byte, 3);
-  if (active && (lane & 3) == 0) {
-    const uint32_t word = byte | (b1 << 8) | (b2 << 16) | (b3 << 24);
+  uint32_t word = byte | (b1 << 8) | (b2 << 16) | (b3 << 24);
+  if (rep) {
+    word = __shfl_sync(0xffffffffu, word, lane & ~3u);
+    if (active)
+      *reinterpret_cast<uint32_t*>(sf_base + sf_offset_rep(row, col & ~3, kb, 128, (int)(lane & 3))) = word;
+  } else if (active && (lane & 3) == 0) {
     *reinterpret_cast<uint32_t*>(sf_base + sf_offset(row, col, kb)) = word;
   }
 }
@@ -89,7 +104,7 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
     const int64_t* __restrict__ inverse, const int32_t* __restrict__ csr, const int32_t* __restrict__ pcsr,
     const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int top_k, int experts,
     const TileEntry* __restrict__ tiles, const int32_t* __restrict__ num_tiles, int token_blocks,
-    uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+    uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
   __shared__ int64_t s_dest[8][8];
   __shared__ float s_g[8][8], s_ig[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -104,8 +119,14 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
       const int64_t row = (int64_t)t.row0 + r;
       uint4* qr = reinterpret_cast<uint4*>(q + row * (k_dim / 2));
       for (int i = lane; i < k_dim / 32; i += 32) qr[i] = make_uint4(0, 0, 0, 0);
-      for (int g4 = lane; g4 < kb / 4; g4 += 32)
-        *reinterpret_cast<uint32_t*>(sf + sf_offset(row, g4 * 4, kb)) = 0u;
+      for (int g4 = lane; g4 < kb / 4; g4 += 32) {
+        if (rep) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) *reinterpret_cast<uint32_t*>(sf + sf_offset_rep(row, g4 * 4, kb, 128, c)) = 0u;
+        } else {
+          *reinterpret_cast<uint32_t*>(sf + sf_offset(row, g4 * 4, kb)) = 0u;
+        }
+      }
     }
     return;
   }
@@ -138,7 +159,7 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
         quantize16(v, amax, s_g[warp][s], s_ig[warp][s], lo, hi, sfb);
         *reinterpret_cast<uint2*>(q + dest * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
       }
-      store_sf_group(sf, dest, j, kb, sfb, active);
+      store_sf_group(sf, dest, j, kb, sfb, active, rep);
     }
   }
 }
@@ -149,7 +170,7 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
 __global__ void __launch_bounds__(256) quantize_rows_kernel(
     const uint16_t* __restrict__ x, int k_dim, const TileEntry* __restrict__ tiles,
     const int32_t* __restrict__ num_tiles, const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits,
-    uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+    uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * 8 + warp;  // tile * 128 + row
   const int m = (int)(item / kTileRows);
@@ -171,7 +192,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
       quantize16(v, amax, g, ig, lo, hi, sfb);
       *reinterpret_cast<uint2*>(q + row * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
     }
-    store_sf_group(sf, row, j, kb, sfb, active);
+    store_sf_group(sf, row, j, kb, sfb, active, rep);
   }
 }
 
@@ -234,30 +255,56 @@ __global__ void interleave_gate_up_kernel(const uint8_t* __restrict__ q, const u
 }
 
 // ---------------------------------------------------------------------------
+// Compact -> replicated scales: one thread per 16-byte chunk (one row of 32
+// within the atom: 4 quadrants x 4 scales), written to the four copies.
+// ---------------------------------------------------------------------------
+__global__ void replicate_scales_kernel(const uint4* __restrict__ sf, int64_t chunks, int kb, int group_rows,
+                                        uint4* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= chunks) return;
+  const int64_t atom = i >> 5;
+  const int r32 = (int)(i & 31);
+  const int kblocks = kb >> 2;
+  const int64_t tile = atom / kblocks;  // 128-row tile
+  const int col = (int)(atom % kblocks) * 4;
+  const uint4 v = ldg_stream(sf + i);
+  const int64_t row = tile * 128 + r32;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) out[sf_offset_rep(row, col, kb, group_rows, c) >> 4] = v;
+}
+
+// ---------------------------------------------------------------------------
 // Host entries
 // ---------------------------------------------------------------------------
 int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int64_t* top_idx, const int64_t* inverse,
                         const int32_t* csr, const int32_t* pcsr, const float* globals, const uint32_t* amax_bits,
                         int top_k, int experts, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
-                        uint8_t* q, uint8_t* sf, cudaStream_t stream) {
+                        uint8_t* q, uint8_t* sf, int sf_layout, cudaStream_t stream) {
   if (k_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "quantize needs K % 64 == 0");
   if (top_k < 1 || top_k > 8) return set_error(PRAXIS_B200_EINVAL, "top_k must be 1..8");
   if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
+  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
+    return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
   const int token_blocks = (int)((tokens + 7) / 8);
   const int grid = token_blocks + max_tiles;
   if (grid == 0) return PRAXIS_B200_OK;
   quantize_gather_kernel<<<grid, 256, 0, stream>>>(x, tokens, k_dim, top_idx, inverse, csr, pcsr, globals, amax_bits,
-                                                   top_k, experts, tiles, num_tiles, token_blocks, q, sf);
+                                                   top_k, experts, tiles, num_tiles, token_blocks, q, sf,
+                                                   sf_layout == PRAXIS_B200_SF_REPLICATED);
   return check_launch("quantize_gather");
 }
 
 int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
-                      const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, cudaStream_t stream) {
+                      const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, int sf_layout,
+                      cudaStream_t stream) {
   if (k_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "quantize needs K % 64 == 0");
   if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
+  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
+    return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
   const int64_t blocks = (int64_t)max_tiles * kTileRows / 8;
   if (blocks == 0) return PRAXIS_B200_OK;
-  quantize_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, k_dim, tiles, num_tiles, globals, amax_bits, q, sf);
+  quantize_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, k_dim, tiles, num_tiles, globals, amax_bits, q, sf,
+                                                             sf_layout == PRAXIS_B200_SF_REPLICATED);
   return check_launch("quantize_rows");
 }
 
@@ -284,6 +331,20 @@ int run_interleave_gate_up(const uint8_t* q, const uint8_t* sf, int experts, int
   dim3 grid((unsigned)(2 * f_dim), (unsigned)experts);
   interleave_gate_up_kernel<<<grid, 128, 0, stream>>>(q, sf, f_dim, c_dim, q_out, sf_out);
   return check_launch("interleave_gate_up");
+}
+
+int run_replicate_scales(const uint8_t* sf, int64_t rows, int k_dim, int group_rows, uint8_t* out,
+                         cudaStream_t stream) {
+  if (k_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "replicate_scales needs K % 64 == 0");
+  if (group_rows != 128 && group_rows != 256) return set_error(PRAXIS_B200_EINVAL, "group_rows must be 128 or 256");
+  if (rows < 0 || rows % group_rows != 0)
+    return set_error(PRAXIS_B200_EINVAL, "replicate_scales: rows (%lld) must be a multiple of %d", (long long)rows,
+                     group_rows);
+  const int64_t chunks = rows * (k_dim / 16) / 16;
+  if (chunks == 0) return PRAXIS_B200_OK;
+  replicate_scales_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const uint4*>(sf), chunks, k_dim / 16, group_rows, reinterpret_cast<uint4*>(out));
+  return check_launch("replicate_scales");
 }
 
 }  // namespace praxis

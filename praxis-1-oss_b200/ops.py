@@ -171,42 +171,57 @@ def route_dispatch(logits: Tensor, bias: Tensor, rows: tuple, top_k: int = 8,
     return dispatch(top_idx, gate, logits.shape[1])
 
 
-def quantize_gather(x: Tensor, routing: Routing, act_global: Tensor) -> tuple[Tensor, Tensor]:
+def _sf_buffer(rows: int, kdim: int, sf_layout: int, device) -> Tensor:
+    """Scale buffer: [rows, K/16] compact, or the flat replicated layout."""
+    if sf_layout == capi.SF_COMPACT:
+        return torch.empty(rows, kdim // 16, dtype=torch.uint8, device=device)
+    if sf_layout == capi.SF_REPLICATED:
+        return torch.empty(4 * rows * (kdim // 16), dtype=torch.uint8, device=device)
+    raise ValueError(f"unknown scale layout {sf_layout}")
+
+
+def quantize_gather(x: Tensor, routing: Routing, act_global: Tensor, *,
+                    sf_layout: int = capi.SF_COMPACT) -> tuple[Tensor, Tensor]:
     """``quantize_activations(x, csr, row_indices=tokens, alignment=128,
     grouped_scales=False)`` (praxis/kernels/nvfp4.py:197-254) into the
-    padded layout; padding rows of partly filled tiles are zero."""
+    padded layout; padding rows of partly filled tiles are zero. With
+    ``sf_layout=SF_REPLICATED`` the scales come in the GEMM's replicated
+    layout (flat, 4x the compact size)."""
     _need(x, "x", BF16, 2)
     t, c = x.shape
     k = routing.top_idx.shape[1]
     e = routing.csr.numel() - 1
     rp = padded_rows(t * k, e)
     q = torch.empty(rp, c // 2, dtype=torch.uint8, device=x.device)
-    sf = torch.empty(rp, c // 16, dtype=torch.uint8, device=x.device)
+    sf = _sf_buffer(rp, c, sf_layout, x.device)
     capi.check(capi.load().praxis_b200_quantize_gather(
         _p(x), t, c, _p(routing.top_idx), _p(routing.inverse), _p(routing.csr), _p(routing.pcsr), _p(act_global),
-        None, k, e, _p(routing.tiles), _p(routing.num_tiles), rp // 128, _p(q), _p(sf), _dev(x), _stream(x)))
+        None, k, e, _p(routing.tiles), _p(routing.num_tiles), rp // 128, _p(q), _p(sf), sf_layout, _dev(x),
+        _stream(x)))
     return q, sf
 
 
 def quantize_rows(x: Tensor, routing: Routing, globals_: Tensor | None = None,
-                  amax_bits: Tensor | None = None) -> tuple[Tensor, Tensor]:
+                  amax_bits: Tensor | None = None, *, sf_layout: int = capi.SF_COMPACT) -> tuple[Tensor, Tensor]:
     """Quantize every row of the routed tiles of a padded [Rp, K] tensor."""
     _need(x, "x", BF16, 2)
     rp, kdim = x.shape
     q = torch.empty(rp, kdim // 2, dtype=torch.uint8, device=x.device)
-    sf = torch.empty(rp, kdim // 16, dtype=torch.uint8, device=x.device)
+    sf = _sf_buffer(rp, kdim, sf_layout, x.device)
     capi.check(capi.load().praxis_b200_quantize_rows(
         _p(x), kdim, _p(routing.tiles), _p(routing.num_tiles), rp // 128, _p(globals_), _p(amax_bits), _p(q),
-        _p(sf), _dev(x), _stream(x)))
+        _p(sf), sf_layout, _dev(x), _stream(x)))
     return q, sf
 
 
 def grouped_gemm(a_q: Tensor, a_sf: Tensor, b_q: Tensor, b_sf: Tensor, routing: Routing, *,
                  epilogue: int = capi.EPI_PLAIN, act_global: Tensor | None = None,
                  act_amax: Tensor | None = None, w_global: Tensor | None = None,
-                 amax_out: Tensor | None = None) -> Tensor:
+                 amax_out: Tensor | None = None, sf_layout: int = capi.SF_COMPACT) -> Tensor:
     """``grouped_nvfp4_mm`` (praxis/kernels/nvfp4.py:355-419) on tcgen05 with
-    an optional fused epilogue (see include/praxis_b200_moe.h)."""
+    an optional fused epilogue (see include/praxis_b200_moe.h). With
+    ``sf_layout=SF_REPLICATED`` a_sf is replicated in 128-row groups and b_sf
+    in 256-row groups (:func:`replicate_scales`)."""
     rp = a_q.shape[0]
     kdim = a_q.shape[1] * 2
     e, n = b_q.shape[0], b_q.shape[1]
@@ -216,7 +231,21 @@ def grouped_gemm(a_q: Tensor, a_sf: Tensor, b_q: Tensor, b_sf: Tensor, routing: 
     out = torch.empty(rp, cols, dtype=BF16, device=a_q.device)
     capi.check(capi.load().praxis_b200_grouped_gemm(
         _p(a_q), _p(a_sf), _p(b_q), _p(b_sf), _p(routing.tiles), _p(routing.num_tiles), rp // 128, rp, n, kdim, e,
-        epilogue, _p(out), _p(act_global), _p(act_amax), _p(w_global), _p(amax_out), _dev(a_q), _stream(a_q)))
+        epilogue, _p(out), _p(act_global), _p(act_amax), _p(w_global), _p(amax_out), sf_layout, _dev(a_q),
+        _stream(a_q)))
+    return out
+
+
+def replicate_scales(sf: Tensor, group_rows: int) -> Tensor:
+    """Compact swizzled scales [..., rows, K/16] -> the GEMM's replicated
+    layout (flat uint8, 4x the size); ``group_rows`` 128 for activation
+    rows, 256 for weight rows (all experts' rows taken as one stack)."""
+    _need(sf, "sf", torch.uint8)
+    kdim = sf.shape[-1] * 16
+    rows = sf.numel() // sf.shape[-1]
+    out = torch.empty(4 * sf.numel(), dtype=torch.uint8, device=sf.device)
+    capi.check(capi.load().praxis_b200_replicate_scales(
+        _p(sf), rows, kdim, group_rows, _p(out), _dev(sf), _stream(sf)))
     return out
 
 
@@ -281,10 +310,11 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
                 gate_up_global: Tensor, down_q: Tensor, down_sf: Tensor, down_global: Tensor, scaling: float,
                 shared: Tensor | None = None, *, router_terms: Tensor | None = None,
                 router_bias: Tensor | None = None, top_k: int | None = None, activation: str = "sigmoid",
-                out: Tensor | None = None):
+                out: Tensor | None = None, weight_sf_layout: int | None = None):
     """One dispatch chunk through ``praxis_b200_moe_forward``. With
     ``router_terms`` the router runs too and (out, top_idx, gate) is returned.
-    ``gate_up_q/sf`` are in the interleaved kernel layout."""
+    ``gate_up_q/sf`` are in the interleaved kernel layout; the weight scales
+    are compact or replicated (``weight_sf_layout``, else told by size)."""
     _need(x, "x", BF16, 2)
     t, c = x.shape
     e, c_half_f, _ = down_q.shape
@@ -298,6 +328,13 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         k = top_idx.shape[1]
     if out is None:
         out = torch.empty_like(x)
+    if weight_sf_layout is None:
+        if down_sf.numel() * 8 == down_q.numel():
+            weight_sf_layout = capi.SF_COMPACT
+        elif down_sf.numel() * 2 == down_q.numel():
+            weight_sf_layout = capi.SF_REPLICATED
+        else:
+            raise ValueError("down_sf size matches neither scale layout")
     lib = capi.load()
     ws_size = int(lib.praxis_b200_moe_workspace_size(t, k, e, c, f, int(router_terms is not None)))
     ws = torch.empty(ws_size, dtype=torch.uint8, device=dev)
@@ -310,7 +347,7 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         shared=None if shared is None else shared.data_ptr(), out=out.data_ptr(),
         gate_up_q=gate_up_q.data_ptr(), gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(),
         down_q=down_q.data_ptr(), down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(),
-        tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
+        weight_sf_layout=int(weight_sf_layout), tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
         workspace=ws.data_ptr(), workspace_size=ws_size, device=_dev(x),
         stream=torch.cuda.current_stream(dev).cuda_stream,
     )

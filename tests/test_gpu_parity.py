@@ -55,6 +55,15 @@ def make_bank(e, c, f, seed):
     return gu, down
 
 
+def replicated(sf: torch.Tensor, rows: int, kb: int, group_rows: int) -> torch.Tensor:
+    """The GEMM's replicated scale layout from compact swizzled scales, as
+    [groups, k-blocks, halves, copies, 512] (halves = group_rows / 128)."""
+    atoms = sf.reshape(rows // 128, kb // 4, 512)  # compact: [tile][k-block][atom]
+    halves = group_rows // 128
+    a = atoms.reshape(rows // group_rows, halves, kb // 4, 512).permute(0, 2, 1, 3)
+    return a.unsqueeze(3).expand(-1, -1, -1, 4, -1).contiguous()
+
+
 def ulp_mismatch(a: torch.Tensor, b: torch.Tensor):
     a = a.detach().cpu().view(torch.int16).int()
     b = b.detach().cpu().view(torch.int16).int()
@@ -171,7 +180,8 @@ def test_dispatch_bit_exact(P, t, e, k, mode):
 # Quantization and packing
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("t,c,e,k", [(256, 512, 8, 2), (300, 3072, 16, 8), (50, 256, 8, 2)])
-def test_quantize_gather_bit_exact(P, t, c, e, k):
+@pytest.mark.parametrize("layout", ["compact", "replicated"])
+def test_quantize_gather_bit_exact(P, t, c, e, k, layout):
     top, gate = random_routing(t, e, k, seed=c)
     g = gen(c + 1)
     x = (torch.randn(t, c, generator=g) * 1.5).to(torch.bfloat16)
@@ -180,7 +190,8 @@ def test_quantize_gather_bit_exact(P, t, c, e, k):
     xd = x.to(DEV)
     amax = P.ops.row_amax(xd)
     r = P.ops.dispatch(top.to(DEV), gate.to(DEV), e, amax)
-    q, sf = P.ops.quantize_gather(xd, r, r.act_global)
+    sf_layout = P.capi.SF_REPLICATED if layout == "replicated" else P.capi.SF_COMPACT
+    q, sf = P.ops.quantize_gather(xd, r, r.act_global, sf_layout=sf_layout)
     _, _, tokens, _, offsets, csr = O.dispatch(top, gate, e)
     pcsr = O.pad_csr(csr)
     rp = O.padded_rows(t * k, e)
@@ -195,9 +206,21 @@ def test_quantize_gather_bit_exact(P, t, c, e, k):
     rows = torch.tensor(rows, dtype=torch.int64)
     assert_bytes_equal(q.cpu()[rows], oq[rows])
     kb = c // 16
+    if layout == "replicated":
+        live = torch.unique(rows // 128)
+        got = sf.cpu().view(rp // 128, kb // 4, 1, 4, 512)[live]
+        assert_bytes_equal(got, replicated(osf, rp, kb, 128)[live])
+        return
     got = O.unswizzle_scales(sf.cpu(), rp, kb)[rows]
     want = O.unswizzle_scales(osf, rp, kb)[rows]
     assert_bytes_equal(got, want)
+
+
+@pytest.mark.parametrize("rows,kdim,group", [(128, 256, 128), (768, 512, 128), (512, 3072, 256), (256, 64, 256)])
+def test_replicate_scales_layout(P, rows, kdim, group):
+    sf = torch.randint(0, 127, (rows, kdim // 16), dtype=torch.uint8, generator=gen(rows + kdim))
+    got = P.ops.replicate_scales(sf.to(DEV), group)
+    assert_bytes_equal(got.cpu().view(-1), replicated(sf, rows, kdim // 16, group).view(-1))
 
 
 @pytest.mark.parametrize("e,kdim,n", [(2, 256, 128), (4, 512, 256), (3, 3072, 384)])
@@ -288,11 +311,20 @@ def _gemm_case(P, t, e, k, c, f, seed, mode="plain"):
     return top, gate, x, bank, r, aq, asf
 
 
-@pytest.fixture(params=["pair", "single"])
+@pytest.fixture(params=["pair_replicated", "pair", "single"])
 def gemm_variant(request, monkeypatch):
-    """The CTA-pair (M=256, N=256) and the 1-CTA (M=128, N=128) kernels."""
-    monkeypatch.setenv("PRAXIS_B200_GEMM", request.param)
+    """The CTA-pair (M=256, N=256) kernel with replicated or compact scales
+    and the 1-CTA (M=128, N=128) kernel."""
+    monkeypatch.setenv("PRAXIS_B200_GEMM", "single" if request.param == "single" else "pair")
     return request.param
+
+
+def gemm_scales(P, variant, asf, bsf):
+    """(a_sf, b_sf, sf_layout) for the variant: replicated copies of the
+    compact scales for "pair_replicated"."""
+    if variant != "pair_replicated":
+        return asf, bsf, P.capi.SF_COMPACT
+    return P.ops.replicate_scales(asf, 128), P.ops.replicate_scales(bsf, 256), P.capi.SF_REPLICATED
 
 
 @pytest.mark.parametrize("t,e,k,c,f,mode", [
@@ -304,7 +336,8 @@ def test_grouped_gemm_plain_vs_dequantised_oracle(P, gemm_variant, t, e, k, c, f
     bq, bsf = bank["down_q"].to(DEV), bank["down_sf"].to(DEV)  # N = C, K = F
     # use gate_up (N = 2F, K = C) as a plain GEMM
     bq, bsf = bank["gate_up_q"].to(DEV), bank["gate_up_sf"].to(DEV)
-    out = P.ops.grouped_gemm(aq, asf, bq, bsf, r, epilogue=P.capi.EPI_PLAIN)
+    a_sf, b_sf, layout = gemm_scales(P, gemm_variant, asf, bsf)
+    out = P.ops.grouped_gemm(aq, a_sf, bq, b_sf, r, epilogue=P.capi.EPI_PLAIN, sf_layout=layout)
     csr = r.csr.cpu()
     pcsr = r.pcsr.cpu()
     want = O.grouped_gemm(aq.cpu(), asf.cpu(), bank["gate_up_q"], bank["gate_up_sf"], pcsr, c, 2 * f)
@@ -322,8 +355,9 @@ def test_gemm_swiglu_and_rescale_epilogues(P, gemm_variant):
     top, gate, x, bank, r, aq, asf = _gemm_case(P, t, e, k, c, f, seed=17)
     gq, gsf = P.ops.interleave_gate_up(bank["gate_up_q"].to(DEV), bank["gate_up_sf"].to(DEV))
     amax = torch.zeros(e, dtype=torch.int32, device=DEV)
-    hidden = P.ops.grouped_gemm(aq, asf, gq, gsf, r, epilogue=P.capi.EPI_SWIGLU, act_global=r.act_global,
-                                w_global=bank["gate_up_global"].to(DEV), amax_out=amax)
+    a_sf, g_sf, layout = gemm_scales(P, gemm_variant, asf, gsf)
+    hidden = P.ops.grouped_gemm(aq, a_sf, gq, g_sf, r, epilogue=P.capi.EPI_SWIGLU, act_global=r.act_global,
+                                w_global=bank["gate_up_global"].to(DEV), amax_out=amax, sf_layout=layout)
     pcsr, csr = r.pcsr.cpu(), r.csr.cpu()
     gu = O.grouped_gemm(aq.cpu(), asf.cpu(), bank["gate_up_q"], bank["gate_up_sf"], pcsr, c, 2 * f)
     want_h, rowmax = O.rescale_swiglu_maximum(gu, pcsr, r.act_global.cpu(), bank["gate_up_global"])
@@ -340,8 +374,16 @@ def test_gemm_swiglu_and_rescale_epilogues(P, gemm_variant):
         assert amax[ex].view(torch.float32).item() == m
     # rescale epilogue on the down projection
     hq, hsf = P.ops.quantize_rows(hidden, r, amax_bits=amax)
-    rows_out = P.ops.grouped_gemm(hq, hsf, bank["down_q"].to(DEV), bank["down_sf"].to(DEV), r,
-                                  epilogue=P.capi.EPI_RESCALE, act_amax=amax, w_global=bank["down_global"].to(DEV))
+    h_sf, d_sf, layout = gemm_scales(P, gemm_variant, hsf, bank["down_sf"].to(DEV))
+    if layout == P.capi.SF_REPLICATED:
+        # the row quantizer's own replicated output must match
+        _, h_sf2 = P.ops.quantize_rows(hidden, r, amax_bits=amax, sf_layout=layout)
+        live = torch.unique(torch.cat([torch.arange(int(pcsr[ex]), int(pcsr[ex]) + counts[ex]) for ex in range(e)])
+                            // 128)
+        rp = hidden.shape[0]
+        assert_bytes_equal(h_sf2.cpu().view(rp // 128, -1)[live], h_sf.cpu().view(rp // 128, -1)[live])
+    rows_out = P.ops.grouped_gemm(hq, h_sf, bank["down_q"].to(DEV), d_sf, r, epilogue=P.capi.EPI_RESCALE,
+                                  act_amax=amax, w_global=bank["down_global"].to(DEV), sf_layout=layout)
     hg = O.global_scale_from_amax(amax.cpu().view(torch.float32).to(torch.bfloat16))
     raw = O.grouped_gemm(hq.cpu(), hsf.cpu(), bank["down_q"], bank["down_sf"], pcsr, f, c)
     expert = O.expert_of_rows(pcsr, torch.arange(raw.shape[0]))
@@ -360,6 +402,7 @@ def test_gemm_swiglu_and_rescale_epilogues(P, gemm_variant):
     (64, 256, 32, 2, 512, 64, True),
     (130, 256, 64, 4, 256, 130, False),
     (1, 256, 8, 1, 128, 1, True),
+    (96, 384, 8, 2, 256, 96, False),        # C % 256 != 0: compact weight scales
 ])
 def test_bank_forward_matches_oracle(P, t, c, e, k, f, chunk, shared):
     top, gate = random_routing(t, e, k, seed=t * k + e)

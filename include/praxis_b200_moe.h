@@ -248,6 +248,37 @@ size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t exp
                                       int32_t with_router);
 int praxis_b200_moe_forward(const praxis_b200_moe_args* args);
 
+/* Dispatch without a caller workspace: praxis_b200_dispatch with the same
+ * arguments (minus workspace / workspace_size) and the same outputs, its
+ * scratch taken from a static device array of this library instead.
+ * No counterpart in the reference (its dispatch allocates with torch).
+ *
+ * For callers that cannot allocate device memory: a plugin host that hands
+ * out only its own input/output buffers and no workspace, a runtime whose
+ * memory budget is fixed up front, or a serving loop that must not call
+ * cudaMalloc/cudaFree (they synchronize the device). This entry point
+ * allocates nothing, torch included.
+ *  - Limit: the scratch is PRAXIS_B200_DISPATCH_NOALLOC_SCRATCH bytes
+ *    (4 MiB + 256, per device): enough for every token count with up to 256
+ *    experts. A call needing more (praxis_b200_dispatch_workspace_size above
+ *    the limit) returns PRAXIS_B200_EINVAL before any launch; use
+ *    praxis_b200_dispatch with a workspace for it.
+ *  - Set-up: the first call on each device looks up the scratch address
+ *    (with that device current) and keeps it; make that first call before
+ *    any stream capture starts.
+ *  - Zeroing: no part of the scratch needs to start at zero; every call
+ *    writes each scratch word before reading it.
+ *  - Races: all calls on one device share the one scratch. Calls whose work
+ *    can overlap (unordered streams, other host threads) corrupt each
+ *    other's results; order them (one stream, or events).
+ * The outputs, output sizes and errors are those of praxis_b200_dispatch. */
+#define PRAXIS_B200_DISPATCH_NOALLOC_SCRATCH (((size_t)4 << 20) + 256)
+int praxis_b200_dispatch_noalloc(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
+                                 int32_t top_k, int32_t experts, int64_t* order, int64_t* inverse,
+                                 int64_t* tokens_out, int32_t* tokens32, void* sorted_gate, int32_t* offsets,
+                                 int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles, int32_t* num_tiles,
+                                 float* act_global, uint32_t* act_amax, int device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

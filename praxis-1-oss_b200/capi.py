@@ -95,6 +95,10 @@ SIGNATURES: dict[str, tuple] = {
     "praxis_b200_interleave_gate_up": (C.c_int, [P, P, I32, I32, I32, P, P, C.c_int, P]),
     "praxis_b200_moe_workspace_size": (SZ, [I64, I32, I32, I32, I32, I32]),
     "praxis_b200_moe_forward": (C.c_int, [C.POINTER(MoeArgs)]),
+    "praxis_b200_dispatch_noalloc": (
+        C.c_int,
+        [P, P, P, I64, I32, I32, P, P, P, P, P, P, P, P, P, I32, P, P, P, C.c_int, P],
+    ),
 }
 
 

@@ -4,6 +4,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -71,6 +73,27 @@ int sm_count() {
 }
 
 // Makes `device` current for this host thread and checks it is sm_100.
+// Scratch of praxis_b200_dispatch_noalloc: one static array per device
+// (module storage, no allocation call), its address looked up once per
+// device with that device current.
+static __device__ __align__(256) unsigned char g_dispatch_noalloc_scratch[PRAXIS_B200_DISPATCH_NOALLOC_SCRATCH];
+
+static int dispatch_noalloc_scratch(int device, void** out) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {nullptr};
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_dispatch_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(PRAXIS_B200_ECUDA, "dispatch_noalloc: scratch address on device %d: %s", device,
+                       cudaGetErrorString(e));
+    addr[device] = p;
+  }
+  *out = addr[device];
+  return PRAXIS_B200_OK;
+}
+
 static int use_device(int device) {
   static int arch_ok[kMaxDevices] = {0};
   if (device < 0 || device >= kMaxDevices) return set_error(PRAXIS_B200_EINVAL, "bad device %d", device);
@@ -210,6 +233,27 @@ int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* r
                       static_cast<uint16_t*>(sorted_gate), off ? off : csr + 1, csr, pcsr,
                       reinterpret_cast<TileEntry*>(tiles), max_tiles, num_tiles, act_global, act_amax,
                       PRAXIS_STREAM(stream));
+}
+
+int praxis_b200_dispatch_noalloc(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
+                                 int32_t top_k, int32_t experts, int64_t* order, int64_t* inverse,
+                                 int64_t* tokens_out, int32_t* tokens32, void* sorted_gate, int32_t* offsets,
+                                 int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles, int32_t* num_tiles,
+                                 float* act_global, uint32_t* act_amax, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (tokens < 0 || top_k <= 0 || experts <= 0) return set_error(PRAXIS_B200_EINVAL, "dispatch_noalloc: bad sizes");
+  const size_t need = dispatch_workspace_bytes(tokens, top_k, experts);
+  if (need > PRAXIS_B200_DISPATCH_NOALLOC_SCRATCH)
+    return set_error(PRAXIS_B200_EINVAL,
+                     "dispatch_noalloc: %lld rows x %d experts need %zu bytes of scratch, the static scratch holds "
+                     "%zu; use praxis_b200_dispatch with a workspace",
+                     (long long)(tokens * top_k), experts, need, (size_t)PRAXIS_B200_DISPATCH_NOALLOC_SCRATCH);
+  void* scratch = nullptr;
+  const int rc = dispatch_noalloc_scratch(device, &scratch);
+  if (rc) return rc;
+  return praxis_b200_dispatch(top_idx, gate, row_amax, tokens, top_k, experts, scratch,
+                              PRAXIS_B200_DISPATCH_NOALLOC_SCRATCH, order, inverse, tokens_out, tokens32, sorted_gate,
+                              offsets, csr, pcsr, tiles, max_tiles, num_tiles, act_global, act_amax, device, stream);
 }
 
 int praxis_b200_quantize_gather(const void* x, int64_t tokens, int32_t dim, const int64_t* top_idx,

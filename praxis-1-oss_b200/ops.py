@@ -161,6 +161,24 @@ def dispatch(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | Non
                    tiles, num_tiles, act_global, act_amax)
 
 
+def dispatch_noalloc(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | None = None, *,
+                     order: Tensor, inverse: Tensor, tokens: Tensor, tokens32: Tensor, sorted_gate: Tensor,
+                     offsets: Tensor, csr: Tensor, pcsr: Tensor, tiles: Tensor, num_tiles: Tensor,
+                     act_global: Tensor | None = None, act_amax: Tensor | None = None) -> None:
+    """:func:`dispatch` into caller-owned output tensors through
+    ``praxis_b200_dispatch_noalloc``: no workspace, nothing allocated."""
+    _need(top_idx, "top_idx", torch.int64, 2)
+    _need(gate, "gate", BF16, 2, top_idx.device)
+    if gate.shape != top_idx.shape:
+        raise ValueError("gate / top_idx shape mismatch")
+    t, k = top_idx.shape
+    max_tiles = tiles.shape[0] // 2
+    capi.check(capi.load().praxis_b200_dispatch_noalloc(
+        _p(top_idx), _p(gate), _p(amax), t, k, num_experts, _p(order), _p(inverse), _p(tokens), _p(tokens32),
+        _p(sorted_gate), _p(offsets), _p(csr), _p(pcsr), _p(tiles), max_tiles, _p(num_tiles), _p(act_global),
+        _p(act_amax), _dev(top_idx), _stream(top_idx)))
+
+
 def route_dispatch(logits: Tensor, bias: Tensor, rows: tuple, top_k: int = 8,
                    activation: str = "sigmoid") -> Routing:
     """``router_fused.route_dispatch`` (praxis/kernels/router_fused.py:738)

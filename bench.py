@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override the config's token count (small profiling cases)")
     return ap.parse_args()
 
 
@@ -317,7 +319,8 @@ def run_b200(args, cfg):
         "stages_ms": stages,
         "roofline": roofline,
         "clocks": clk.summary(),
-        "gpu_launches": 9 * args.steps,
+        # router 2, dispatch 3, quantize 2 + scale replication 2, GEMM 2, combine 1
+        "gpu_launches": 12 * args.steps,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -346,7 +349,9 @@ def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
         evs[2].record(stream)
         r = ops.dispatch(top, gate, cfg["experts"], amax, full=False)
         evs[3].record(stream)
-        aq, asf = ops.quantize_gather(x, r, r.act_global, sf_layout=kw.sf_layout)
+        aq, asf = ops.quantize_gather(x, r, r.act_global)
+        if kw.sf_layout == capi.SF_REPLICATED:
+            asf = ops.replicate_scales(asf, 128)
         evs[4].record(stream)
         hamax = torch.zeros(cfg["experts"], dtype=torch.int32, device=x.device)
         e_g0 = torch.cuda.Event(enable_timing=True)
@@ -355,7 +360,9 @@ def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
                                   act_global=r.act_global, w_global=bank.gate_up_global, amax_out=hamax,
                                   sf_layout=kw.sf_layout)
         evs[5].record(stream)
-        hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax, sf_layout=kw.sf_layout)
+        hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
+        if kw.sf_layout == capi.SF_REPLICATED:
+            hsf = ops.replicate_scales(hsf, 128)
         evs[6].record(stream)
         rows = ops.grouped_gemm(hq, hsf, bank.down_q, kw.down_sf, r, epilogue=capi.EPI_RESCALE, act_amax=hamax,
                                 w_global=bank.down_global, sf_layout=kw.sf_layout)
@@ -409,7 +416,9 @@ def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.tokens is not None:
+        cfg["tokens"] = args.tokens
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -118,7 +118,7 @@ static int64_t padded_rows(int64_t rows, int64_t experts) { return (rows + 127 *
 // Workspace of one routed forward, 256-byte aligned pieces.
 struct MoeLayout {
   size_t dispatch, row_amax, logits, inverse, csr, pcsr, offsets, tiles, num_tiles, act_amax, act_global, h_amax,
-      aq, asf, hidden, hq, hsf, rows, total;
+      aq, asf, asf_compact, hidden, hq, hsf, hsf_compact, rows, total;
   int64_t rp;
   int max_tiles;
 };
@@ -148,9 +148,11 @@ static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int
   L.h_amax = take((size_t)experts * 4);
   L.aq = take((size_t)L.rp * dim / 2);
   L.asf = take((size_t)L.rp * dim / 16 * 4);  // room for the replicated layout
+  L.asf_compact = take((size_t)L.rp * dim / 16);
   L.hidden = take((size_t)L.rp * hidden * 2);
   L.hq = take((size_t)L.rp * hidden / 2);
   L.hsf = take((size_t)L.rp * hidden / 16 * 4);
+  L.hsf_compact = take((size_t)L.rp * hidden / 16);
   L.rows = take((size_t)L.rp * dim * 2);
   L.total = off;
   return L;
@@ -405,17 +407,31 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
                     L.row_amax - L.dispatch, nullptr, inverse, nullptr, nullptr, nullptr, offsets, csr, pcsr, tiles,
                     L.max_tiles, num_tiles, act_global, act_amax, s);
   if (rc) return rc;
+  // The quantizers write compact scales (one 4-byte word per row and 64
+  // columns); a coalesced pass then builds the replicated copies, cheaper
+  // than four scattered word stores per scale group.
+  const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
   rc = run_quantize_gather(x, a->tokens, a->dim, a->top_idx, inverse, csr, pcsr, act_global, nullptr, a->top_k,
-                           a->experts, tiles, num_tiles, L.max_tiles, aq, asf, sf_layout, s);
+                           a->experts, tiles, num_tiles, L.max_tiles, aq, rep ? ws + L.asf_compact : asf,
+                           PRAXIS_B200_SF_COMPACT, s);
   if (rc) return rc;
+  if (rep) {
+    rc = run_replicate_scales(ws + L.asf_compact, L.rp, a->dim, 128, asf, s);
+    if (rc) return rc;
+  }
   cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * a->experts, s);
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
                         a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
                         h_amax, sf_layout, s);
   if (rc) return rc;
-  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq, hsf, sf_layout, s);
+  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
+                         rep ? ws + L.hsf_compact : hsf, PRAXIS_B200_SF_COMPACT, s);
   if (rc) return rc;
+  if (rep) {
+    rc = run_replicate_scales(ws + L.hsf_compact, L.rp, a->hidden, 128, hsf, s);
+    if (rc) return rc;
+  }
   rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
                         a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, sf_layout, s);
   if (rc) return rc;

@@ -168,6 +168,83 @@ __device__ __forceinline__ float swiglu_element(float gate_acc, float up_acc, fl
 }
 
 // ---------------------------------------------------------------------------
+// Paired epilogue arithmetic: sm_100 f32x2 instructions (two IEEE fp32
+// operations, each rounded to nearest like its scalar form) and one
+// conversion for two bf16 roundings. Same bits as the scalar forms above.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// a * b + c with one rounding per lane
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+// (lo, hi) -> packed bf16x2 (lo in bits 0-15), round to nearest even
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+}
+// bf16(bf16(acc) * mult) for two accumulators of one row (packed)
+__device__ __forceinline__ uint32_t rescale_pair(float a0, float a1, float mult) {
+  const float2 v = mul2_rn(unpack_bf16x2(cvt_bf16x2(a0, a1)), make_float2(mult, mult));
+  return cvt_bf16x2(v.x, v.y);
+}
+
+// The SwiGLU element of swiglu_element<> for two adjacent columns of one row
+// (gate accumulators g0, g1; up accumulators u0, u1); returns h packed as
+// bf16x2. The sigmoid's division 1 / d (d = 1 + 2^t >= 1) is recip_rn_ge1
+// unrolled: for d <= 2^64 its scale is 1, so
+//   y1 = y0 + y0 (1 - d y0);  q = y1 + (1 - d y1) y1
+// on both lanes at once; larger (or infinite) d take the scalar form.
+__device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, float u1, float mult) {
+  const float2 g = unpack_bf16x2(rescale_pair(g0, g1, mult));
+  const float2 u = unpack_bf16x2(rescale_pair(u0, u1, mult));
+  const float2 t = mul2_rn(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  float e0, e1;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(e0) : "f"(t.x));
+  asm("ex2.approx.f32 %0, %1;" : "=f"(e1) : "f"(t.y));
+  const float2 one = make_float2(1.0f, 1.0f);
+  const float2 d = add2_rn(one, make_float2(e0, e1));
+  float2 s;
+  if (d.x > 1.8446744073709552e19f || d.y > 1.8446744073709552e19f) {
+    s = make_float2(recip_rn_ge1(d.x), recip_rn_ge1(d.y));
+  } else {
+    float2 y0;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0.y) : "f"(d.y));
+    const float2 nd = make_float2(-d.x, -d.y);
+    const float2 y1 = fma2_rn(y0, fma2_rn(nd, y0, one), y0);
+    s = fma2_rn(fma2_rn(nd, y1, one), y1, y1);
+  }
+  const float2 gs = mul2_rn(g, s);
+  const float2 silu = unpack_bf16x2(cvt_bf16x2(gs.x, gs.y));
+  const float2 h = mul2_rn(silu, u);
+  return cvt_bf16x2(h.x, h.y);
+}
+
+// ---------------------------------------------------------------------------
 // Shared-memory addresses and mbarriers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

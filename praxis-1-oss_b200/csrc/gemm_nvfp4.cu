@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
         // up rows (praxis_b200_interleave_gate_up): tile columns [64c, 64c+32)
         // are gate and [64c+32, 64c+64) up for hidden columns 32c.. of the tile.
         const float mult = expert_multiplier(p, t.expert);
-        float rmax = 0.0f;
+        __nv_bfloat162 hmax = __floats2bfloat162_rn(0.0f, 0.0f);
         constexpr int HALF = BLOCK_N / 2;
 #pragma unroll 1
         for (int c = 0; c < HALF / 32; ++c) {
@@ -223,14 +223,16 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            float h0 = swiglu_element<true>(__uint_as_float(g[j]), __uint_as_float(up[j]), mult);
-            float h1 = swiglu_element<true>(__uint_as_float(g[j + 1]), __uint_as_float(up[j + 1]), mult);
-            if (!valid) h0 = h1 = 0.0f;
-            rmax = fmaxf(rmax, fmaxf(fabsf(h0), fabsf(h1)));
-            packed[j / 2] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632);
+            uint32_t h = swiglu_pair(__uint_as_float(g[j]), __uint_as_float(g[j + 1]), __uint_as_float(up[j]),
+                                     __uint_as_float(up[j + 1]), mult);
+            if (!valid) h = 0u;
+            hmax = __hmax2(hmax, __habs2(*reinterpret_cast<__nv_bfloat162*>(&h)));
+            packed[j / 2] = h;
           }
           store_row_chunk(p.out + grow * p.out_cols + (size_t)n * HALF + c * 32, packed);
         }
+        const uint32_t hm = *reinterpret_cast<uint32_t*>(&hmax);
+        float rmax = fmaxf(__uint_as_float(hm << 16), __uint_as_float(hm & 0xFFFF0000u));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
         if (lane == 0) atomicMax(p.amax_out + t.expert, __float_as_uint(rmax));
@@ -245,13 +247,8 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
             uint32_t packed[16];
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-              float v0 = __uint_as_float(r[j]);
-              float v1 = __uint_as_float(r[j + 1]);
-              if constexpr (EPI == EPI_RESCALE) {
-                v0 = __fmul_rn(bf16_round_alu(v0), mult);
-                v1 = __fmul_rn(bf16_round_alu(v1), mult);
-              }
-              packed[j / 2] = pack_bf16x2_alu(v0, v1);
+              const float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+              packed[j / 2] = EPI == EPI_RESCALE ? rescale_pair(v0, v1, mult) : cvt_bf16x2(v0, v1);
             }
             store_row_chunk(p.out + grow * p.out_cols + (size_t)n * BLOCK_N + c * 32, packed);
           }
@@ -513,7 +510,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
       const bool valid = row_in_tile < here_valid;
       const uint32_t tbase = tmem + ((quad * 32u) << 16) + (odd ? S::ACC_ALT_COL : 0u);
       const float mult = (EPI == EPI_PLAIN) ? 1.0f : expert_multiplier(p, t.expert);
-      float rmax = 0.0f;
+      __nv_bfloat162 hmax = __floats2bfloat162_rn(0.0f, 0.0f);  // max |h| per column parity
       // the staging boxes are free once this warp's previous stores read them
       if (lane == 0) bulk_wait_group_read0();
       __syncwarp();
@@ -536,11 +533,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const int e0 = c * 8 + 2 * j;
-              float h0 = swiglu_element<true>(__uint_as_float(r0[e0]), __uint_as_float(r1[e0]), mult);
-              float h1 = swiglu_element<true>(__uint_as_float(r0[e0 + 1]), __uint_as_float(r1[e0 + 1]), mult);
-              if (!valid) h0 = h1 = 0.0f;
-              rmax = fmaxf(rmax, fmaxf(fabsf(h0), fabsf(h1)));
-              w[j] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632);
+              uint32_t h = swiglu_pair(__uint_as_float(r0[e0]), __uint_as_float(r0[e0 + 1]),
+                                       __uint_as_float(r1[e0]), __uint_as_float(r1[e0 + 1]), mult);
+              if (!valid) h = 0u;
+              hmax = __hmax2(hmax, __habs2(*reinterpret_cast<__nv_bfloat162*>(&h)));
+              w[j] = h;
             }
             stage_chunk(stg, (int)lane, 4 * bl + c, make_uint4(w[0], w[1], w[2], w[3]));
           }
@@ -558,12 +555,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
             uint32_t w[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              float v0 = __uint_as_float(r[b0 + 2 * j]), v1 = __uint_as_float(r[b0 + 2 * j + 1]);
-              if constexpr (EPI == EPI_RESCALE) {
-                v0 = __fmul_rn(bf16_round_alu(v0), mult);
-                v1 = __fmul_rn(bf16_round_alu(v1), mult);
-              }
-              w[j] = pack_bf16x2_alu(v0, v1);
+              const float v0 = __uint_as_float(r[b0 + 2 * j]), v1 = __uint_as_float(r[b0 + 2 * j + 1]);
+              w[j] = EPI == EPI_RESCALE ? rescale_pair(v0, v1, mult) : cvt_bf16x2(v0, v1);
             }
             stage_chunk(stg, (int)lane, c, make_uint4(w[0], w[1], w[2], w[3]));
           }
@@ -584,6 +577,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
         }
       }
       if constexpr (EPI == EPI_SWIGLU) {
+        const uint32_t hm = *reinterpret_cast<uint32_t*>(&hmax);
+        float rmax = fmaxf(__uint_as_float(hm << 16), __uint_as_float(hm & 0xFFFF0000u));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
         if (lane == 0) atomicMax(p.amax_out + t.expert, __float_as_uint(rmax));

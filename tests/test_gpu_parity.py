@@ -257,14 +257,17 @@ def test_interleave_gate_up_layout(P):
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("mult", [1.0, 0.3])
 def test_swiglu_alu_arithmetic_equals_ieee_on_every_bf16_gate(P, mult):
-    """The fused epilogue rounds with integer ops and divides with a refined
-    reciprocal; it must give the bits of conversion instructions and IEEE
-    division for every bf16 gate value (NaN payloads aside)."""
+    """The fused epilogue computes two columns at a time with paired fp32
+    instructions and divides with a refined reciprocal; it must give the bits
+    of the scalar IEEE-division form for every bf16 gate value in either
+    column of a pair (NaN payloads aside)."""
     rows, hidden = 65536, 128
     g = gen(11)
     raw = torch.empty(rows, 2 * hidden, dtype=torch.bfloat16)
-    raw[:, 1:hidden] = torch.randn(rows, hidden - 1, generator=g).to(torch.bfloat16) * 4
-    raw[:, 0] = torch.arange(rows, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)  # all 2^16 patterns
+    raw[:, 2:hidden] = torch.randn(rows, hidden - 2, generator=g).to(torch.bfloat16) * 4
+    patterns = torch.arange(rows, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)  # all 2^16 patterns
+    raw[:, 0] = patterns
+    raw[:, 1] = patterns.roll(12345)
     raw[:, hidden:] = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
     raw = raw.to(DEV)
     pcsr = torch.tensor([0, rows], dtype=torch.int32, device=DEV)

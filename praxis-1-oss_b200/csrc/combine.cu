@@ -59,21 +59,25 @@ __global__ void __launch_bounds__(256) combine_kernel(
     for (int u = 0; u < U; ++u) {
       const int c = c0 + u * 256;
       if (c >= cols) break;
-      float acc[4][8];
+      // column pairs (2j, 2j+1) in paired fp32 arithmetic, same operations
+      // and order per element as the scalar form
+      float2 acc[4][4];
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[a][i] = 0.0f;
+        for (int j = 0; j < 4; ++j) acc[a][j] = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         if (s < top_k) {
           const uint32_t wv[4] = {v[u][s].x, v[u][s].y, v[u][s].z, v[u][s].w};
-          const float sc = s_scale[warp][s], mult = s_mult[warp][s];
+          const float2 sc = make_float2(s_scale[warp][s], s_scale[warp][s]);
+          const float mult = s_mult[warp][s];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float val = bf16_to_f32((uint16_t)((wv[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu));
-            if (!rows_rescaled) val = bf16_round_alu(__fmul_rn(val, mult));
-            acc[s & 3][i] = __fadd_rn(acc[s & 3][i], __fmul_rn(val, sc));
+          for (int j = 0; j < 4; ++j) {
+            const float2 val = rows_rescaled ? unpack_bf16x2(wv[j]) : unpack_bf16x2(rescale_pair(
+                                                                          __uint_as_float(wv[j] << 16),
+                                                                          __uint_as_float(wv[j] & 0xFFFF0000u), mult));
+            acc[s & 3][j] = add2_rn(acc[s & 3][j], mul2_rn(val, sc));
           }
         }
       }
@@ -82,16 +86,13 @@ __global__ void __launch_bounds__(256) combine_kernel(
       const uint32_t shv[4] = {sh.x, sh.y, sh.z, sh.w};
       uint32_t packed[4];
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        float y[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          y[j] = bf16_round_alu(
-              __fadd_rn(__fadd_rn(__fadd_rn(acc[0][i + j], acc[1][i + j]), acc[2][i + j]), acc[3][i + j]));
-          if (shared != nullptr)
-            y[j] = __fadd_rn(y[j], bf16_to_f32((uint16_t)((shv[(i + j) >> 1] >> (((i + j) & 1) * 16)) & 0xFFFFu)));
+      for (int j = 0; j < 4; ++j) {
+        const float2 sum = add2_rn(add2_rn(add2_rn(acc[0][j], acc[1][j]), acc[2][j]), acc[3][j]);
+        packed[j] = cvt_bf16x2(sum.x, sum.y);
+        if (shared != nullptr) {
+          const float2 y = add2_rn(unpack_bf16x2(packed[j]), unpack_bf16x2(shv[j]));
+          packed[j] = cvt_bf16x2(y.x, y.y);
         }
-        packed[i >> 1] = pack_bf16x2_alu(y[0], y[1]);
       }
       *reinterpret_cast<uint4*>(out + t * cols + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }

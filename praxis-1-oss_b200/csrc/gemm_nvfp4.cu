@@ -599,22 +599,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
 // Packed FP4 rows viewed as bytes: dims {K/2, rows}, box {128 B, box_rows}.
 static int make_fp4_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
   EncodeTiledFn fn = encode_fn();

@@ -13,142 +13,192 @@
 //   gate = bf16(s[top] / sum)   ATen's CUDA reduction order of a k-wide row
 // softmax gating (this build's extension) uses the same selection and gates.
 //
-// logits: one CTA per 64 tokens, bf16 mma.sync (m16n8k16, fp32 accumulate) on
-// the exact bf16 inputs; an fp32 router weight is passed as 3 bf16 terms
-// (hi + mid + lo == the fp32 value), so every product is exact and only the
-// fp32 summation order differs from cuBLAS SGEMM. The same pass computes the
-// per-token max |x| used by the activation global scale.
+// logits: tcgen05 kind::f16 MMA, one CTA per 128 tokens. x and the weight
+// terms are staged by TMA in 64-column (128-byte swizzled) slabs; an fp32
+// router weight is passed as 3 bf16 terms (hi + mid + lo == the fp32 value),
+// each term's products accumulate in its own tensor-memory columns and the
+// epilogue adds the three (every product is exact; only the fp32 summation
+// order differs from cuBLAS SGEMM). While the MMAs run, the epilogue warps
+// take the per-token max |x| (activation global scale) from the staged slabs.
 // routing: one warp per token.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace praxis {
 
-constexpr int kRouterBM = 64;
-constexpr int kRouterBK = 32;
-constexpr int kRouterPad = 40;  // bf16 per smem row (80 B: conflict-free ldmatrix)
+constexpr int kRouterBM = 128;
+constexpr int kRouterBK = 64;          // bf16 columns per 128-byte swizzled slab
+constexpr int kRouterABytes = kRouterBM * 128;
+constexpr int kRouterSmemBudget = 200 * 1024;
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
-  const uint32_t d = smem_u32(dst);
-  const int size = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(size) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldmatrix_x2(uint32_t (&r)[2], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
-               : "=r"(r[0]), "=r"(r[1])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-
-// NT = experts/8 rounded up to a power of two; SPLITS = 1 (bf16 weight) or 3.
-template <int NT, int SPLITS>
-__global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                            const uint16_t* __restrict__ w, int64_t tokens,
-                                                            int dim, int experts, float* __restrict__ logits,
-                                                            uint16_t* __restrict__ row_amax) {
-  constexpr int EP = NT * 8;
-  extern __shared__ __align__(16) uint16_t s_router[];
-  uint16_t* sx = s_router;                                // [2][64][40]
-  uint16_t* sw = s_router + 2 * kRouterBM * kRouterPad;  // [2][SPLITS*EP][40]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Warp 0: TMA producer; warp 1: tensor-memory owner and MMA issuer; warps
+// 2..5: row max |x| during the main loop, then the logits epilogue (warp w
+// reads tensor-memory lanes 32 * (w % 4) .. + 31 = tokens of those rows).
+__global__ void __launch_bounds__(192, 1) router_logits_kernel(
+    const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w, int64_t tokens, int dim,
+    int experts, int splits, int e_pad, int stages, uint32_t tmem_cols, float* __restrict__ logits,
+    uint16_t* __restrict__ row_amax) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int b_bytes = splits * e_pad * 128;
+  const int stage_bytes = kRouterABytes + b_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)stages * stage_bytes);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
   const int64_t row0 = (int64_t)blockIdx.x * kRouterBM;
-  const int ktiles = dim / kRouterBK;
+  const int ktiles = (dim + kRouterBK - 1) / kRouterBK;
 
-  auto load_stage = [&](int stage, int kt) {
-    const int k0 = kt * kRouterBK;
-    for (int c = tid; c < kRouterBM * 4; c += 128) {
-      const int r = c >> 2, ch = c & 3;
-      const int64_t gr = row0 + r;
-      const bool ok = gr < tokens;
-      cp_async16(sx + (stage * kRouterBM + r) * kRouterPad + ch * 8, x + (ok ? gr : 0) * dim + k0 + ch * 8, ok);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 row-max warps
     }
-    for (int c = tid; c < SPLITS * EP * 4; c += 128) {
-      const int r = c >> 2, ch = c & 3;
-      const int s = r / EP, e = r % EP;
-      const bool ok = e < experts;
-      cp_async16(sw + (stage * SPLITS * EP + r) * kRouterPad + ch * 8,
-                 w + ((int64_t)s * experts + (ok ? e : 0)) * dim + k0 + ch * 8, ok);
-    }
-    cp_async_commit();
-  };
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  float acc[NT][4];
-#pragma unroll
-  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-  float rmax = 0.0f;
-
-  load_stage(0, 0);
-  for (int kt = 0; kt < ktiles; ++kt) {
-    const int stage = kt & 1;
-    if (kt + 1 < ktiles) {
-      load_stage(stage ^ 1, kt + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint16_t* xs = sx + stage * kRouterBM * kRouterPad;
-    const uint16_t* ws = sw + stage * SPLITS * EP * kRouterPad;
-    {  // per-token max |x| (thread -> row tid/2, 16 columns)
-      const uint4* p = reinterpret_cast<const uint4*>(xs + (tid >> 1) * kRouterPad + (tid & 1) * 16);
-      uint4 a = p[0], b = p[1];
-      const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        rmax = fmaxf(rmax, fmaxf(fabsf(bf16_to_f32((uint16_t)(v[i] & 0xFFFFu))), fabsf(bf16_to_f32((uint16_t)(v[i] >> 16)))));
-    }
-#pragma unroll
-    for (int ks = 0; ks < kRouterBK / 16; ++ks) {
-      uint32_t a[4];
-      ldmatrix_x4(a, xs + (warp * 16 + (lane & 15)) * kRouterPad + ks * 16 + (lane >> 4) * 8);
-#pragma unroll
-      for (int s = 0; s < SPLITS; ++s) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          uint32_t b[2];
-          ldmatrix_x2(b, ws + (s * EP + nt * 8 + (lane & 7)) * kRouterPad + ks * 16 + ((lane >> 3) & 1) * 8);
-          mma_bf16(acc[nt], a, b);
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) break;
+        uint8_t* st = smem + (size_t)stage * stage_bytes;
+        mbar_arrive_expect_tx(&full[stage], (uint32_t)stage_bytes);
+        tma_load_2d(st, &tmap_x, &full[stage], kt * kRouterBK, (int32_t)row0);
+        for (int s = 0; s < splits; ++s)
+          tma_load_2d(st + kRouterABytes + s * e_pad * 128, &tmap_w, &full[stage], kt * kRouterBK, s * experts);
+        if (++stage == (uint32_t)stages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
     }
-    __syncthreads();
-  }
-  rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
-  if (row_amax != nullptr && (tid & 1) == 0 && row0 + (tid >> 1) < tokens) row_amax[row0 + (tid >> 1)] = f32_to_bf16(rmax);
-  const int r_lo = warp * 16 + (lane >> 2);
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // the terms' weight rows are contiguous in shared memory: one MMA per
+      // chunk of up to 256 columns covers several terms at once
+      const int n_total = splits * e_pad;
+      const int n0 = n_total > 256 ? 256 : n_total;
+      const uint32_t idesc0 = idesc_bf16(128, (uint32_t)n0);
+      const uint32_t idesc1 = idesc_bf16(128, (uint32_t)(n_total > 256 ? n_total - 256 : 16));
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        if (!mbar_wait(&full[stage], phase, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + (size_t)stage * stage_bytes);
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int col = nt * 8 + (lane & 3) * 2;
-    if (col < experts) {
-      if (row0 + r_lo < tokens)
-        *reinterpret_cast<float2*>(logits + (row0 + r_lo) * experts + col) = make_float2(acc[nt][0], acc[nt][1]);
-      if (row0 + r_lo + 8 < tokens)
-        *reinterpret_cast<float2*>(logits + (row0 + r_lo + 8) * experts + col) = make_float2(acc[nt][2], acc[nt][3]);
+        for (int ks = 0; ks < kRouterBK / 16; ++ks) {
+          const uint64_t ad = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSwizzle128B);
+          const uint32_t acc = (kt | ks) != 0 ? 1u : 0u;
+          tc_mma_bf16(tmem, ad, smem_desc(a_base + kRouterABytes + ks * 32, 16, 1024, kLayoutSwizzle128B), idesc0,
+                      acc);
+          if (n_total > 256)
+            tc_mma_bf16(tmem + 256, ad,
+                        smem_desc(a_base + kRouterABytes + 256 * 128 + ks * 32, 16, 1024, kLayoutSwizzle128B),
+                        idesc1, acc);
+        }
+        tc_commit(&empty[stage]);
+        if (++stage == (uint32_t)stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) tc_commit(acc_full);
     }
+  } else {
+    const uint32_t quad = (uint32_t)(warp & 3);
+    const int row = (int)(quad * 32 + lane);
+    // partial max |x| of rows quad*32 + 4i + lane/8, 16-byte chunk lane%8:
+    // each load instruction reads 4 whole slab rows (512 contiguous bytes)
+    float part[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int kt = 0; kt < ktiles; ++kt) {
+      if (!mbar_wait(&full[stage], phase, kErrTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      // (the swizzle permutes 16-byte chunks within a row; the max does not care)
+      const uint8_t* src = smem + (size_t)stage * stage_bytes + quad * 32 * 128 + lane * 16;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + i * 512);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          part[i] = fmaxf(part[i], fmaxf(fabsf(__uint_as_float(w[j] << 16)), fabsf(__uint_as_float(w[j] & 0xFFFF0000u))));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == (uint32_t)stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    // reduce each row's 8 chunk maxima; lane L keeps row quad*32 + L
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float v = part[i];
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+      const float r = __shfl_sync(0xffffffffu, v, (lane & 3) * 8);
+      if ((int)(lane >> 2) == i) m = r;
+    }
+    const int64_t grow = row0 + row;
+    if (row_amax != nullptr && grow < tokens) row_amax[grow] = f32_to_bf16(m);
+    if (ok && mbar_wait(acc_full, 0, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+      const uint32_t lane_base = tmem + ((quad * 32u) << 16);
+      float* out = logits + grow * experts;
+      for (int e0 = 0; e0 < e_pad; e0 += 16) {
+        float acc[16];
+        for (int s = 0; s < splits; ++s) {
+          uint32_t r[16];
+          tc_ld_32x32b_x16(lane_base + s * e_pad + e0, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = s == 0 ? __uint_as_float(r[j]) : add_rn(acc[j], __uint_as_float(r[j]));
+        }
+        if (grow < tokens) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (e0 + j < experts) out[e0 + j] = acc[j];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Routing (one warp per token; experts <= 256, top_k <= 8)
 // ---------------------------------------------------------------------------
-constexpr int kMaxPerLane = 8;
 
 __device__ __forceinline__ uint32_t ordered_u32(float v) {
   // float order -> unsigned integer order (-0.0 < +0.0), ATen TopKTypeConfig
@@ -163,6 +213,8 @@ __device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int o) {
   return ((uint64_t)hi << 32) | lo;
 }
 
+// P = experts per lane (experts <= 32 * P).
+template <int P>
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
                                                     int64_t tokens, int experts, int top_k, int activation,
                                                     int64_t* __restrict__ top_idx, uint16_t* __restrict__ gate) {
@@ -170,10 +222,10 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
   const float* lr = logits + t * experts;
-  float score[kMaxPerLane], biased[kMaxPerLane];
+  float score[P], biased[P];
   float lmax = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < P; ++i) {
     const int e = lane + 32 * i;
     score[i] = e < experts ? lr[e] : -INFINITY;
     lmax = fmaxf(lmax, score[i]);
@@ -183,7 +235,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
     float sum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < P; ++i) {
       const int e = lane + 32 * i;
       score[i] = e < experts ? expf(__fsub_rn(score[i], lmax)) : 0.0f;
       sum = add_rn(sum, score[i]);
@@ -191,13 +243,13 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum = add_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) score[i] = div_rn(score[i], sum);
+    for (int i = 0; i < P; ++i) score[i] = div_rn(score[i], sum);
   } else {
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) score[i] = div_rn(1.0f, add_rn(1.0f, expf(-score[i])));
+    for (int i = 0; i < P; ++i) score[i] = div_rn(1.0f, add_rn(1.0f, expf(-score[i])));
   }
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < P; ++i) {
     const int e = lane + 32 * i;
     biased[i] = (bias != nullptr && e < experts) ? add_rn(score[i], bias[e]) : score[i];
   }
@@ -217,7 +269,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     if (j < top_k) {
       uint64_t best = 0;
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) {
+      for (int i = 0; i < P; ++i) {
         const int e = lane + 32 * i;
         if (e < experts && !(taken & (1u << i))) {
           const uint64_t key = ((uint64_t)ordered_u32(biased[i]) << 32) | (uint32_t)(experts - 1 - e);
@@ -237,7 +289,10 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   }
 
   // -- gather order: entries above the k-th value, then the ties, each by index
-  const uint32_t kth = sel_hi[top_k - 1];
+  uint32_t kth = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (j == top_k - 1) kth = sel_hi[j];
   int my_idx = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -261,7 +316,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     const int src_lane = my_idx & 31, src_i = my_idx >> 5;
     float bv = 0.0f, sv = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < P; ++i) {
       const float b_i = __shfl_sync(0xffffffffu, biased[i], src_lane);
       const float s_i = __shfl_sync(0xffffffffu, score[i], src_lane);
       if (i == src_i) {
@@ -323,46 +378,51 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 // ---------------------------------------------------------------------------
 // Host entries
 // ---------------------------------------------------------------------------
-template <int NT, int SPLITS>
-static int launch_router_logits(const uint16_t* x, const uint16_t* w, int64_t tokens, int dim, int experts,
-                                float* logits, uint16_t* row_amax, cudaStream_t stream) {
-  const size_t smem = (size_t)2 * (kRouterBM + SPLITS * NT * 8) * kRouterPad * 2;
-  auto kern = router_logits_kernel<NT, SPLITS>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
-  const int64_t blocks = (tokens + kRouterBM - 1) / kRouterBM;
-  kern<<<(unsigned)blocks, 128, smem, stream>>>(x, w, tokens, dim, experts, logits, row_amax);
-  return check_launch("router_logits");
-}
-
-template <int SPLITS>
-static int dispatch_router_nt(int nt, const uint16_t* x, const uint16_t* w, int64_t tokens, int dim, int experts,
-                              float* logits, uint16_t* row_amax, cudaStream_t stream) {
-  switch (nt) {
-    case 1: return launch_router_logits<1, SPLITS>(x, w, tokens, dim, experts, logits, row_amax, stream);
-    case 2: return launch_router_logits<2, SPLITS>(x, w, tokens, dim, experts, logits, row_amax, stream);
-    case 4: return launch_router_logits<4, SPLITS>(x, w, tokens, dim, experts, logits, row_amax, stream);
-    case 8: return launch_router_logits<8, SPLITS>(x, w, tokens, dim, experts, logits, row_amax, stream);
-    case 16: return launch_router_logits<16, SPLITS>(x, w, tokens, dim, experts, logits, row_amax, stream);
-    case 32: return launch_router_logits<32, SPLITS>(x, w, tokens, dim, experts, logits, row_amax, stream);
-    default: return set_error(PRAXIS_B200_EINVAL, "unsupported expert count");
-  }
+static int make_bf16_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kRouterBK, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PRAXIS_B200_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PRAXIS_B200_OK;
 }
 
 int run_router_logits(const uint16_t* x, const uint16_t* w, int splits, int64_t tokens, int dim, int experts,
                       float* logits, uint16_t* row_amax, cudaStream_t stream) {
   if (experts < 1 || experts > 256) return set_error(PRAXIS_B200_EINVAL, "router supports 1..256 experts");
-  if (dim % kRouterBK != 0) return set_error(PRAXIS_B200_EINVAL, "router needs dim %% 32 == 0");
+  if (dim % 32 != 0) return set_error(PRAXIS_B200_EINVAL, "router needs dim %% 32 == 0");
   if (splits != 1 && splits != 3) return set_error(PRAXIS_B200_EINVAL, "router weight splits must be 1 or 3");
+  if (splits == 3 && experts > 128) return set_error(PRAXIS_B200_EINVAL, "fp32 router weight supports <= 128 experts");
+  if (((uintptr_t)x | (uintptr_t)w) & 15) return set_error(PRAXIS_B200_EINVAL, "router inputs must be 16-byte aligned");
   if (tokens == 0) return PRAXIS_B200_OK;
-  int nt = 1;
-  while (nt * 8 < experts) nt <<= 1;
-  if (nt > 16 && splits == 3) return set_error(PRAXIS_B200_EINVAL, "fp32 router weight supports <= 128 experts");
-  return splits == 1 ? dispatch_router_nt<1>(nt, x, w, tokens, dim, experts, logits, row_amax, stream)
-                     : dispatch_router_nt<3>(nt, x, w, tokens, dim, experts, logits, row_amax, stream);
+  const int e_pad = (experts + 15) / 16 * 16;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < (uint32_t)(splits * e_pad)) tmem_cols <<= 1;
+  const int stage_bytes = kRouterABytes + splits * e_pad * 128;
+  int stages = kRouterSmemBudget / stage_bytes;
+  stages = stages < 2 ? 2 : stages > 6 ? 6 : stages;
+  const size_t smem = 1024 + (size_t)stages * stage_bytes + (2 * stages + 2) * 8;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "router smem attribute: %s", cudaGetErrorString(e));
+    attr = true;
+  }
+  CUtensorMap mx, mw;
+  int rc = make_bf16_map(&mx, x, tokens, dim, kRouterBM);
+  if (rc) return rc;
+  rc = make_bf16_map(&mw, w, (int64_t)splits * experts, dim, e_pad);
+  if (rc) return rc;
+  const int64_t blocks = (tokens + kRouterBM - 1) / kRouterBM;
+  router_logits_kernel<<<(unsigned)blocks, 192, smem, stream>>>(mx, mw, tokens, dim, experts, splits, e_pad, stages,
+                                                                 tmem_cols, logits, row_amax);
+  return check_launch("router_logits");
 }
 
 int run_route(const float* logits, const float* bias, int64_t tokens, int experts, int top_k, int activation,
@@ -372,8 +432,15 @@ int run_route(const float* logits, const float* bias, int64_t tokens, int expert
   if (activation != PRAXIS_B200_SIGMOID && activation != PRAXIS_B200_SOFTMAX)
     return set_error(PRAXIS_B200_EINVAL, "unknown router activation");
   if (tokens == 0) return PRAXIS_B200_OK;
-  const int64_t blocks = (tokens + 7) / 8;
-  route_kernel<<<(unsigned)blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+  const unsigned blocks = (unsigned)((tokens + 7) / 8);
+  if (experts <= 32)
+    route_kernel<1><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+  else if (experts <= 64)
+    route_kernel<2><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+  else if (experts <= 128)
+    route_kernel<4><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+  else
+    route_kernel<8><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
   return check_launch("route");
 }
 

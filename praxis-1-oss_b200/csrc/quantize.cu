@@ -42,35 +42,60 @@ __device__ __forceinline__ uint32_t sf_offset_rep(int64_t row, int col, int kb, 
 
 __device__ __forceinline__ float clamp6(float x) { return fminf(fmaxf(x, -6.0f), 6.0f); }
 
+// Eight floats -> eight E2M1 codes in one word (element 0 in the low nibble).
+__device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 d) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y), "f"(d.x), "f"(d.y));
+  return out;
+}
+
 // Quantize 16 values with global g (inv_g = div_rn(1, g)); returns the 8
-// code bytes in (lo, hi) and the scale byte.
-__device__ __forceinline__ void quantize16(const float (&v)[16], float amax, float g, float inv_g, uint32_t& lo,
-                                           uint32_t& hi, uint32_t& sf) {
+// code bytes in (lo, hi) and the scale byte. The reference clamps v * rc to
+// [-6, 6] (NaN-ignoring min/max, so NaN -> -6) before the saturating
+// conversion. For finite inputs v * rc stays finite (|v| <= amax, the scale
+// is at least 2^-6), where the saturating conversion alone gives the same
+// codes; blocks holding an infinity or NaN (has_nan) take the clamp.
+__device__ __forceinline__ void quantize16(const float (&v)[16], float amax, float g, float inv_g, bool has_nan,
+                                           uint32_t& lo, uint32_t& hi, uint32_t& sf) {
   const float bs = mul_rn(amax, kOneSixth);
   const float sfv = fminf(fmaxf(div_rn(bs, g), 0.015625f), 448.0f);
   sf = f32_to_e4m3_byte(sfv);
   const float rc = div_rn(inv_g, e4m3_byte_to_f32(sf));
-  lo = 0;
-  hi = 0;
+  const float2 rc2 = make_float2(rc, rc);
+  float2 n[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    lo |= f32x2_to_e2m1_byte(clamp6(mul_rn(v[2 * i], rc)), clamp6(mul_rn(v[2 * i + 1], rc))) << (8 * i);
+  for (int i = 0; i < 8; ++i) n[i] = mul2_rn(make_float2(v[2 * i], v[2 * i + 1]), rc2);
+  if (has_nan) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    hi |= f32x2_to_e2m1_byte(clamp6(mul_rn(v[8 + 2 * i], rc)), clamp6(mul_rn(v[9 + 2 * i], rc))) << (8 * i);
+    for (int i = 0; i < 8; ++i) n[i] = make_float2(clamp6(n[i].x), clamp6(n[i].y));
+  }
+  lo = e2m1x8(n[0], n[1], n[2], n[3]);
+  hi = e2m1x8(n[4], n[5], n[6], n[7]);
 }
 
-__device__ __forceinline__ void load16_bf16(const uint16_t* src, float (&v)[16], float& amax) {
+// 16 bf16 values -> floats, their max |v| (NaN-ignoring) and whether any is
+// not finite (magnitude bits >= 0x7F80: infinity or NaN).
+__device__ __forceinline__ void load16_bf16(const uint16_t* src, float (&v)[16], float& amax, bool& has_nan) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
   uint4 a = __ldg(s), b = __ldg(s + 1);
   const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
   amax = 0.0f;
+  uint32_t nan_bits = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    v[2 * i] = bf16_to_f32((uint16_t)(w[i] & 0xFFFFu));
-    v[2 * i + 1] = bf16_to_f32((uint16_t)(w[i] >> 16));
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
     amax = fmaxf(amax, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
+    nan_bits |= (w[i] & 0x7FFF7FFFu) + 0x00800080u;
   }
+  has_nan = (nan_bits & 0x80008000u) != 0;
 }
 
 // Gather the four scale bytes of lanes 4i..4i+3 into one word (the 4 scales
@@ -151,12 +176,13 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
     const bool active = j < kb;
     float v[16];
     float amax = 0.0f;
-    if (active) load16_bf16(xr + j * 16, v, amax);
+    bool has_nan = false;
+    if (active) load16_bf16(xr + j * 16, v, amax, has_nan);
     for (int s = 0; s < top_k; ++s) {
       uint32_t lo = 0, hi = 0, sfb = 0;
       const int64_t dest = s_dest[warp][s];
       if (active) {
-        quantize16(v, amax, s_g[warp][s], s_ig[warp][s], lo, hi, sfb);
+        quantize16(v, amax, s_g[warp][s], s_ig[warp][s], has_nan, lo, hi, sfb);
         *reinterpret_cast<uint2*>(q + dest * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
       }
       store_sf_group(sf, dest, j, kb, sfb, active, rep);
@@ -188,8 +214,9 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
     if (active) {
       float v[16];
       float amax;
-      load16_bf16(xr + j * 16, v, amax);
-      quantize16(v, amax, g, ig, lo, hi, sfb);
+      bool has_nan;
+      load16_bf16(xr + j * 16, v, amax, has_nan);
+      quantize16(v, amax, g, ig, has_nan, lo, hi, sfb);
       *reinterpret_cast<uint2*>(q + row * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
     }
     store_sf_group(sf, row, j, kb, sfb, active, rep);
@@ -222,13 +249,15 @@ __global__ void pack_quant_kernel(const uint16_t* __restrict__ w, int k_dim, int
   const uint16_t* src = w + (int64_t)e * k_dim * n_dim + (int64_t)j * 16 * n_dim + n;
   float v[16];
   float m = 0.0f;
+  bool has_nan = false;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     v[i] = bf16_to_f32(src[(int64_t)i * n_dim]);
     m = fmaxf(m, fabsf(v[i]));
+    has_nan |= !isfinite(v[i]);
   }
   uint32_t lo, hi, sfb;
-  quantize16(v, m, g, div_rn(1.0f, g), lo, hi, sfb);
+  quantize16(v, m, g, div_rn(1.0f, g), has_nan, lo, hi, sfb);
   const int kb = k_dim / 16;
   *reinterpret_cast<uint2*>(q + ((int64_t)e * n_dim + n) * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
   sf[(int64_t)e * n_dim * kb + sf_offset(n, j, kb)] = (uint8_t)sfb;

@@ -187,6 +187,9 @@ def test_quantize_gather_bit_exact(P, t, c, e, k, layout):
     x = (torch.randn(t, c, generator=g) * 1.5).to(torch.bfloat16)
     x[0, :16] = torch.tensor([0.0, -0.0, 1e-30, -1e-30, 6.0, -6.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 100.0,
                               -100.0, 0.5]).to(torch.bfloat16)
+    # values near the bf16 maximum (the experts' global scale follows them)
+    x[1, 16:32] = torch.tensor([3e38, -3e38, 1.0, -2.0, 3.0, 0.0, -0.0, 7.0, 1e30, -1e30, 0.1, 0.2, 0.3, -0.4,
+                                5.5, 6.5]).to(torch.bfloat16)
     xd = x.to(DEV)
     amax = P.ops.row_amax(xd)
     r = P.ops.dispatch(top.to(DEV), gate.to(DEV), e, amax)

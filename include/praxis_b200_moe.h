@@ -162,6 +162,7 @@ int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, co
  * Replaces praxis/kernels/nvfp4.py:355-419 (grouped_nvfp4_mm) with
  * praxis/kernels/nvfp4_moe.py:102-158 (EPI_SWIGLU) or the rescale of
  * praxis/kernels/nvfp4_moe.py:236-247 (EPI_RESCALE) fused. N, K % 128 == 0. */
+/* (A tile whose expert index is >= experts uses weights index % experts.) */
 int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf,
                              const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles,
                              int64_t rows_padded, int32_t n, int32_t k, int32_t experts, int32_t epilogue,
@@ -247,6 +248,46 @@ typedef struct praxis_b200_moe_args {
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,
                                       int32_t with_router);
 int praxis_b200_moe_forward(const praxis_b200_moe_args* args);
+
+/* Expert-rank half of an expert-parallel layer (no reference counterpart:
+ * the reference runs every expert on every GPU). Input: rows received from
+ * the source ranks, already NVFP4-quantized by each source with its own
+ * per-expert activation global scale, in padded segments: segment v
+ * (= source * experts + local expert; local expert v % experts) holds
+ * counts[v] rows from padded row starts[v] (multiples of 128, ascending,
+ * starts[segments] = rows). Runs gate/up GEMM + SwiGLU, hidden quantize with
+ * one global scale per segment (the reference's per-expert, per-dispatch-chunk
+ * scale when each source's batch is one chunk), down GEMM + rescale, and
+ * writes rows_out [rows, C] bf16 in the same layout for the return exchange.
+ * Weights are the rank's local experts in the kernel layouts of
+ * praxis_b200_moe_forward. */
+typedef struct praxis_b200_expert_args {
+  const void* q;              /* [rows, C/2] E2M1 */
+  const void* sf;             /* [rows, C/16] UE4M3, compact swizzled */
+  int64_t rows;
+  const int32_t* counts;      /* [segments] */
+  const int32_t* starts;      /* [segments + 1] */
+  const float* act_global;    /* [segments] */
+  int32_t segments;           /* <= 1024 */
+  const void* gate_up_q;
+  const void* gate_up_sf;
+  const float* gate_up_global;
+  const void* down_q;
+  const void* down_sf;
+  const float* down_global;
+  int32_t weight_sf_layout;   /* PRAXIS_B200_SF_* of gate_up_sf and down_sf */
+  int32_t dim;                /* C */
+  int32_t hidden;             /* F */
+  int32_t experts;            /* local experts */
+  void* rows_out;             /* [rows, C] bf16 */
+  void* workspace;
+  size_t workspace_size;
+  int device;
+  void* stream;
+} praxis_b200_expert_args;
+
+size_t praxis_b200_expert_workspace_size(int64_t rows, int32_t segments, int32_t dim, int32_t hidden);
+int praxis_b200_expert_forward(const praxis_b200_expert_args* args);
 
 /* Dispatch without a caller workspace: praxis_b200_dispatch with the same
  * arguments (minus workspace / workspace_size) and the same outputs, its

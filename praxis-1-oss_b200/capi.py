@@ -61,6 +61,35 @@ class MoeArgs(C.Structure):
     ]
 
 
+class ExpertArgs(C.Structure):
+    """``praxis_b200_expert_args``."""
+
+    _fields_ = [
+        ("q", P),
+        ("sf", P),
+        ("rows", I64),
+        ("counts", P),
+        ("starts", P),
+        ("act_global", P),
+        ("segments", I32),
+        ("gate_up_q", P),
+        ("gate_up_sf", P),
+        ("gate_up_global", P),
+        ("down_q", P),
+        ("down_sf", P),
+        ("down_global", P),
+        ("weight_sf_layout", I32),
+        ("dim", I32),
+        ("hidden", I32),
+        ("experts", I32),
+        ("rows_out", P),
+        ("workspace", P),
+        ("workspace_size", SZ),
+        ("device", C.c_int),
+        ("stream", P),
+    ]
+
+
 # name -> (restype, argtypes); the order and types follow the header.
 SIGNATURES: dict[str, tuple] = {
     "praxis_b200_abi_version": (C.c_int, []),
@@ -95,6 +124,8 @@ SIGNATURES: dict[str, tuple] = {
     "praxis_b200_interleave_gate_up": (C.c_int, [P, P, I32, I32, I32, P, P, C.c_int, P]),
     "praxis_b200_moe_workspace_size": (SZ, [I64, I32, I32, I32, I32, I32]),
     "praxis_b200_moe_forward": (C.c_int, [C.POINTER(MoeArgs)]),
+    "praxis_b200_expert_workspace_size": (SZ, [I64, I32, I32, I32]),
+    "praxis_b200_expert_forward": (C.c_int, [C.POINTER(ExpertArgs)]),
     "praxis_b200_dispatch_noalloc": (
         C.c_int,
         [P, P, P, I64, I32, I32, P, P, P, P, P, P, P, P, P, I32, P, P, P, C.c_int, P],

@@ -27,6 +27,8 @@ int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, cons
                       const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, int sf_layout,
                       cudaStream_t stream);
 int run_replicate_scales(const uint8_t* sf, int64_t rows, int k_dim, int group_rows, uint8_t* out, cudaStream_t stream);
+int run_segment_tiles(const int32_t* counts, const int32_t* starts, int segments, TileEntry* tiles, int max_tiles,
+                      int32_t* num_tiles, cudaStream_t stream);
 int run_pack_weights(const uint16_t* w, int experts, int k_dim, int n_dim, uint8_t* q, uint8_t* sf, float* global_out,
                      uint32_t* amax_scratch, cudaStream_t stream);
 int run_interleave_gate_up(const uint8_t* q, const uint8_t* sf, int experts, int f_dim, int c_dim, uint8_t* q_out,
@@ -154,6 +156,33 @@ static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int
   L.hsf = take((size_t)L.rp * hidden / 16 * 4);
   L.hsf_compact = take((size_t)L.rp * hidden / 16);
   L.rows = take((size_t)L.rp * dim * 2);
+  L.total = off;
+  return L;
+}
+
+// Workspace of the expert-rank forward (expert parallelism).
+struct ExpertLayout {
+  size_t tiles, num_tiles, h_amax, asf, hidden, hq, hsf_compact, hsf, total;
+  int max_tiles;
+};
+
+static ExpertLayout expert_layout(int64_t rows, int segments, int dim, int hidden) {
+  ExpertLayout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  L.max_tiles = (int)(rows / 128);
+  L.tiles = take((size_t)(2 * L.max_tiles + 1) * sizeof(TileEntry));
+  L.num_tiles = take(8);
+  L.h_amax = take((size_t)segments * 4);
+  L.asf = take((size_t)rows * dim / 16 * 4);
+  L.hidden = take((size_t)rows * hidden * 2);
+  L.hq = take((size_t)rows * hidden / 2);
+  L.hsf_compact = take((size_t)rows * hidden / 16);
+  L.hsf = take((size_t)rows * hidden / 16 * 4);
   L.total = off;
   return L;
 }
@@ -342,6 +371,67 @@ int praxis_b200_interleave_gate_up(const void* q, const void* sf, int32_t expert
   if (!q || !sf || !q_out || !sf_out) return set_error(PRAXIS_B200_EINVAL, "interleave: null pointer");
   return run_interleave_gate_up(static_cast<const uint8_t*>(q), static_cast<const uint8_t*>(sf), experts, hidden, dim,
                                 static_cast<uint8_t*>(q_out), static_cast<uint8_t*>(sf_out), PRAXIS_STREAM(stream));
+}
+
+size_t praxis_b200_expert_workspace_size(int64_t rows, int32_t segments, int32_t dim, int32_t hidden) {
+  return expert_layout(rows, segments, dim, hidden).total;
+}
+
+int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
+  if (!a) return set_error(PRAXIS_B200_EINVAL, "expert_forward: null args");
+  PRAXIS_DEVICE_OR_RETURN(a->device);
+  if (!a->counts || !a->starts || !a->act_global || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
+      !a->down_q || !a->down_sf || !a->down_global || !a->rows_out || !a->workspace)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: null pointer");
+  if (a->rows < 0 || a->rows % 128 || a->segments < 1 || a->segments > 1024 || a->experts < 1 || a->dim <= 0 ||
+      a->hidden <= 0)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: bad sizes");
+  if (a->dim % 128 || a->hidden % 128)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: C and F must be multiples of 128");
+  const int sf_layout = a->weight_sf_layout;
+  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: unknown weight scale layout %d", sf_layout);
+  if (sf_layout == PRAXIS_B200_SF_REPLICATED && a->dim % 256 != 0)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: replicated scales need C % 256 == 0");
+  if (a->rows * (int64_t)(a->dim > 2 * a->hidden ? a->dim : 2 * a->hidden) >= ((int64_t)1 << 31) * 8)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: rows exceed the kernels' indexing range");
+  const ExpertLayout L = expert_layout(a->rows, a->segments, a->dim, a->hidden);
+  if (a->workspace_size < L.total)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: workspace %zu < %zu bytes", a->workspace_size, L.total);
+  if (a->rows == 0) return PRAXIS_B200_OK;
+  if (!a->q || !a->sf) return set_error(PRAXIS_B200_EINVAL, "expert_forward: null rows");
+  cudaStream_t s = PRAXIS_STREAM(a->stream);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  TileEntry* tiles = reinterpret_cast<TileEntry*>(ws + L.tiles);
+  int32_t* num_tiles = reinterpret_cast<int32_t*>(ws + L.num_tiles);
+  uint32_t* h_amax = reinterpret_cast<uint32_t*>(ws + L.h_amax);
+  uint16_t* hidden = reinterpret_cast<uint16_t*>(ws + L.hidden);
+  uint8_t* hq = ws + L.hq;
+  const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
+  int rc = run_segment_tiles(a->counts, a->starts, a->segments, tiles, L.max_tiles, num_tiles, s);
+  if (rc) return rc;
+  const uint8_t* asf = static_cast<const uint8_t*>(a->sf);
+  if (rep) {
+    rc = run_replicate_scales(asf, a->rows, a->dim, 128, ws + L.asf, s);
+    if (rc) return rc;
+    asf = ws + L.asf;
+  }
+  cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * a->segments, s);
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
+  rc = run_grouped_gemm(a->q, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, a->rows,
+                        2 * a->hidden, a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, a->act_global, nullptr,
+                        a->gate_up_global, h_amax, sf_layout, s);
+  if (rc) return rc;
+  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
+                         rep ? ws + L.hsf_compact : ws + L.hsf, PRAXIS_B200_SF_COMPACT, s);
+  if (rc) return rc;
+  if (rep) {
+    rc = run_replicate_scales(ws + L.hsf_compact, a->rows, a->hidden, 128, ws + L.hsf, s);
+    if (rc) return rc;
+  }
+  return run_grouped_gemm(hq, ws + L.hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, a->rows, a->dim,
+                          a->hidden, a->experts, EPI_RESCALE, static_cast<uint16_t*>(a->rows_out), a->dim, nullptr,
+                          h_amax, a->down_global, nullptr, sf_layout, s);
 }
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,

@@ -239,6 +239,61 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Tile tables of received segments (expert parallelism): segment v holds
+// counts[v] routed rows from padded row starts[v] (128-aligned); the 128-row
+// tiles and 256-row pairs are laid out as by the dispatch, with v as the
+// tile's expert. One CTA of 1024 threads, segments <= 1024.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) segment_tiles_kernel(const int32_t* __restrict__ counts,
+                                                             const int32_t* __restrict__ starts, int segments,
+                                                             TileEntry* __restrict__ tiles, int max_tiles,
+                                                             int32_t* __restrict__ num_tiles) {
+  __shared__ int s_warp[32];
+  const int v = threadIdx.x;
+  const int count = v < segments ? max(counts[v], 0) : 0;
+  const int64_t row0 = v < segments ? starts[v] : 0;
+  const int ntile = (count + kTileRows - 1) / kTileRows;
+  int tiles_total = 0;
+  const int tstart = block_exclusive_scan(ntile, s_warp, &tiles_total);
+  for (int j = 0; j < ntile; ++j) {
+    if (tstart + j < max_tiles) {
+      TileEntry t;
+      t.expert = v;
+      t.row0 = (int32_t)(row0 + (int64_t)j * kTileRows);
+      t.valid = min(kTileRows, count - j * kTileRows);
+      t.pad = 0;
+      tiles[tstart + j] = t;
+    } else {
+      record_error(kErrIndexRange);
+    }
+  }
+  const int npair = (count + 2 * kTileRows - 1) / (2 * kTileRows);
+  int pairs_total = 0;
+  const int pstart = block_exclusive_scan(npair, s_warp, &pairs_total);
+  for (int j = 0; j < npair; ++j) {
+    if (pstart + j < max_tiles) {
+      TileEntry t;
+      t.expert = v;
+      t.row0 = (int32_t)(row0 + (int64_t)j * 2 * kTileRows);
+      t.valid = min(2 * kTileRows, count - j * 2 * kTileRows);
+      t.pad = min(2 * kTileRows, ntile * kTileRows - j * 2 * kTileRows);
+      tiles[max_tiles + pstart + j] = t;
+    }
+  }
+  if (threadIdx.x == 0) {
+    num_tiles[0] = min(tiles_total, max_tiles);
+    num_tiles[1] = min(pairs_total, max_tiles);
+  }
+}
+
+int run_segment_tiles(const int32_t* counts, const int32_t* starts, int segments, TileEntry* tiles, int max_tiles,
+                      int32_t* num_tiles, cudaStream_t stream) {
+  if (segments < 1 || segments > 1024) return set_error(PRAXIS_B200_EINVAL, "segments must be 1..1024");
+  segment_tiles_kernel<<<1, 1024, 0, stream>>>(counts, starts, segments, tiles, max_tiles, num_tiles);
+  return check_launch("segment_tiles");
+}
+
+// ---------------------------------------------------------------------------
 // 3. scatter
 // ---------------------------------------------------------------------------
 __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate,

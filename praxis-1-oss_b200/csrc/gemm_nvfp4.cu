@@ -51,6 +51,13 @@ __device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&
     d[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
 }
 
+// Tile expert e reads weights e % weight_experts: one expert per tile on a
+// single GPU; with expert parallelism a tile's "expert" is a segment
+// (source rank, local expert) whose activation scales are its own.
+__device__ __forceinline__ int weight_expert(const GemmParams& p, int e) {
+  return e < p.weight_experts ? e : e % p.weight_experts;
+}
+
 __device__ __forceinline__ float expert_multiplier(const GemmParams& p, int e) {
   // bf16(g_a * g_w) in float32 (praxis/kernels/nvfp4_moe.py:117-121, :237-241)
   float ga;
@@ -59,7 +66,7 @@ __device__ __forceinline__ float expert_multiplier(const GemmParams& p, int e) {
   } else {
     ga = global_from_amax_bits(p.act_amax[e]);
   }
-  return bf16_round(mul_rn(ga, p.w_global[e]));
+  return bf16_round(mul_rn(ga, p.w_global[weight_expert(p, e)]));
 }
 
 template <int BLOCK_N, int EPI>
@@ -119,10 +126,11 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
         const TileEntry t = p.tiles[m];
-        const int brow = t.expert * p.N + n * BLOCK_N;
+        const int we = weight_expert(p, t.expert);
+        const int brow = we * p.N + n * BLOCK_N;
         const uint8_t* sfa = p.sfa + (size_t)(t.row0 / 128) * kb_total * S::SF_ATOM;
         const uint8_t* sfb =
-            p.sfb + ((size_t)t.expert * (p.N / 128) + (size_t)n * (BLOCK_N / 128)) * kb_total * S::SF_ATOM;
+            p.sfb + ((size_t)we * (p.N / 128) + (size_t)n * (BLOCK_N / 128)) * kb_total * S::SF_ATOM;
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) {
             ok = false;
@@ -395,11 +403,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
         const int m = u / n_tiles, n = u - (u / n_tiles) * n_tiles;
         const TileEntry t = pairs[m];
         const int a_row = t.row0 + 128 * (int)rank;
-        const int b_row = t.expert * p.N + n * S::BN + 128 * (int)rank;
+        const int we = weight_expert(p, t.expert);
+        const int b_row = we * p.N + n * S::BN + 128 * (int)rank;
         // scale atoms as 256-byte rows (2 per 512-byte atom)
         const int sfa_row = ((t.row0 / 128 + (int)rank) * kb_total) * 2 * S::SF_COPIES;
         const int sfb_row0 =
-            REP ? ((t.expert * (p.N / 256) + n) * kb_total) * 16 : ((t.expert * (p.N / 128) + n * 2) * kb_total) * 2;
+            REP ? ((we * (p.N / 256) + n) * kb_total) * 16 : ((we * (p.N / 128) + n * 2) * kb_total) * 2;
         const int sfb_row1 = sfb_row0 + kb_total * 2;
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) {
@@ -726,6 +735,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
                      cudaStream_t stream) {
   if (n % 128 != 0 || k % 128 != 0 || n <= 0 || k <= 0)
     return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs N and K multiples of 128 (N=%d K=%d)", n, k);
+  if (experts < 1) return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs at least one expert");
   if (max_tiles < 0 || rows_padded < (int64_t)max_tiles * 128)
     return set_error(PRAXIS_B200_EINVAL, "tile table larger than the padded rows");
   if (epilogue == EPI_SWIGLU && (out_cols * 2 != n || amax_out == nullptr || w_global == nullptr))
@@ -762,6 +772,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.w_global = w_global;
   p.amax_out = amax_out;
   p.max_tiles = max_tiles;
+  p.weight_experts = experts;
   const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
   if (n % 256 == 0 && (rep || gemm_variant() == 0)) {
     const size_t copies = rep ? 4 : 1;

@@ -32,6 +32,7 @@ struct GemmParams {
   const uint32_t* act_amax;
   const float* w_global;
   uint32_t* amax_out;
+  int32_t weight_experts;  // tile expert e uses weights e % weight_experts
 };
 
 // Records a message for praxis_b200_last_error and returns `code`.

@@ -324,6 +324,40 @@ def interleave_gate_up(q: Tensor, sf: Tensor) -> tuple[Tensor, Tensor]:
     return qo, so
 
 
+def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
+                   gate_up_q: Tensor, gate_up_sf: Tensor, gate_up_global: Tensor, down_q: Tensor,
+                   down_sf: Tensor, down_global: Tensor, *, weight_sf_layout: int) -> Tensor:
+    """The expert-rank half of an expert-parallel layer
+    (``praxis_b200_expert_forward``): received NVFP4 rows in padded segments
+    (segment v = source * E_local + local expert, ``counts[v]`` rows from
+    ``starts[v]``) -> rescaled bf16 down-projection rows in the same layout."""
+    _need(q, "q", torch.uint8, 2)
+    rows, c_half = q.shape
+    c = c_half * 2
+    f = down_q.shape[2] * 2
+    e_local = down_q.shape[0]
+    segments = counts.numel()
+    _need(counts, "counts", torch.int32, 1, q.device)
+    _need(starts, "starts", torch.int32, 1, q.device)
+    _need(act_global, "act_global", torch.float32, 1, q.device)
+    if starts.numel() != segments + 1 or act_global.numel() != segments:
+        raise ValueError("starts / act_global do not match the segment count")
+    out = torch.empty(rows, c, dtype=BF16, device=q.device)
+    lib = capi.load()
+    ws_size = int(lib.praxis_b200_expert_workspace_size(rows, segments, c, f))
+    ws = torch.empty(max(ws_size, 1), dtype=torch.uint8, device=q.device)
+    args = capi.ExpertArgs(
+        q=q.data_ptr(), sf=sf.data_ptr(), rows=rows, counts=counts.data_ptr(), starts=starts.data_ptr(),
+        act_global=act_global.data_ptr(), segments=segments, gate_up_q=gate_up_q.data_ptr(),
+        gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(), down_q=down_q.data_ptr(),
+        down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(), weight_sf_layout=int(weight_sf_layout),
+        dim=c, hidden=f, experts=e_local, rows_out=out.data_ptr(), workspace=ws.data_ptr(),
+        workspace_size=ws.numel(), device=_dev(q), stream=torch.cuda.current_stream(q.device).cuda_stream,
+    )
+    capi.check(lib.praxis_b200_expert_forward(C.byref(args)))
+    return out
+
+
 def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_q: Tensor, gate_up_sf: Tensor,
                 gate_up_global: Tensor, down_q: Tensor, down_sf: Tensor, down_global: Tensor, scaling: float,
                 shared: Tensor | None = None, *, router_terms: Tensor | None = None,

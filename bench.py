@@ -41,6 +41,8 @@ CONFIGS = {
     "1": dict(tokens=256, dim=512, experts=8, top_k=2, hidden=1024, skew=False),
     "2": dict(tokens=16384, dim=3072, experts=64, top_k=4, hidden=1536, skew=False),
     "3": dict(tokens=16384, dim=3072, experts=64, top_k=4, hidden=1536, skew=True),
+    # expert parallel over N GPUs: tokens per rank (weak scaling)
+    "4": dict(tokens=65536, dim=3072, experts=64, top_k=4, hidden=1536, skew=False),
     "5": dict(tokens=512, dim=1024, experts=32, top_k=2, hidden=2048, skew=False),
     "ckpt": dict(tokens=16384, dim=3072, experts=128, top_k=8, hidden=1280, skew=False),
 }
@@ -53,7 +55,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default=None, choices=sorted(CONFIGS),
+                    help="default: 2 on one GPU, 4 (expert parallel) on several")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
@@ -331,6 +334,147 @@ def run_b200(args, cfg):
         dist.destroy_process_group()
 
 
+def run_expert_parallel(args, cfg):
+    """N > 1: the layer expert-parallel over the N GPUs of one node (config 4:
+    each rank routes its own tokens; experts sharded 64/N per rank; NVFP4 rows
+    and scales out, bf16 rows back over NCCL all-to-all)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    pkg = importlib.import_module("praxis-1-oss_b200")
+    pkg.capi.load()
+    ops = pkg.ops
+    peaks = {}
+    pfile = ROOT / "MEASURED_PEAKS.json"
+    if pfile.exists():
+        peaks = json.loads(pfile.read_text())
+    t, c, e, k, f = cfg["tokens"], cfg["dim"], cfg["experts"], cfg["top_k"], cfg["hidden"]
+    if e % world:
+        raise SystemExit(f"{e} experts do not shard over {world} ranks")
+    el = e // world
+    # tokens seeded per rank; the same weights on every rank (the full bank is
+    # generated from one seed, each rank packs its own experts)
+    x_cpu, router, bias, _gu, _dn = make_inputs(dict(cfg, experts=0), 1000 + rank, dev)
+    gw = torch.Generator(device=dev).manual_seed(7)
+    gu = (torch.randn(e, c, 2 * f, generator=gw, device=dev) * 0.02).to(torch.bfloat16)[rank * el:(rank + 1) * el]
+    down = (torch.randn(e, f, c, generator=gw, device=dev) * 0.02).to(torch.bfloat16)[rank * el:(rank + 1) * el]
+    bank = pkg.pack_routed_experts(gu.contiguous(), down.contiguous(), keep_on_device=True)
+    del gu, down
+    bank.prepare()
+    ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e)
+    grouter = torch.Generator().manual_seed(11)
+    router = (torch.randn(e, c, generator=grouter) * (1.0 / c) ** 0.5).to(dev)
+    terms = ops.split_router_weight(router)
+    bias = torch.zeros(e, device=dev)
+    x = x_cpu.to(dev)
+
+    def step(inp=None):
+        xin = x if inp is None else inp
+        logits, _amax = ops.router_logits(xin, terms)
+        top, gate = ops.route(logits, bias, k)
+        return ep.routed_forward(xin, top, gate, scaling=2.5)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    tt = torch.tensor([ms], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    value = t * world / (ms / 1e3)
+
+    # expert-rank compute of one exchange, timed alone (both GEMMs and the
+    # hidden quantize on the rows this rank received)
+    be = ep._backend
+    routing = be.route_rows(x, *ops.route(ops.router_logits(x, terms)[0], bias, k), e)
+    q, sf = be.quantize(x, routing)
+    pc = routing.pcsr.cpu().long()
+    rows_here = int(pc[-1])
+    cnt = (routing.csr[1:] - routing.csr[:-1]).to(torch.int32)
+    starts = routing.pcsr[:-1].to(torch.int32)
+    # (every expert's rows of this rank's tokens through the local weights:
+    # the same FLOPs as the rank's share of the layer)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    be.experts(q[:rows_here], sf[:rows_here], cnt, torch.cat([starts, routing.pcsr[-1:]]).to(torch.int32),
+               routing.act_global)
+    torch.cuda.synchronize()
+    evs[0].record(stream)
+    be.experts(q[:rows_here], sf[:rows_here], cnt, torch.cat([starts, routing.pcsr[-1:]]).to(torch.int32),
+               routing.act_global)
+    evs[1].record(stream)
+    torch.cuda.synchronize()
+    exp_ms = evs[0].elapsed_time(evs[1])
+    flops = 6.0 * t * k * c * f
+    fp4_peak = 4.0 * float(peaks.get("bf16_tflops", 1590.0))
+    roofline = {"bound": "tensor", "kernel": "expert_forward (gate/up GEMM + SwiGLU, hidden quantize, down GEMM)",
+                "achieved": flops / (exp_ms / 1e3) / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
+                "frac": flops / (exp_ms / 1e3) / 1e12 / fp4_peak, "traffic": None,
+                "peak_note": "4 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json); rows of this rank's own tokens "
+                             "through its local experts' weights, one launch sequence"}
+    e2e = None
+    if not args.no_e2e:
+        host_in = x_cpu.pin_memory()
+        host_out = torch.empty(t, c, dtype=torch.bfloat16).pin_memory()
+        xin = torch.empty_like(x)
+        for _ in range(2):
+            xin.copy_(host_in, non_blocking=True)
+            host_out.copy_(step(xin), non_blocking=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            xin.copy_(host_in, non_blocking=True)
+            host_out.copy_(step(xin), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1) / args.steps
+        te = torch.tensor([ems], device=dev)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        ems = float(te.item())
+        e2e = {"value": t * world / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": host_in.numel() * 2 * world, "d2h_bytes_per_step": host_out.numel() * 2 * world}
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 block16 scales, fp32 accumulate), bf16 I/O",
+        "data": "synthetic (seeded N(0,1) activations per rank, N(0,0.02) expert weights packed to NVFP4)",
+        "config": {"workload": f"BASELINE config {args.config}: expert-parallel MoE layer forward incl. router",
+                   "tokens_per_rank": t, "dim": c, "experts": e, "experts_per_rank": el, "top_k": k,
+                   "expert_hidden": f, "router": "sigmoid+renorm", "parallelism": f"ep{world}",
+                   "exchange": "NCCL all-to-all: FP4 rows + UE4M3 scales out, bf16 rows back",
+                   "l2": "per-rank inputs and weights exceed the 126 MB L2; no flush"},
+        "layer_tflops": flops * world / (ms / 1e3) / 1e12,
+        "roofline": roofline,
+        "clocks": clk.summary(),
+        # router 2, row max 1, dispatch 3, quantize 1, tiles 1, scale replication 2, GEMM 2, hidden quantize 1,
+        # combine 1 (NCCL's own kernels not counted)
+        "gpu_launches": 14 * args.steps,
+        "e2e": e2e,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
     import torch
 
@@ -416,11 +560,15 @@ def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
+    if args.config is None:
+        args.config = "4" if dist_env()[1] > 1 else "2"
     cfg = dict(CONFIGS[args.config])
     if args.tokens is not None:
         cfg["tokens"] = args.tokens
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif dist_env()[1] > 1:
+        run_expert_parallel(args, cfg)
     else:
         run_b200(args, cfg)
 

@@ -260,10 +260,13 @@ def run_b200(args, cfg):
     out = torch.empty_like(x)
     ops = pkg.ops
 
-    def step():
-        return ops.moe_forward(x, None, None, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
+    def layer(xin, yout):
+        return ops.moe_forward(xin, None, None, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
                                kw.down_sf, bank.down_global, 2.5, router_terms=terms, router_bias=mod.expert_bias,
-                               top_k=k, out=out, weight_sf_layout=kw.sf_layout)
+                               top_k=k, out=yout, weight_sf_layout=kw.sf_layout)
+
+    def step():
+        return layer(x, out)
 
     # correctness guard of the measured path: routing and output vs the
     # stage-by-stage ops path (same kernels, separate launches)
@@ -308,7 +311,7 @@ def run_b200(args, cfg):
     layer_flops = 6.0 * t * k * c * f
     e2e = None
     if not args.no_e2e:
-        e2e = time_e2e(step, x, x_cpu, out, args, dev, t, world)
+        e2e = time_e2e(pkg, layer, x_cpu, out, args, dev, t, world)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -524,26 +527,22 @@ def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
     return {n: v / reps for n, v in acc.items()}
 
 
-def time_e2e(step, x, x_cpu, out, args, dev, t, world):
-    """Same metric through the public API with host buffers: each step
-    copies its input from pinned host memory and reads the output back."""
+def time_e2e(pkg, layer, x_cpu, out, args, dev, t, world):
+    """Same metric through the public API with host buffers: every step
+    copies its input from pinned host memory and reads the whole output back
+    (praxis_b200.pipeline.HostPipeline: the copies of neighbouring steps
+    overlap the compute on their own streams)."""
     import torch
 
     host_in = x_cpu.pin_memory()
     host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    stream = torch.cuda.current_stream(dev)
-    for _ in range(2):
-        x.copy_(host_in, non_blocking=True)
-        step()
-        host_out.copy_(out, non_blocking=True)
+    pipe = pkg.pipeline.HostPipeline(layer, x_cpu.shape, out.shape, out.dtype, dev)
+    pipe.run([host_in] * 2, [host_out] * 2)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        x.copy_(host_in, non_blocking=True)
-        step()
-        host_out.copy_(out, non_blocking=True)
-    e1.record(stream)
+    e0.record(pipe.copy_in)
+    pipe.run([host_in] * args.steps, [host_out] * args.steps)
+    e1.record(pipe.copy_out)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     if world > 1:

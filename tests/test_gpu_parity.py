@@ -478,3 +478,28 @@ def test_cuda_graph_replay_matches_eager(P):
     torch.cuda.synchronize()
     assert_bytes_equal(out, bank.routed_forward(x, top, gate, scaling=2.5, chunk_size=t))
     del graph
+
+
+def test_host_pipeline_matches_direct_calls(P):
+    t, c, e, k, f = 256, 512, 8, 2, 1024
+    gu, down = make_bank(e, c, f, seed=51)
+    bank = P.pack_routed_experts(gu.to(DEV), down.to(DEV), keep_on_device=True)
+    bank.prepare()
+    kw = bank.kernel_weights()
+    top, gate = random_routing(t, e, k, seed=52)
+    top, gate = top.to(DEV), gate.to(DEV)
+
+    def layer(xin, yout):
+        P.ops.moe_forward(xin, top, gate, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
+                          kw.down_sf, bank.down_global, 2.5, out=yout, weight_sf_layout=kw.sf_layout)
+
+    g = gen(53)
+    host_in = [torch.randn(t, c, generator=g).to(torch.bfloat16).pin_memory() for _ in range(5)]
+    host_out = [torch.empty(t, c, dtype=torch.bfloat16).pin_memory() for _ in range(5)]
+    pipe = P.pipeline.HostPipeline(layer, (t, c), (t, c), torch.bfloat16, torch.device(DEV))
+    pipe.run(host_in, host_out)
+    torch.cuda.synchronize()
+    for hi, ho in zip(host_in, host_out):
+        want = torch.empty(t, c, dtype=torch.bfloat16, device=DEV)
+        layer(hi.to(DEV), want)
+        assert torch.equal(ho.view(torch.int16), want.cpu().view(torch.int16))

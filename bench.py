@@ -24,6 +24,7 @@ bounded sample of tokens of the same layer; rank 0 only.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import importlib
 import json
 import os
@@ -90,7 +91,8 @@ def make_inputs(cfg, seed, device):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """nvidia-smi clocks and throttle reasons during the timed region (index
+    None: every GPU of the node from one process)."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -103,8 +105,9 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", *(["-i", str(self.index)] if self.index is not None else []),
+                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
@@ -390,7 +393,9 @@ def run_expert_parallel(args, cfg):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
+    # one sampler process for the node (rank 0), not one per rank
+    clk = ClockSampler(None) if rank == 0 else None
+    with clk if clk is not None else contextlib.nullcontext():
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -416,11 +421,11 @@ def run_expert_parallel(args, cfg):
     # the same FLOPs as the rank's share of the layer)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     be.experts(q[:rows_here], sf[:rows_here], cnt, torch.cat([starts, routing.pcsr[-1:]]).to(torch.int32),
-               routing.act_global)
+               routing.act_global, 0, el)
     torch.cuda.synchronize()
     evs[0].record(stream)
     be.experts(q[:rows_here], sf[:rows_here], cnt, torch.cat([starts, routing.pcsr[-1:]]).to(torch.int32),
-               routing.act_global)
+               routing.act_global, 0, el)
     evs[1].record(stream)
     torch.cuda.synchronize()
     exp_ms = evs[0].elapsed_time(evs[1])
@@ -466,7 +471,7 @@ def run_expert_parallel(args, cfg):
                    "l2": "per-rank inputs and weights exceed the 126 MB L2; no flush"},
         "layer_tflops": flops * world / (ms / 1e3) / 1e12,
         "roofline": roofline,
-        "clocks": clk.summary(),
+        "clocks": clk.summary() if clk is not None else None,
         # router 2, row max 1, dispatch 3, quantize 1, tiles 1, scale replication 2, GEMM 2, hidden quantize 1,
         # combine 1 (NCCL's own kernels not counted)
         "gpu_launches": 14 * args.steps,

@@ -279,6 +279,8 @@ typedef struct praxis_b200_expert_args {
   int32_t dim;                /* C */
   int32_t hidden;             /* F */
   int32_t experts;            /* local experts */
+  int32_t sm_limit;           /* GEMMs on at most this many SMs (0: all), leaving the rest to
+                                 concurrent transfer kernels */
   void* rows_out;             /* [rows, C] bf16 */
   void* workspace;
   size_t workspace_size;

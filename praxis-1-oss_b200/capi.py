@@ -82,6 +82,7 @@ class ExpertArgs(C.Structure):
         ("dim", I32),
         ("hidden", I32),
         ("experts", I32),
+        ("sm_limit", I32),
         ("rows_out", P),
         ("workspace", P),
         ("workspace_size", SZ),

@@ -384,7 +384,7 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
       !a->down_q || !a->down_sf || !a->down_global || !a->rows_out || !a->workspace)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: null pointer");
   if (a->rows < 0 || a->rows % 128 || a->segments < 1 || a->segments > 1024 || a->experts < 1 || a->dim <= 0 ||
-      a->hidden <= 0)
+      a->hidden <= 0 || a->sm_limit < 0)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: bad sizes");
   if (a->dim % 128 || a->hidden % 128)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: C and F must be multiples of 128");
@@ -420,7 +420,7 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(a->q, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, a->rows,
                         2 * a->hidden, a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, a->act_global, nullptr,
-                        a->gate_up_global, h_amax, sf_layout, s);
+                        a->gate_up_global, h_amax, sf_layout, s, a->sm_limit);
   if (rc) return rc;
   rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
                          rep ? ws + L.hsf_compact : ws + L.hsf, PRAXIS_B200_SF_COMPACT, s);
@@ -431,7 +431,7 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
   }
   return run_grouped_gemm(hq, ws + L.hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, a->rows, a->dim,
                           a->hidden, a->experts, EPI_RESCALE, static_cast<uint16_t*>(a->rows_out), a->dim, nullptr,
-                          h_amax, a->down_global, nullptr, sf_layout, s);
+                          h_amax, a->down_global, nullptr, sf_layout, s, a->sm_limit);
 }
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,

@@ -637,7 +637,8 @@ static int launch_gemm(const GemmParams& p, int max_tiles, cudaStream_t stream) 
   }
   const int units = max_tiles * (p.N / BLOCK_N);
   if (units <= 0) return PRAXIS_B200_OK;
-  const int grid = units < sm_count() ? units : sm_count();
+  int grid = units < sm_count() ? units : sm_count();
+  if (p.sm_limit > 0 && grid > p.sm_limit) grid = p.sm_limit;
   kernel<<<grid, 192, S::SMEM_BYTES, stream>>>(p);
   return check_launch("gemm_nvfp4");
 }
@@ -711,7 +712,8 @@ static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t str
   }
   const int units = max_tiles * (p.N / S::BN);
   if (units <= 0) return PRAXIS_B200_OK;
-  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  if (p.sm_limit > 0 && clusters > p.sm_limit / 2) clusters = p.sm_limit / 2 > 0 ? p.sm_limit / 2 : 1;
   kernel<<<2 * clusters, S::THREADS, S::SMEM_BYTES, stream>>>(p);
   return check_launch("gemm_nvfp4_pair");
 }
@@ -732,7 +734,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
                      const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int sm_limit) {
   if (n % 128 != 0 || k % 128 != 0 || n <= 0 || k <= 0)
     return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs N and K multiples of 128 (N=%d K=%d)", n, k);
   if (experts < 1) return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs at least one expert");
@@ -773,6 +775,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.amax_out = amax_out;
   p.max_tiles = max_tiles;
   p.weight_experts = experts;
+  p.sm_limit = sm_limit;
   const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
   if (n % 256 == 0 && (rep || gemm_variant() == 0)) {
     const size_t copies = rep ? 4 : 1;

@@ -11,15 +11,19 @@ rank (its own tokens are one dispatch chunk):
 2. NVFP4 quantization of the outbound rows on the source rank;
 3. exchange of the per-(destination, expert) counts, padded offsets and
    global scales (one small all-to-all), then of the FP4 rows and their
-   compact scale atoms: destination d receives rows
-   [pcsr[d * E/R], pcsr[(d + 1) * E/R]) of every source, whole 128-row tiles,
-   so the swizzled scale atoms travel as contiguous bytes;
-4. on the expert rank: gate/up GEMM + SwiGLU, hidden quantize with one global
-   scale per (source, expert) segment, down GEMM + rescale
+   compact scale atoms (one batch of point-to-point transfers): destination
+   d receives rows [pcsr[d * E/R], pcsr[(d + 1) * E/R]) of every source,
+   whole 128-row tiles, so the swizzled scale atoms travel as contiguous
+   bytes; the rank's own rows for its own experts do not move and are
+   computed while the transfers run;
+4. on the expert rank, per source: gate/up GEMM + SwiGLU, hidden quantize with
+   one global scale per (source, expert) segment, down GEMM + rescale
    (``praxis_b200_expert_forward``);
-5. the bf16 rows travel back (the reverse all-to-all) into the source's own
-   padded layout, and the source combines its tokens with the reference's
-   four-accumulator order.
+5. the bf16 rows travel back into the source's own padded layout: sources
+   are taken in rotating order (step j: compute for rank + j, receive from
+   rank - j), so each return transfer overlaps the next source's compute;
+   the source combines its tokens with the reference's four-accumulator
+   order.
 
 Every row meets the same arithmetic as on one GPU, so a rank's output equals
 the single-GPU layer on that rank's tokens bit for bit. The exchange step
@@ -52,10 +56,14 @@ def shard_packed_state(state: Mapping[str, Tensor], rank: int, world: int) -> di
 
 
 class CudaBackend:
-    """The compute steps on this library's sm_100a kernels."""
+    """The compute steps on this library's sm_100a kernels. ``transfer_sms``
+    SMs are left out of the expert GEMMs' persistent grids so that the
+    transfer kernels of the exchange run beside them."""
 
-    def __init__(self, bank: B200NVFP4RoutedExperts) -> None:
+    def __init__(self, bank: B200NVFP4RoutedExperts, transfer_sms: int = 16) -> None:
         self.bank = bank
+        props = torch.cuda.get_device_properties(bank.gate_up_q.device)
+        self.sm_limit = max(2, props.multi_processor_count - transfer_sms) if transfer_sms > 0 else 0
 
     def route_rows(self, x: Tensor, top_idx: Tensor, gate: Tensor, num_experts: int):
         return ops.dispatch(top_idx, gate, num_experts, ops.row_amax(x), full=False)
@@ -63,20 +71,31 @@ class CudaBackend:
     def quantize(self, x: Tensor, routing) -> tuple[Tensor, Tensor]:
         return ops.quantize_gather(x, routing, routing.act_global)
 
-    def experts(self, q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor) -> Tensor:
+    def experts(self, q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
+                first: int, last: int) -> Tensor:
+        """Segments of local experts [first, last) (segment v: expert first + v % (last - first))."""
         kw = self.bank.kernel_weights()
         b = self.bank
-        return ops.expert_forward(q, sf, counts, starts, act_global, kw.gate_up_q, kw.gate_up_sf, b.gate_up_global,
-                                  b.down_q, kw.down_sf, b.down_global, weight_sf_layout=kw.sf_layout)
+        n = b.num_experts
+
+        def part(t: Tensor) -> Tensor:  # experts [first, last) of a per-expert buffer (flat when replicated)
+            return t[first:last] if t.dim() > 1 else t.view(n, -1)[first:last].reshape(-1)
+
+        return ops.expert_forward(q, sf, counts, starts, act_global, part(kw.gate_up_q), part(kw.gate_up_sf),
+                                  b.gate_up_global[first:last], part(b.down_q), part(kw.down_sf),
+                                  b.down_global[first:last], weight_sf_layout=kw.sf_layout, sm_limit=self.sm_limit)
 
     def combine(self, rows: Tensor, routing, scaling: float, shared: Tensor | None) -> Tensor:
         return ops.combine(rows, routing, scaling, rows_rescaled=True, shared=shared)
 
 
 def exchange_forward(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: int, scaling: float,
-                     backend, group=None, shared: Tensor | None = None) -> Tensor:
+                     backend, group=None, shared: Tensor | None = None, chunks: int | None = None) -> Tensor:
     """One expert-parallel layer forward of this rank's tokens (see the module
-    docstring). Every rank of ``group`` must call it the same number of times."""
+    docstring). Every rank of ``group`` must call it the same number of times
+    with the same ``chunks`` (expert groups per source for the return
+    pipeline; default 1: on 2 GPUs the split launches cost more than the
+    overlap wins)."""
     world = dist.get_world_size(group)
     e_local = num_experts // world
     if e_local * world != num_experts:
@@ -102,33 +121,88 @@ def exchange_forward(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: i
     sizes = torch.stack([block.squeeze(1), meta_recv[:, -1].to(torch.int64)]).cpu()
     send_rows = sizes[0].tolist()
     recv_rows = sizes[1].tolist()
-    total_send, total_recv = sum(send_rows), sum(recv_rows)
+    rank = dist.get_rank(group)
+    peer = [dist.get_global_rank(group, i) if group is not None else i for i in range(world)]
+    lo = [int(v) for v in bounds.cpu().tolist()]
 
-    q_recv = _exchange_rows(q[:total_send], total_recv, recv_rows, send_rows, group)
-    sf_recv = _exchange_rows(sf[:total_send], total_recv, recv_rows, send_rows, group)
+    # outbound rows and scale atoms of every other rank, as one batch
+    recv_q: list[Tensor | None] = [None] * world
+    recv_sf: list[Tensor | None] = [None] * world
+    p2p = []
+    for s in range(world):
+        if s == rank or recv_rows[s] == 0:
+            continue
+        recv_q[s] = torch.empty(recv_rows[s], q.shape[1], dtype=q.dtype, device=dev)
+        recv_sf[s] = torch.empty(recv_rows[s], sf.shape[1], dtype=sf.dtype, device=dev)
+        p2p += [dist.P2POp(dist.irecv, recv_q[s].view(torch.uint8), peer[s], group),
+                dist.P2POp(dist.irecv, recv_sf[s].view(torch.uint8), peer[s], group)]
+    for d in range(world):
+        if d == rank or send_rows[d] == 0:
+            continue
+        p2p += [dist.P2POp(dist.isend, q[lo[d]:lo[d + 1]].contiguous().view(torch.uint8), peer[d], group),
+                dist.P2POp(dist.isend, sf[lo[d]:lo[d + 1]].contiguous().view(torch.uint8), peer[d], group)]
+    outbound = dist.batch_isend_irecv(p2p) if p2p else []
 
-    # received segments: source s, local expert e -> segment s * e_local + e
-    base = torch.zeros(world, dtype=torch.int64)
-    if world > 1:
-        base[1:] = torch.tensor(recv_rows[:-1], dtype=torch.int64).cumsum(0)
-    base = base.to(dev)
-    seg_counts = meta_recv[:, :e_local].reshape(-1).contiguous()
-    seg_starts = torch.cat([(base.unsqueeze(1) + meta_recv[:, e_local:2 * e_local].to(torch.int64)).reshape(-1),
-                            torch.tensor([total_recv], dtype=torch.int64, device=dev)]).to(torch.int32)
-    seg_global = meta_recv[:, 2 * e_local:3 * e_local].reshape(-1).contiguous().view(torch.float32)
-    rows_out = backend.experts(q_recv, sf_recv, seg_counts, seg_starts, seg_global)
+    rows_back = torch.empty(lo[world], x.shape[1], dtype=torch.bfloat16, device=dev)
+    chunks = max(1, min(e_local, chunks or 1))
+    # every source's segments in one go: counts, starts (relative to its
+    # block, then the block end) and global scales, one row per source
+    seg_counts = meta_recv[:, :e_local].contiguous()
+    seg_starts = torch.cat([meta_recv[:, e_local:2 * e_local], meta_recv[:, -1:]], dim=1).contiguous()
+    seg_global = meta_recv[:, 2 * e_local:3 * e_local].contiguous().view(torch.float32)
+    if chunks > 1:
+        rel_host = meta_recv[:, e_local:2 * e_local].cpu().tolist()
+        first = (torch.arange(num_experts + 1, device=dev) // e_local).clamp_max(world - 1) * e_local
+        mine = (pcsr - pcsr[first]).cpu()
 
-    rows_back = _exchange_rows(rows_out, total_send, send_rows, recv_rows, group)
+    def segments(s: int, a: int, b: int):
+        """Received segments of source s for local experts [a, b), rows
+        relative to the first one, and that row range in the source block."""
+        if chunks == 1:
+            return (seg_counts[s], seg_starts[s], seg_global[s]), 0, recv_rows[s]
+        r0 = int(rel_host[s][a])
+        r1 = int(rel_host[s][b]) if b < e_local else recv_rows[s]
+        starts_s = torch.tensor([int(v) - r0 for v in rel_host[s][a:b]] + [r1 - r0], dtype=torch.int32, device=dev)
+        return (seg_counts[s, a:b].contiguous(), starts_s, seg_global[s, a:b].contiguous()), r0, r1
+
+    # this rank's own rows for its own experts: computed while the exchange runs
+    own = None
+    if send_rows[rank]:
+        seg, _, _ = segments(rank, 0, e_local)
+        own = backend.experts(q[lo[rank]:lo[rank + 1]], sf[lo[rank]:lo[rank + 1]], *seg, 0, e_local)
+    for w in outbound:
+        w.wait()
+
+    # the other sources in rotating order: at step j this rank computes the
+    # rows of source (rank + j) and returns them while it receives its own
+    # rows from rank (rank - j), which computes them at the same step; each
+    # source's experts go in `chunks` groups so the return transfers pipeline
+    groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
+    keep = []
+    returns = []
+    for j in range(1, world):
+        s, d = (rank + j) % world, (rank - j) % world
+        for a, b in groups:
+            p2p = []
+            if recv_rows[s]:
+                seg, r0, r1 = segments(s, a, b)
+                if r1 > r0:
+                    res = backend.experts(recv_q[s][r0:r1], recv_sf[s][r0:r1], *seg, a, b)
+                    keep.append(res)
+                    p2p.append(dist.P2POp(dist.isend, res.view(torch.uint8), peer[s], group))
+            if send_rows[d]:
+                g0 = 0 if chunks == 1 else int(mine[d * e_local + a])
+                g1 = send_rows[d] if chunks == 1 or b == e_local else int(mine[d * e_local + b])
+                if g1 > g0:
+                    dst = rows_back[lo[d] + g0:lo[d] + g1]
+                    p2p.append(dist.P2POp(dist.irecv, dst.view(torch.uint8), peer[d], group))
+            if p2p:
+                returns += dist.batch_isend_irecv(p2p)
+    if own is not None:
+        rows_back[lo[rank]:lo[rank + 1]] = own
+    for w in returns:
+        w.wait()
     return backend.combine(rows_back, routing, scaling, shared)
-
-
-def _exchange_rows(src: Tensor, out_rows: int, out_splits: list[int], in_splits: list[int], group) -> Tensor:
-    """all_to_all of whole rows, moved as bytes (any dtype, any backend)."""
-    src = src.contiguous()
-    width = src.shape[1]
-    out = torch.empty(out_rows, width, dtype=src.dtype, device=src.device)
-    dist.all_to_all_single(out.view(torch.uint8), src.view(torch.uint8), out_splits, in_splits, group=group)
-    return out
 
 
 class ExpertParallelRoutedExperts(torch.nn.Module):
@@ -141,7 +215,8 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
     backend = "b200_sm100a_tcgen05_nvfp4_expert_parallel"
     ACCEPTS_DISPATCH = False
 
-    def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None) -> None:
+    def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *, transfer_sms: int = 16,
+                 chunks: int | None = None) -> None:
         super().__init__()
         world = dist.get_world_size(group)
         if bank.num_experts * world != num_experts:
@@ -149,7 +224,8 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
         self.bank = bank
         self.num_experts = num_experts
         self.group = group
-        self._backend = CudaBackend(bank)
+        self.chunks = chunks
+        self._backend = CudaBackend(bank, transfer_sms if world > 1 else 0)
 
     @classmethod
     def from_packed(cls, state: Mapping[str, Tensor], group=None) -> ExpertParallelRoutedExperts:
@@ -165,13 +241,13 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
                        dispatch=None) -> Tensor:
         self.bank._check(x, top_idx, gate, scaling, max(chunk_size, x.shape[0], 1))
         return exchange_forward(x, top_idx, gate, num_experts=self.num_experts, scaling=float(scaling),
-                                backend=self._backend, group=self.group)
+                                backend=self._backend, group=self.group, chunks=self.chunks)
 
     def routed_forward_with_shared(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float,
                                    chunk_size: int = 0, shared: Tensor, dispatch=None) -> Tensor:
         self.bank._check(x, top_idx, gate, scaling, max(chunk_size, x.shape[0], 1))
         return exchange_forward(x, top_idx, gate, num_experts=self.num_experts, scaling=float(scaling),
-                                backend=self._backend, group=self.group, shared=shared)
+                                backend=self._backend, group=self.group, shared=shared, chunks=self.chunks)
 
 
 __all__ = ["CudaBackend", "ExpertParallelRoutedExperts", "exchange_forward", "shard_packed_state"]

@@ -326,7 +326,7 @@ def interleave_gate_up(q: Tensor, sf: Tensor) -> tuple[Tensor, Tensor]:
 
 def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
                    gate_up_q: Tensor, gate_up_sf: Tensor, gate_up_global: Tensor, down_q: Tensor,
-                   down_sf: Tensor, down_global: Tensor, *, weight_sf_layout: int) -> Tensor:
+                   down_sf: Tensor, down_global: Tensor, *, weight_sf_layout: int, sm_limit: int = 0) -> Tensor:
     """The expert-rank half of an expert-parallel layer
     (``praxis_b200_expert_forward``): received NVFP4 rows in padded segments
     (segment v = source * E_local + local expert, ``counts[v]`` rows from
@@ -351,7 +351,7 @@ def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_gl
         act_global=act_global.data_ptr(), segments=segments, gate_up_q=gate_up_q.data_ptr(),
         gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(), down_q=down_q.data_ptr(),
         down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(), weight_sf_layout=int(weight_sf_layout),
-        dim=c, hidden=f, experts=e_local, rows_out=out.data_ptr(), workspace=ws.data_ptr(),
+        dim=c, hidden=f, experts=e_local, sm_limit=int(sm_limit), rows_out=out.data_ptr(), workspace=ws.data_ptr(),
         workspace_size=ws.numel(), device=_dev(q), stream=torch.cuda.current_stream(q.device).cuda_stream,
     )
     capi.check(lib.praxis_b200_expert_forward(C.byref(args)))

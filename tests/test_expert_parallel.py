@@ -46,9 +46,9 @@ class OracleBackend:
         rows = O.padded_rows(r.tokens.numel(), r.experts)
         return O.quantize_activations(x, r.csr.long(), r.pcsr.long(), rows, r.act_global, row_indices=r.tokens)
 
-    def experts(self, q, sf, counts, starts, ag):
-        b = self.bank
-        e_local = b["gate_up_q"].shape[0]
+    def experts(self, q, sf, counts, starts, ag, first, last):
+        b = {name: v[first:last] for name, v in self.bank.items()}
+        e_local = last - first
         f = b["down_q"].shape[2] * 2
         c = q.shape[1] * 2
         rows = q.shape[0]
@@ -96,7 +96,7 @@ def _bank(e: int, c: int, f: int):
     return O.pack_routed_experts(gu, down)
 
 
-def _worker(rank, world, port, shape, fail_rank, results):
+def _worker(rank, world, port, shape, fail_rank, results, chunks=None):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -109,7 +109,7 @@ def _worker(rank, world, port, shape, fail_rank, results):
         if rank == fail_rank:
             raise RuntimeError("planted failure before the exchange")
         out = ep.exchange_forward(x, top_idx, gate, num_experts=e, scaling=2.5,
-                                  backend=OracleBackend(local, k), shared=shared)
+                                  backend=OracleBackend(local, k), shared=shared, chunks=chunks)
         want = O.routed_forward(x, top_idx, gate, bank, 2.5, t, shared=shared)
         results.put((rank, "ok", bool(torch.equal(out.view(torch.int16), want.view(torch.int16))),
                      float(O.rel_l2(out, want))))
@@ -120,11 +120,12 @@ def _worker(rank, world, port, shape, fail_rank, results):
             dist.destroy_process_group()
 
 
-def _run(world, shape, fail_rank=-1):
+def _run(world, shape, fail_rank=-1, chunks=None):
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fail_rank, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fail_rank, results, chunks))
+             for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -138,13 +139,14 @@ def _run(world, shape, fail_rank=-1):
     return out
 
 
-@pytest.mark.parametrize("world,shape", [
-    (2, (64, 256, 8, 2, 128)),
-    (2, (40, 256, 4, 2, 256)),     # two experts per rank, ragged counts
-    (4, (48, 128, 8, 3, 128)),
+@pytest.mark.parametrize("world,shape,chunks", [
+    (2, (64, 256, 8, 2, 128), None),
+    (2, (64, 256, 8, 2, 128), 2),      # return transfers in two expert groups per source
+    (2, (40, 256, 4, 2, 256), None),   # two experts per rank, ragged counts
+    (4, (48, 128, 8, 3, 128), None),
 ])
-def test_exchange_matches_single_rank_layer(world, shape):
-    res = _run(world, shape)
+def test_exchange_matches_single_rank_layer(world, shape, chunks):
+    res = _run(world, shape, chunks=chunks)
     for rank in range(world):
         status, *info = res[rank]
         assert status == "ok", info

@@ -299,6 +299,10 @@ def run_b200(args, cfg):
         ms = float(tt.item())
     value = t * world / (ms / 1e3)
 
+    latency = None
+    if args.config == "5":
+        latency = graph_latency(step, dev, calls=max(20, args.steps * 5))
+
     # per-stage timing (same kernels launched stage by stage, events on the
     # launching stream) for the roofline of the dominant kernel
     stages = time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=max(3, min(args.steps, 10)))
@@ -327,6 +331,7 @@ def run_b200(args, cfg):
         "layer_tflops": layer_flops / (ms / 1e3) / 1e12,
         "stages_ms": stages,
         "roofline": roofline,
+        "graph_latency": latency,
         "clocks": clk.summary(),
         # router 2, dispatch 3, quantize 2 + scale replication 2, GEMM 2, combine 1
         "gpu_launches": 12 * args.steps,
@@ -481,6 +486,41 @@ def run_expert_parallel(args, cfg):
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def graph_latency(step, dev, calls=50, euler_steps=10):
+    """the layer forward captured in a CUDA graph and
+    replayed as the 10 steps of a flow-matching Euler loop; per-call (one
+    replay) latency p50/p90 from CUDA events around each replay."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(5):
+        graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(calls):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(euler_steps + 1)]
+        evs[0].record(stream)
+        for i in range(euler_steps):
+            graph.replay()
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        times += [evs[i].elapsed_time(evs[i + 1]) for i in range(euler_steps)]
+    times.sort()
+    del graph
+    return {"p50_ms": times[len(times) // 2], "p90_ms": times[(len(times) * 9) // 10], "calls": len(times),
+            "euler_steps_per_loop": euler_steps, "capture": "whole layer incl. router in one CUDA graph"}
 
 
 def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):

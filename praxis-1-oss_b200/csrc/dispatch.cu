@@ -23,6 +23,7 @@
 namespace praxis {
 
 constexpr int kDispatchWarps = 8;
+constexpr int kDispatchUnroll = 8;  // 32-position passes whose loads are issued together
 constexpr int kMaxExperts = 1024;
 
 __device__ __forceinline__ int clamp_expert(int64_t e, int experts) {
@@ -78,16 +79,26 @@ __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const
     const int64_t end = min(positions, begin + seg_len);
     uint32_t* h = hist + warp * experts;
     uint32_t* hm = hmax + warp * experts;
-    for (int64_t p0 = begin; p0 < end; p0 += 32) {
-      const int64_t p = p0 + lane;
-      const bool live = p < end;
-      const int e = live ? clamp_expert(top_idx[p], experts) : -1;
-      const uint32_t peers = __match_any_sync(0xffffffffu, e);
-      const int leader = __ffs(peers) - 1;
-      if (live && lane == leader) atomicAdd(&h[e], (uint32_t)__popc(peers));
-      if (live && row_amax != nullptr) {
-        const uint32_t bits = __float_as_uint(bf16_to_f32(row_amax[p / top_k]));
-        atomicMax(&hm[e], bits);
+    // the loads of 8 passes of 32 positions go out before the histogram work
+    for (int64_t base = begin; base < end; base += 32 * kDispatchUnroll) {
+      int ev[kDispatchUnroll];
+      uint32_t mv[kDispatchUnroll];
+#pragma unroll
+      for (int u = 0; u < kDispatchUnroll; ++u) {
+        const int64_t p = base + 32 * u + lane;
+        const bool live = p < end;
+        ev[u] = live ? clamp_expert(top_idx[p], experts) : -1;
+        mv[u] = (live && row_amax != nullptr) ? __float_as_uint(bf16_to_f32(row_amax[p / top_k])) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kDispatchUnroll; ++u) {
+        if (base + 32 * u >= end) break;
+        const int e = ev[u];
+        const bool live = e >= 0;
+        const uint32_t peers = __match_any_sync(0xffffffffu, e);
+        const int leader = __ffs(peers) - 1;
+        if (live && lane == leader) atomicAdd(&h[e], (uint32_t)__popc(peers));
+        if (live && row_amax != nullptr) atomicMax(&hm[e], mv[u]);
       }
     }
   }
@@ -312,22 +323,35 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
   const int64_t begin = (int64_t)seg * seg_len;
   const int64_t end = min(positions, begin + seg_len);
   const uint32_t lt = (1u << lane) - 1u;
-  for (int64_t p0 = begin; p0 < end; p0 += 32) {
-    const int64_t p = p0 + lane;
-    const bool live = p < end;
-    const int e = live ? clamp_expert(top_idx[p], experts) : -1;
-    const uint32_t peers = __match_any_sync(0xffffffffu, e);
-    int dest = 0;
-    if (live) dest = cur[e] + __popc(peers & lt);
-    __syncwarp();
-    if (live && lane == __ffs(peers) - 1) cur[e] += __popc(peers);
-    __syncwarp();
-    if (live) {
-      if (order) order[dest] = p;
-      if (inverse) inverse[p] = dest;
-      if (tokens) tokens[dest] = p / top_k;
-      if (tokens32) tokens32[dest] = (int32_t)(p / top_k);
-      if (sorted_gate) sorted_gate[dest] = gate[p];
+  for (int64_t base = begin; base < end; base += 32 * kDispatchUnroll) {
+    int ev[kDispatchUnroll];
+    uint16_t gv[kDispatchUnroll];
+#pragma unroll
+    for (int u = 0; u < kDispatchUnroll; ++u) {
+      const int64_t p = base + 32 * u + lane;
+      const bool live = p < end;
+      ev[u] = live ? clamp_expert(top_idx[p], experts) : -1;
+      gv[u] = (live && sorted_gate) ? gate[p] : (uint16_t)0;
+    }
+#pragma unroll
+    for (int u = 0; u < kDispatchUnroll; ++u) {
+      if (base + 32 * u >= end) break;
+      const int64_t p = base + 32 * u + lane;
+      const int e = ev[u];
+      const bool live = e >= 0;
+      const uint32_t peers = __match_any_sync(0xffffffffu, e);
+      int dest = 0;
+      if (live) dest = cur[e] + __popc(peers & lt);
+      __syncwarp();
+      if (live && lane == __ffs(peers) - 1) cur[e] += __popc(peers);
+      __syncwarp();
+      if (live) {
+        if (order) order[dest] = p;
+        if (inverse) inverse[p] = dest;
+        if (tokens) tokens[dest] = p / top_k;
+        if (tokens32) tokens32[dest] = (int32_t)(p / top_k);
+        if (sorted_gate) sorted_gate[dest] = gv[u];
+      }
     }
   }
 }

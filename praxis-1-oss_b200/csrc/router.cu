@@ -79,9 +79,12 @@ __global__ void __launch_bounds__(192, 1) router_logits_kernel(
         if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) break;
         uint8_t* st = smem + (size_t)stage * stage_bytes;
         mbar_arrive_expect_tx(&full[stage], (uint32_t)stage_bytes);
-        tma_load_2d(st, &tmap_x, &full[stage], kt * kRouterBK, (int32_t)row0);
+        // CTAs start at different slabs, so they do not all read the same
+        // weight lines at the same time (the sum order is any order anyway)
+        const int slab = (kt + (int)blockIdx.x) % ktiles;
+        tma_load_2d(st, &tmap_x, &full[stage], slab * kRouterBK, (int32_t)row0);
         for (int s = 0; s < splits; ++s)
-          tma_load_2d(st + kRouterABytes + s * e_pad * 128, &tmap_w, &full[stage], kt * kRouterBK, s * experts);
+          tma_load_2d(st + kRouterABytes + s * e_pad * 128, &tmap_w, &full[stage], slab * kRouterBK, s * experts);
         if (++stage == (uint32_t)stages) {
           stage = 0;
           phase ^= 1u;
@@ -206,6 +209,11 @@ __device__ __forceinline__ uint32_t ordered_u32(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// inverse of ordered_u32
+__device__ __forceinline__ float from_ordered_u32(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+
 __device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int o) {
   uint32_t lo = (uint32_t)v, hi = (uint32_t)(v >> 32);
   lo = __shfl_xor_sync(0xffffffffu, lo, o);
@@ -288,6 +296,20 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     }
   }
 
+  // -- distinct selected values (the usual case): the sort below yields them
+  //    in descending order, which is the selection order; otherwise (ties,
+  //    +0/-0, NaN) the sort's tie order is emulated step by step
+  bool distinct = true;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int i = 0; i < j; ++i)
+      if (j < top_k) {
+        const float vi = from_ordered_u32(sel_hi[i]), vj = from_ordered_u32(sel_hi[j]);
+        distinct = distinct && vi != vj && vi == vi && vj == vj;
+      }
+  }
+
   // -- gather order: entries above the k-th value, then the ties, each by index
   uint32_t kth = 0;
 #pragma unroll
@@ -306,7 +328,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
           rank += (ti < tj) || (ti == tj && sel_idx[i] < sel_idx[j]);
         }
       }
-      if (rank == lane) my_idx = sel_idx[j];
+      if (distinct ? j == (int)lane : rank == (int)lane) my_idx = sel_idx[j];
     }
   }
   bool valid = lane < top_k;
@@ -330,7 +352,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 
   // -- ATen's 32-wide bitonic key/value sort (16 threads x 2 items; invalid
   //    entries sort last), one item per lane: positions p and p^stride.
-  for (int size = 2; size <= 32; size <<= 1) {
+  for (int size = distinct ? 64 : 2; size <= 32; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       const float o_val = __shfl_xor_sync(0xffffffffu, my_val, stride);
       const float o_score = __shfl_xor_sync(0xffffffffu, my_score, stride);

@@ -207,7 +207,9 @@ int praxis_b200_pack_weights(const void* w, int32_t experts, int32_t k, int32_t 
                              float* global_out, uint32_t* scratch, int device, void* stream);
 
 /* Copies gate_up q [E, 2F, C/2] / sf [E, 2F, C/16] into the fused-SwiGLU
- * GEMM layout: 64-row blocks of 32 gate rows then the matching 32 up rows.
+ * GEMM layout: 64-row blocks of 32 gate rows then the matching 32 up rows;
+ * block b serves hidden columns 32*h .. 32*h+31 with h = b except that blocks
+ * 1 and 2 of every group of four trade places. F % 128 == 0.
  * Kernel-side layout only (the reference keeps gate rows 0..F-1, up rows
  * F..2F-1: praxis/quantization/nvfp4.py:132-144). */
 int praxis_b200_interleave_gate_up(const void* q, const void* sf, int32_t experts, int32_t hidden, int32_t dim,

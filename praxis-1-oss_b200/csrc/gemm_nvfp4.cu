@@ -69,6 +69,14 @@ __device__ __forceinline__ float expert_multiplier(const GemmParams& p, int e) {
   return bf16_round(mul_rn(ga, p.w_global[weight_expert(p, e)]));
 }
 
+// Hidden 32-column chunk computed by 64-row gate/up block `blk` of the
+// interleaved weights: blocks 1 and 2 of every group of four trade places
+// (see interleave_gate_up_kernel).
+__host__ __device__ __forceinline__ int hidden_chunk(int blk) {
+  const int b = blk & 3;
+  return (blk & ~3) | ((b & 1) << 1) | (b >> 1);
+}
+
 template <int BLOCK_N, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmShape<BLOCK_N>;
@@ -237,7 +245,7 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
             hmax = __hmax2(hmax, __habs2(*reinterpret_cast<__nv_bfloat162*>(&h)));
             packed[j / 2] = h;
           }
-          store_row_chunk(p.out + grow * p.out_cols + (size_t)n * HALF + c * 32, packed);
+          store_row_chunk(p.out + grow * p.out_cols + (size_t)32 * hidden_chunk(n * (BLOCK_N / 64) + c), packed);
         }
         const uint32_t hm = *reinterpret_cast<uint32_t*>(&hmax);
         float rmax = fmaxf(__uint_as_float(hm << 16), __uint_as_float(hm & 0xFFFF0000u));
@@ -288,13 +296,20 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
 // SFB of every N column in each CTA's tensor memory).
 //
 // Tensor memory (512 columns per CTA): the accumulator of tile i starts at
-// column 0 for even i and 192 for odd i; the two overlap in 64 columns, which
-// the epilogue drains first and then releases, so the next tile's MMAs run
-// while the remaining 192 columns drain. Scales live in columns 448..495.
+// column 0 for even i and 128 for odd i; the two overlap in 128 columns
+// (columns 128..255). Each epilogue warp drains the 64-column block it owns
+// inside the overlap first and then releases, so the next tile's MMAs start
+// after one tensor-memory load per warp. Scales live in columns 384..479: two
+// slots of 48 columns (A scales at +0, B scales at +16), one per k-tile in
+// flight.
 //
 // Roles: warp 0 TMA (both CTAs; completion counted on the leader's barrier),
-// warp 1 tcgen05 issuer (leader CTA only), warps 2..9 epilogue (both CTAs,
-// two warps per TMEM lane quadrant, 128 columns each).
+// warp 1 MMA issuer (leader CTA only), warps 2..9 epilogue (both CTAs, two
+// warps per TMEM lane quadrant; the warps of half h take 64-column blocks h
+// and h + 2), warp 10 scale copier (leader CTA only). The scale copies run in
+// the tensor pipe like the MMAs; issued by their own warp into the slot the
+// MMAs are not reading, they overlap the MMAs (issued by the MMA thread, each
+// copy waits for the MMAs issued before it).
 //
 // Scale factors reach tensor memory in one of two ways:
 //  REP = false  the reference's compact layout (512-byte atom = 128 rows x 4
@@ -317,13 +332,13 @@ struct PairShape {
   static constexpr int SFA_BYTES = 4 * 512 * SF_COPIES;      // 4 k-blocks
   static constexpr int SFB_BYTES = 2 * 4 * 512 * SF_COPIES;  // 2 row-tiles x 4 k-blocks
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-  static constexpr int ACC_ALT_COL = 192;  // start of every other accumulator
-  static constexpr int OVERLAP = 64;       // columns shared by consecutive accumulators
-  static constexpr int SFA_COL = 448;
-  static constexpr int SFB_COL = 464;
+  static constexpr int ACC_ALT_COL = 128;  // start of every other accumulator
+  static constexpr int SF_COL = 384;       // scale slot s: A at +48s, B at +48s + 16
+  static constexpr int SF_SLOT_COLS = 48;
   static constexpr int TMEM_COLS = 512;
   static constexpr int EPI_WARPS = 8;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int THREADS = 96 + 32 * EPI_WARPS;
+  static constexpr int COPY_WARP = 2 + EPI_WARPS;
   // Output staging per epilogue warp: one 32 x 64 bf16 box (4 KB) in the TMA
   // 128-byte swizzle.
   static constexpr int OUT_STAGE_BYTES = 4096;
@@ -354,7 +369,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
   uint64_t* empty = bars + S::STAGES;      // each CTA: stage free again
   uint64_t* acc_full = bars + 2 * S::STAGES;
   uint64_t* acc_empty = acc_full + 1;      // leader: 16 epilogue warps of the pair
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* sf_ready = acc_empty + 1;     // leader: a scale slot holds its k-tile's scales
+  uint64_t* sf_free = sf_ready + 2;       // leader: the MMAs reading a scale slot are done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + 2);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
@@ -367,6 +384,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * S::EPI_WARPS);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sf_ready[b], 1);
+      mbar_init(&sf_free[b], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -437,18 +458,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      // ---------------- tcgen05 issuer (leader) ----------------
+      // ---------------- MMA issuer (leader) ----------------
       constexpr uint32_t idesc = idesc_nvf4(256, S::BN);
-      const uint32_t sfa_t = tmem + S::SFA_COL;
-      const uint32_t sfb_t = tmem + S::SFB_COL;
-      uint32_t stage = 0, phase = 0, it = 0;
+      uint32_t stage = 0, phase = 0, it = 0, g = 0;  // g: k-tiles consumed (scale slot g % 2)
       bool ok = true;
       for (int u = cluster; u < total && ok; u += nclusters, ++it) {
         if (!mbar_wait(acc_empty, (it & 1u) ^ 1u, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + ((it & 1u) ? S::ACC_ALT_COL : 0u);
-        for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma)) {
+        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+          const uint32_t slot = g & 1u;
+          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma) ||
+              !mbar_wait(&sf_ready[slot], (g >> 1) & 1u, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -456,8 +477,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
           const int kb_n = min(4, kb_total - kt * 4);
           const uint32_t a_base = smem_u32(sA + stage * S::A_BYTES);
           const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
+          const uint32_t sfa_t = tmem + S::SF_COL + S::SF_SLOT_COLS * slot, sfb_t = sfa_t + 16;
+          for (int kb = 0; kb < kb_n; ++kb) {
+            const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+            const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+            tc_mma_nvf4_pair(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * 8, (kt | kb) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(&sf_free[slot], 0x1);
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(acc_full, 0x3);
+      }
+    }
+  } else if (warp == S::COPY_WARP) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- scale copier (leader) ----------------
+      // The A and B scales of one k-tile, shared memory -> tensor memory of
+      // both CTAs, into the slot the MMAs are not reading.
+      uint32_t stage = 0, phase = 0, g = 0;
+      bool ok = true;
+      for (int u = cluster; u < total && ok; u += nclusters) {
+        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
+          const uint32_t slot = g & 1u;
+          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma) ||
+              !mbar_wait(&sf_free[slot], ((g >> 1) & 1u) ^ 1u, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int kb_n = min(4, kb_total - kt * 4);
           const uint32_t sfa_s = smem_u32(sSFA + stage * S::SFA_BYTES);
           const uint32_t sfb_s = smem_u32(sSFB + stage * S::SFB_BYTES);
+          const uint32_t sfa_t = tmem + S::SF_COL + S::SF_SLOT_COLS * slot, sfb_t = sfa_t + 16;
           if constexpr (REP) {
             // 128 lanes x 32 bytes per copy: lane l reads line l of two
             // replicated atoms (the two 16-byte halves are 2 KB apart).
@@ -473,19 +529,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
                                         smem_desc(sfb_s + 2048 + kb * 512, 0, 128, kLayoutSwizzleNone));
             }
           }
-          for (int kb = 0; kb < kb_n; ++kb) {
-            const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
-            const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
-            tc_mma_nvf4_pair(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * 8, (kt | kb) != 0 ? 1u : 0u);
-          }
-          tc_commit_pair(&empty[stage], 0x3);
+          tc_commit_pair(&sf_ready[slot], 0x1);
           if (++stage == S::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (!ok) break;
-        tc_commit_pair(acc_full, 0x3);
       }
     }
   } else {
@@ -502,9 +551,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
       if (!mbar_wait(acc_full, it & 1u, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       const bool odd = (it & 1u) != 0;
-      // The 64 columns this tile shares with the next accumulator: the last
-      // block of an even tile (half 1), the first block of an odd tile (half 0).
-      const bool owns_overlap = odd ? (half == 0) : (half == 1);
+      // This warp's blocks are half and half + 2; the next accumulator covers
+      // blocks 2, 3 of an even tile and blocks 0, 1 of an odd one, so the
+      // warp's block inside it goes first and is released once it is read.
+      const int first_blk = odd ? half : half + 2;
       auto release = [&]() {
         tc_fence_before();
         __syncwarp();
@@ -513,7 +563,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
           else mbar_arrive_cluster(acc_empty_leader);
         }
       };
-      if (!owns_overlap) release();
       const int here_valid = min(max(t.valid - 128 * (int)rank, 0), 128);
       const bool live = t.pad - 128 * (int)rank > 0;  // this CTA's 128 rows are in live tiles
       const bool valid = row_in_tile < here_valid;
@@ -525,17 +574,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
       __syncwarp();
 #pragma unroll 1
       for (int i = 0; i < 2; ++i) {
-        // 64-column blocks of this warp; the overlapping block goes first
-        const int bl = (owns_overlap && !odd) ? 1 - i : i;
-        const int blk = 2 * half + bl;
+        const int blk = i == 0 ? first_blk : first_blk ^ 2;
+        const int bl = blk >> 1;  // 0 for block half, 1 for block half + 2
         uint32_t r0[32], r1[32];
         tc_ld_32x32b_x32(tbase + blk * 64, r0);
         tc_ld_32x32b_x32(tbase + blk * 64 + 32, r1);
         tc_wait_ld();
-        if (owns_overlap && i == 0) release();
+        if (i == 0) release();
         if constexpr (EPI == EPI_SWIGLU) {
           // block = 32 gate columns then the matching 32 up columns -> 32
-          // hidden columns: chunks 4*bl .. 4*bl+3 of the warp's 64-column box
+          // hidden columns. The gate/up interleave maps blocks (0, 2) to
+          // hidden chunks (0, 1) and (1, 3) to (2, 3) of the tile, so the two
+          // blocks of a warp fill its 64-column box: chunks 4*bl .. 4*bl+3.
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t w[4];

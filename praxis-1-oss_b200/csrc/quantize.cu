@@ -265,14 +265,17 @@ __global__ void pack_quant_kernel(const uint16_t* __restrict__ w, int k_dim, int
 
 // ---------------------------------------------------------------------------
 // Gate/up interleave: kernel-layout row r of an expert's [2F, C] gate_up
-// matrix is gate row 32*(r/64) + r%64 for r%64 < 32, else up row
-// F + 32*(r/64) + r%64 - 32. One CTA per (row, expert).
+// matrix, in 64-row block b = r / 64 serving hidden chunk h = hidden_chunk(b)
+// (blocks 1 and 2 of each group of four swapped, so that each GEMM epilogue
+// warp's two blocks give adjacent hidden columns), is gate row 32*h + r%64
+// for r%64 < 32, else up row F + 32*h + r%64 - 32. One CTA per (row, expert).
 // ---------------------------------------------------------------------------
 __global__ void interleave_gate_up_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sf, int f_dim,
                                           int c_dim, uint8_t* __restrict__ q_out, uint8_t* __restrict__ sf_out) {
   const int r = blockIdx.x, e = blockIdx.y;
   const int blk = r / 64, w = r % 64;
-  const int src = w < 32 ? 32 * blk + w : f_dim + 32 * blk + (w - 32);
+  const int h = (blk & ~3) | ((blk & 1) << 1) | ((blk & 3) >> 1);
+  const int src = w < 32 ? 32 * h + w : f_dim + 32 * h + (w - 32);
   const int64_t rows = 2 * (int64_t)f_dim;
   const uint4* qs = reinterpret_cast<const uint4*>(q + ((int64_t)e * rows + src) * (c_dim / 2));
   uint4* qd = reinterpret_cast<uint4*>(q_out + ((int64_t)e * rows + r) * (c_dim / 2));
@@ -355,7 +358,7 @@ int run_pack_weights(const uint16_t* w, int experts, int k_dim, int n_dim, uint8
 
 int run_interleave_gate_up(const uint8_t* q, const uint8_t* sf, int experts, int f_dim, int c_dim, uint8_t* q_out,
                            uint8_t* sf_out, cudaStream_t stream) {
-  if (f_dim % 64 != 0 || c_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "interleave needs F,C % 64 == 0");
+  if (f_dim % 128 != 0 || c_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "interleave needs F % 128, C % 64 == 0");
   if (experts <= 0) return PRAXIS_B200_OK;
   dim3 grid((unsigned)(2 * f_dim), (unsigned)experts);
   interleave_gate_up_kernel<<<grid, 128, 0, stream>>>(q, sf, f_dim, c_dim, q_out, sf_out);

@@ -247,7 +247,8 @@ def test_interleave_gate_up_layout(P):
         rows = []
         for r in range(2 * f):
             blk, w = divmod(r, 64)
-            rows.append(32 * blk + w if w < 32 else f + 32 * blk + w - 32)
+            h = (blk & ~3) | ((blk & 1) << 1) | ((blk & 3) >> 1)  # blocks 1, 2 of each four swapped
+            rows.append(32 * h + w if w < 32 else f + 32 * h + w - 32)
         rows = torch.tensor(rows)
         assert_bytes_equal(q[ex].cpu(), bank["gate_up_q"][ex][rows])
         got = O.unswizzle_scales(sf[ex].cpu(), 2 * f, c // 16)

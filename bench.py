@@ -266,7 +266,8 @@ def run_b200(args, cfg):
     def layer(xin, yout):
         return ops.moe_forward(xin, None, None, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
                                kw.down_sf, bank.down_global, 2.5, router_terms=terms, router_bias=mod.expert_bias,
-                               top_k=k, out=yout, weight_sf_layout=kw.sf_layout)
+                               top_k=k, out=yout, gate_up_sf_layout=kw.gate_up_sf_layout,
+                               down_sf_layout=kw.down_sf_layout)
 
     def step():
         return layer(x, out)
@@ -333,8 +334,8 @@ def run_b200(args, cfg):
         "roofline": roofline,
         "graph_latency": latency,
         "clocks": clk.summary(),
-        # router 2, dispatch 3, quantize 2 + scale replication 2, GEMM 2, combine 1
-        "gpu_launches": 12 * args.steps,
+        # router 2, dispatch 3, quantize 2 + scale replication 1, GEMM 2, combine 1
+        "gpu_launches": 11 * args.steps,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -477,9 +478,9 @@ def run_expert_parallel(args, cfg):
         "layer_tflops": flops * world / (ms / 1e3) / 1e12,
         "roofline": roofline,
         "clocks": clk.summary() if clk is not None else None,
-        # router 2, row max 1, dispatch 3, quantize 1, tiles 1, scale replication 2, GEMM 2, hidden quantize 1,
-        # combine 1 (NCCL's own kernels not counted)
-        "gpu_launches": 14 * args.steps,
+        # router 2, row max 1, dispatch 3, quantize 1, and per expert-forward call (one per source rank):
+        # tiles 1, scale replication 1, GEMM 2, hidden quantize 1; combine 1 (NCCL's own kernels not counted)
+        "gpu_launches": (8 + 5 * world) * args.steps,
         "e2e": e2e,
     }
     if rank == 0:
@@ -542,7 +543,7 @@ def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
         r = ops.dispatch(top, gate, cfg["experts"], amax, full=False)
         evs[3].record(stream)
         aq, asf = ops.quantize_gather(x, r, r.act_global)
-        if kw.sf_layout == capi.SF_REPLICATED:
+        if kw.gate_up_sf_layout == capi.SF_REPLICATED:
             asf = ops.replicate_scales(asf, 128)
         evs[4].record(stream)
         hamax = torch.zeros(cfg["experts"], dtype=torch.int32, device=x.device)
@@ -550,14 +551,14 @@ def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
         e_g0.record(stream)
         hidden = ops.grouped_gemm(aq, asf, kw.gate_up_q, kw.gate_up_sf, r, epilogue=capi.EPI_SWIGLU,
                                   act_global=r.act_global, w_global=bank.gate_up_global, amax_out=hamax,
-                                  sf_layout=kw.sf_layout)
+                                  sf_layout=kw.gate_up_sf_layout)
         evs[5].record(stream)
         hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
-        if kw.sf_layout == capi.SF_REPLICATED:
+        if kw.down_sf_layout == capi.SF_REPLICATED:
             hsf = ops.replicate_scales(hsf, 128)
         evs[6].record(stream)
         rows = ops.grouped_gemm(hq, hsf, bank.down_q, kw.down_sf, r, epilogue=capi.EPI_RESCALE, act_amax=hamax,
-                                w_global=bank.down_global, sf_layout=kw.sf_layout)
+                                w_global=bank.down_global, sf_layout=kw.down_sf_layout)
         evs[7].record(stream)
         ops.combine(rows, r, 2.5, rows_rescaled=True)
         evs[8].record(stream)

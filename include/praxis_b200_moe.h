@@ -234,7 +234,8 @@ typedef struct praxis_b200_moe_args {
   const void* down_q;        /* [E, C, F/2] */
   const void* down_sf;       /* [E, C, F/16] */
   const float* down_global;
-  int32_t weight_sf_layout;  /* layout of gate_up_sf and down_sf (PRAXIS_B200_SF_*) */
+  int32_t gate_up_sf_layout; /* PRAXIS_B200_SF_* of gate_up_sf */
+  int32_t down_sf_layout;    /* PRAXIS_B200_SF_* of down_sf (replicated needs C % 256 == 0) */
   int64_t tokens;
   int32_t dim;               /* C */
   int32_t hidden;            /* F */
@@ -277,7 +278,8 @@ typedef struct praxis_b200_expert_args {
   const void* down_q;
   const void* down_sf;
   const float* down_global;
-  int32_t weight_sf_layout;   /* PRAXIS_B200_SF_* of gate_up_sf and down_sf */
+  int32_t gate_up_sf_layout;  /* PRAXIS_B200_SF_* of gate_up_sf */
+  int32_t down_sf_layout;     /* PRAXIS_B200_SF_* of down_sf */
   int32_t dim;                /* C */
   int32_t hidden;             /* F */
   int32_t experts;            /* local experts */

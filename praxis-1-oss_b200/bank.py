@@ -34,10 +34,11 @@ _BUFFER_NAMES = frozenset(
 class KernelWeights(NamedTuple):
     """Device copies in the kernels' layouts (built by ``prepare()``)."""
 
-    gate_up_q: Tensor   # rows interleaved in 64-row blocks (32 gate, 32 up)
-    gate_up_sf: Tensor  # same row order; replicated or compact scales
-    down_sf: Tensor     # replicated or compact scales of down_q
-    sf_layout: int      # capi.SF_REPLICATED or capi.SF_COMPACT
+    gate_up_q: Tensor       # rows interleaved in 64-row blocks (32 gate, 32 up)
+    gate_up_sf: Tensor      # same row order, replicated scale layout
+    down_sf: Tensor         # the bank's own compact scales of down_q
+    gate_up_sf_layout: int  # capi.SF_REPLICATED
+    down_sf_layout: int     # capi.SF_COMPACT
 
 
 def _validate(state: Mapping[str, Tensor]) -> tuple[int, int, int]:
@@ -130,20 +131,16 @@ class B200NVFP4RoutedExperts(nn.Module):
         super()._load_from_state_dict(*args, **kwargs)
 
     def prepare(self) -> None:
-        """Build the kernel-layout weights on the buffers' device: gate/up
-        rows interleaved for the fused SwiGLU epilogue and, when C % 256 ==
-        0, both scale tensors in the GEMM's replicated layout (the packed
-        buffers themselves stay in the reference's layout)."""
+        """Build the kernel-layout gate/up weights on the buffers' device:
+        rows interleaved for the fused SwiGLU epilogue, scales in the GEMM's
+        replicated layout (the gate/up GEMM is faster with them; the down GEMM
+        reads the bank's compact scales directly). The packed buffers stay in
+        the reference's layout."""
         if self.gate_up_q.device.type != "cuda":
             raise RuntimeError("prepare() needs the bank on a CUDA device")
         gu_q, gu_sf = ops.interleave_gate_up(self.gate_up_q, self.gate_up_sf)
-        down_sf = self.down_sf
-        layout = capi.SF_COMPACT
-        if self.in_features % 256 == 0:
-            gu_sf = ops.replicate_scales(gu_sf, 256)
-            down_sf = ops.replicate_scales(down_sf, 256)
-            layout = capi.SF_REPLICATED
-        self._kernel = KernelWeights(gu_q, gu_sf, down_sf, layout)
+        gu_sf = ops.replicate_scales(gu_sf, 256)
+        self._kernel = KernelWeights(gu_q, gu_sf, self.down_sf, capi.SF_REPLICATED, capi.SF_COMPACT)
 
     def kernel_weights(self) -> KernelWeights:
         """The kernel-layout weights (prepare() on first use)."""
@@ -223,7 +220,8 @@ class B200NVFP4RoutedExperts(nn.Module):
             ops.moe_forward(
                 x[start:end], top_idx[start:end], gate[start:end], kw.gate_up_q, kw.gate_up_sf, self.gate_up_global,
                 self.down_q, kw.down_sf, self.down_global, float(scaling),
-                None if shared is None else shared[start:end], out=out[start:end], weight_sf_layout=kw.sf_layout,
+                None if shared is None else shared[start:end], out=out[start:end],
+                gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout,
             )
         return out
 

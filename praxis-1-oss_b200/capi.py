@@ -47,7 +47,8 @@ class MoeArgs(C.Structure):
         ("down_q", P),
         ("down_sf", P),
         ("down_global", P),
-        ("weight_sf_layout", I32),
+        ("gate_up_sf_layout", I32),
+        ("down_sf_layout", I32),
         ("tokens", I64),
         ("dim", I32),
         ("hidden", I32),
@@ -78,7 +79,8 @@ class ExpertArgs(C.Structure):
         ("down_q", P),
         ("down_sf", P),
         ("down_global", P),
-        ("weight_sf_layout", I32),
+        ("gate_up_sf_layout", I32),
+        ("down_sf_layout", I32),
         ("dim", I32),
         ("hidden", I32),
         ("experts", I32),

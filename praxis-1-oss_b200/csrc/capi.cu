@@ -388,11 +388,12 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: bad sizes");
   if (a->dim % 128 || a->hidden % 128)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: C and F must be multiples of 128");
-  const int sf_layout = a->weight_sf_layout;
-  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
-    return set_error(PRAXIS_B200_EINVAL, "expert_forward: unknown weight scale layout %d", sf_layout);
-  if (sf_layout == PRAXIS_B200_SF_REPLICATED && a->dim % 256 != 0)
-    return set_error(PRAXIS_B200_EINVAL, "expert_forward: replicated scales need C % 256 == 0");
+  const int gl = a->gate_up_sf_layout, dl = a->down_sf_layout;
+  if ((gl != PRAXIS_B200_SF_COMPACT && gl != PRAXIS_B200_SF_REPLICATED) ||
+      (dl != PRAXIS_B200_SF_COMPACT && dl != PRAXIS_B200_SF_REPLICATED))
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: unknown weight scale layout (%d, %d)", gl, dl);
+  if (dl == PRAXIS_B200_SF_REPLICATED && a->dim % 256 != 0)
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: replicated down scales need C % 256 == 0");
   if (a->rows * (int64_t)(a->dim > 2 * a->hidden ? a->dim : 2 * a->hidden) >= ((int64_t)1 << 31) * 8)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: rows exceed the kernels' indexing range");
   const ExpertLayout L = expert_layout(a->rows, a->segments, a->dim, a->hidden);
@@ -407,11 +408,10 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
   uint32_t* h_amax = reinterpret_cast<uint32_t*>(ws + L.h_amax);
   uint16_t* hidden = reinterpret_cast<uint16_t*>(ws + L.hidden);
   uint8_t* hq = ws + L.hq;
-  const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
   int rc = run_segment_tiles(a->counts, a->starts, a->segments, tiles, L.max_tiles, num_tiles, s);
   if (rc) return rc;
   const uint8_t* asf = static_cast<const uint8_t*>(a->sf);
-  if (rep) {
+  if (gl == PRAXIS_B200_SF_REPLICATED) {
     rc = run_replicate_scales(asf, a->rows, a->dim, 128, ws + L.asf, s);
     if (rc) return rc;
     asf = ws + L.asf;
@@ -420,18 +420,19 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(a->q, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, a->rows,
                         2 * a->hidden, a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, a->act_global, nullptr,
-                        a->gate_up_global, h_amax, sf_layout, s, a->sm_limit);
+                        a->gate_up_global, h_amax, gl, s, a->sm_limit);
   if (rc) return rc;
+  const bool down_rep = dl == PRAXIS_B200_SF_REPLICATED;
   rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
-                         rep ? ws + L.hsf_compact : ws + L.hsf, PRAXIS_B200_SF_COMPACT, s);
+                         down_rep ? ws + L.hsf_compact : ws + L.hsf, PRAXIS_B200_SF_COMPACT, s);
   if (rc) return rc;
-  if (rep) {
+  if (down_rep) {
     rc = run_replicate_scales(ws + L.hsf_compact, a->rows, a->hidden, 128, ws + L.hsf, s);
     if (rc) return rc;
   }
   return run_grouped_gemm(hq, ws + L.hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, a->rows, a->dim,
                           a->hidden, a->experts, EPI_RESCALE, static_cast<uint16_t*>(a->rows_out), a->dim, nullptr,
-                          h_amax, a->down_global, nullptr, sf_layout, s, a->sm_limit);
+                          h_amax, a->down_global, nullptr, dl, s, a->sm_limit);
 }
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,
@@ -446,11 +447,12 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   if (!a->x || !a->top_idx || !a->gate || !a->out || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
       !a->down_q || !a->down_sf || !a->down_global || !a->workspace)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: null pointer");
-  const int sf_layout = a->weight_sf_layout;
-  if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
-    return set_error(PRAXIS_B200_EINVAL, "moe_forward: unknown weight scale layout %d", sf_layout);
-  if (sf_layout == PRAXIS_B200_SF_REPLICATED && a->dim % 256 != 0)
-    return set_error(PRAXIS_B200_EINVAL, "moe_forward: replicated scales need C % 256 == 0");
+  const int gl = a->gate_up_sf_layout, dl = a->down_sf_layout;
+  if ((gl != PRAXIS_B200_SF_COMPACT && gl != PRAXIS_B200_SF_REPLICATED) ||
+      (dl != PRAXIS_B200_SF_COMPACT && dl != PRAXIS_B200_SF_REPLICATED))
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: unknown weight scale layout (%d, %d)", gl, dl);
+  if (dl == PRAXIS_B200_SF_REPLICATED && a->dim % 256 != 0)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: replicated down scales need C % 256 == 0");
   if (a->tokens < 0 || a->dim <= 0 || a->hidden <= 0 || a->experts <= 0 || a->top_k < 1 || a->top_k > 8 ||
       a->top_k > a->experts)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: bad sizes");
@@ -500,7 +502,7 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   // The quantizers write compact scales (one 4-byte word per row and 64
   // columns); a coalesced pass then builds the replicated copies, cheaper
   // than four scattered word stores per scale group.
-  const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
+  const bool rep = gl == PRAXIS_B200_SF_REPLICATED, down_rep = dl == PRAXIS_B200_SF_REPLICATED;
   rc = run_quantize_gather(x, a->tokens, a->dim, a->top_idx, inverse, csr, pcsr, act_global, nullptr, a->top_k,
                            a->experts, tiles, num_tiles, L.max_tiles, aq, rep ? ws + L.asf_compact : asf,
                            PRAXIS_B200_SF_COMPACT, s);
@@ -513,17 +515,17 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
                         a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
-                        h_amax, sf_layout, s);
+                        h_amax, gl, s);
   if (rc) return rc;
   rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
-                         rep ? ws + L.hsf_compact : hsf, PRAXIS_B200_SF_COMPACT, s);
+                         down_rep ? ws + L.hsf_compact : hsf, PRAXIS_B200_SF_COMPACT, s);
   if (rc) return rc;
-  if (rep) {
+  if (down_rep) {
     rc = run_replicate_scales(ws + L.hsf_compact, L.rp, a->hidden, 128, hsf, s);
     if (rc) return rc;
   }
   rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
-                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, sf_layout, s);
+                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, dl, s);
   if (rc) return rc;
   return run_combine(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
                      a->scaling, static_cast<const uint16_t*>(a->shared), static_cast<uint16_t*>(a->out), a->tokens,

@@ -83,7 +83,8 @@ class CudaBackend:
 
         return ops.expert_forward(q, sf, counts, starts, act_global, part(kw.gate_up_q), part(kw.gate_up_sf),
                                   b.gate_up_global[first:last], part(b.down_q), part(kw.down_sf),
-                                  b.down_global[first:last], weight_sf_layout=kw.sf_layout, sm_limit=self.sm_limit)
+                                  b.down_global[first:last], gate_up_sf_layout=kw.gate_up_sf_layout,
+                                  down_sf_layout=kw.down_sf_layout, sm_limit=self.sm_limit)
 
     def combine(self, rows: Tensor, routing, scaling: float, shared: Tensor | None) -> Tensor:
         return ops.combine(rows, routing, scaling, rows_rescaled=True, shared=shared)

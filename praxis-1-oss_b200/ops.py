@@ -326,7 +326,8 @@ def interleave_gate_up(q: Tensor, sf: Tensor) -> tuple[Tensor, Tensor]:
 
 def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
                    gate_up_q: Tensor, gate_up_sf: Tensor, gate_up_global: Tensor, down_q: Tensor,
-                   down_sf: Tensor, down_global: Tensor, *, weight_sf_layout: int, sm_limit: int = 0) -> Tensor:
+                   down_sf: Tensor, down_global: Tensor, *, gate_up_sf_layout: int, down_sf_layout: int,
+                   sm_limit: int = 0) -> Tensor:
     """The expert-rank half of an expert-parallel layer
     (``praxis_b200_expert_forward``): received NVFP4 rows in padded segments
     (segment v = source * E_local + local expert, ``counts[v]`` rows from
@@ -350,7 +351,8 @@ def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_gl
         q=q.data_ptr(), sf=sf.data_ptr(), rows=rows, counts=counts.data_ptr(), starts=starts.data_ptr(),
         act_global=act_global.data_ptr(), segments=segments, gate_up_q=gate_up_q.data_ptr(),
         gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(), down_q=down_q.data_ptr(),
-        down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(), weight_sf_layout=int(weight_sf_layout),
+        down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(), gate_up_sf_layout=int(gate_up_sf_layout),
+        down_sf_layout=int(down_sf_layout),
         dim=c, hidden=f, experts=e_local, sm_limit=int(sm_limit), rows_out=out.data_ptr(), workspace=ws.data_ptr(),
         workspace_size=ws.numel(), device=_dev(q), stream=torch.cuda.current_stream(q.device).cuda_stream,
     )
@@ -358,15 +360,25 @@ def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_gl
     return out
 
 
+def _layout_of(sf: Tensor, q: Tensor, name: str) -> int:
+    """Scale layout told by size: compact = q bytes / 8, replicated = q bytes / 2."""
+    if sf.numel() * 8 == q.numel():
+        return capi.SF_COMPACT
+    if sf.numel() * 2 == q.numel():
+        return capi.SF_REPLICATED
+    raise ValueError(f"{name} size matches neither scale layout")
+
+
 def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_q: Tensor, gate_up_sf: Tensor,
                 gate_up_global: Tensor, down_q: Tensor, down_sf: Tensor, down_global: Tensor, scaling: float,
                 shared: Tensor | None = None, *, router_terms: Tensor | None = None,
                 router_bias: Tensor | None = None, top_k: int | None = None, activation: str = "sigmoid",
-                out: Tensor | None = None, weight_sf_layout: int | None = None):
+                out: Tensor | None = None, gate_up_sf_layout: int | None = None,
+                down_sf_layout: int | None = None):
     """One dispatch chunk through ``praxis_b200_moe_forward``. With
     ``router_terms`` the router runs too and (out, top_idx, gate) is returned.
     ``gate_up_q/sf`` are in the interleaved kernel layout; the weight scales
-    are compact or replicated (``weight_sf_layout``, else told by size)."""
+    are compact or replicated (``*_sf_layout``, else told by their size)."""
     _need(x, "x", BF16, 2)
     t, c = x.shape
     e, c_half_f, _ = down_q.shape
@@ -380,13 +392,10 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         k = top_idx.shape[1]
     if out is None:
         out = torch.empty_like(x)
-    if weight_sf_layout is None:
-        if down_sf.numel() * 8 == down_q.numel():
-            weight_sf_layout = capi.SF_COMPACT
-        elif down_sf.numel() * 2 == down_q.numel():
-            weight_sf_layout = capi.SF_REPLICATED
-        else:
-            raise ValueError("down_sf size matches neither scale layout")
+    if gate_up_sf_layout is None:
+        gate_up_sf_layout = _layout_of(gate_up_sf, gate_up_q, "gate_up_sf")
+    if down_sf_layout is None:
+        down_sf_layout = _layout_of(down_sf, down_q, "down_sf")
     lib = capi.load()
     ws_size = int(lib.praxis_b200_moe_workspace_size(t, k, e, c, f, int(router_terms is not None)))
     ws = torch.empty(ws_size, dtype=torch.uint8, device=dev)
@@ -399,7 +408,7 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         shared=None if shared is None else shared.data_ptr(), out=out.data_ptr(),
         gate_up_q=gate_up_q.data_ptr(), gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(),
         down_q=down_q.data_ptr(), down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(),
-        weight_sf_layout=int(weight_sf_layout), tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
+        gate_up_sf_layout=int(gate_up_sf_layout), down_sf_layout=int(down_sf_layout), tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
         workspace=ws.data_ptr(), workspace_size=ws_size, device=_dev(x),
         stream=torch.cuda.current_stream(dev).cuda_stream,
     )

@@ -91,7 +91,7 @@ def test_two_rank_exchange_emulated_on_one_gpu(P, t, c, e, k, f):
             torch.cat(qs), torch.cat(sfs), torch.tensor(counts, dtype=torch.int32, device=DEV),
             torch.tensor(starts, dtype=torch.int32, device=DEV), torch.tensor(ags, dtype=torch.float32, device=DEV),
             kw.gate_up_q, kw.gate_up_sf, b.gate_up_global, b.down_q, kw.down_sf, b.down_global,
-            weight_sf_layout=kw.sf_layout)
+            gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout)
         off = 0
         for s, src in enumerate(sources):
             pcsr = src[7]

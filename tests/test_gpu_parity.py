@@ -492,7 +492,8 @@ def test_host_pipeline_matches_direct_calls(P):
 
     def layer(xin, yout):
         P.ops.moe_forward(xin, top, gate, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
-                          kw.down_sf, bank.down_global, 2.5, out=yout, weight_sf_layout=kw.sf_layout)
+                          kw.down_sf, bank.down_global, 2.5, out=yout, gate_up_sf_layout=kw.gate_up_sf_layout,
+                          down_sf_layout=kw.down_sf_layout)
 
     g = gen(53)
     host_in = [torch.randn(t, c, generator=g).to(torch.bfloat16).pin_memory() for _ in range(5)]

@@ -49,6 +49,21 @@ CONFIGS = {
 }
 METRIC = "routed-expert tokens/sec per MoE layer"
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate/up GEMM
+# launch, from one single-pass ncu capture of the full-size bench workload:
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#       --clock-control none -k regex:gemm_nvfp4_pair -s 5 -c 5 python bench.py --steps 2 --warmup 3
+# (read 616,211,200 + write 193,506,816 at config 2, 16384 tokens).
+GEMM1_TRAFFIC = {("2", 16384): 616211200 + 193506816}
+
+
+def gemm1_bytes(t, k, c, f, e):
+    """Algorithmic bytes of the gate/up GEMM: every expert's packed weights and
+    compact ue4m3 scales once, the routed rows' packed activations and compact
+    scales once, and the bf16 hidden rows written once (padding rows excluded)."""
+    rows = t * k
+    return e * 2 * f * c // 2 + e * 2 * f * c // 16 + rows * c // 2 + rows * c // 16 + rows * f * 2
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -311,9 +326,12 @@ def run_b200(args, cfg):
     flops1 = 2.0 * t * k * c * 2 * f
     bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
     fp4_peak = 4.0 * bf16_peak
+    traffic = GEMM1_TRAFFIC.get((args.config, t))
     roofline = {"bound": "tensor", "kernel": "gemm_nvfp4_pair_kernel<EPI_SWIGLU> (gate/up)",
                 "achieved": flops1 / (gemm1_ms / 1e3) / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": flops1 / (gemm1_ms / 1e3) / 1e12 / fp4_peak, "traffic": None,
+                "frac": flops1 / (gemm1_ms / 1e3) / 1e12 / fp4_peak,
+                "traffic": traffic, "traffic_unit": "bytes per launch (ncu dram read + write)" if traffic else None,
+                "algorithmic_bytes": gemm1_bytes(t, k, c, f, e),
                 "peak_note": ("dense FP4 peak = 4 x measured cuBLAS bf16 burst "
                               f"({bf16_peak} TFLOP/s, MEASURED_PEAKS.json); nominal dense FP4 9000 TFLOP/s")}
     layer_flops = 6.0 * t * k * c * f

@@ -553,6 +553,9 @@ def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):
     stream = torch.cuda.current_stream(x.device)
     for rep in range(reps + 1):
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        # a spin of ~2 ms ahead of the stages lets the host enqueue all of
+        # them first, so the event gaps hold device time only (no launch gaps)
+        torch.cuda._sleep(4_000_000)
         evs[0].record(stream)
         logits, amax = ops.router_logits(x, terms)
         evs[1].record(stream)

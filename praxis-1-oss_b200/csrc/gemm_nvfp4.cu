@@ -320,12 +320,21 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
 //               praxis_b200_replicate_scales); one tcgen05.cp 128x256b moves
 //               two replicated atoms (6 copies per k-tile, ~5x less copy time
 //               for the same tensor-memory contents).
+//
+// Output stores:
+//  DIRECT       the SwiGLU epilogue (128 hidden columns per tile) stores its
+//               rows straight from registers (16-byte stores, 64 contiguous
+//               bytes per row and block); the freed staging memory holds a
+//               fourth k-tile stage, which the TMA loads need to stay ahead
+//               of the MMAs (3 stages: 441 us, 4 stages: 408 us for GEMM1 of
+//               config 2). The rescale epilogue (256 columns) keeps the
+//               staged TMA stores, which write full lines.
 // ---------------------------------------------------------------------------
-template <bool REP>
+template <bool REP, bool DIRECT>
 struct PairShape {
   static constexpr int BN = 256;
   static constexpr int BK_BYTES = 128;
-  static constexpr int STAGES = REP ? 3 : 4;
+  static constexpr int STAGES = REP ? (DIRECT ? 4 : 3) : 4;
   static constexpr int A_BYTES = 128 * BK_BYTES;
   static constexpr int B_BYTES = 128 * BK_BYTES;
   static constexpr int SF_COPIES = REP ? 4 : 1;
@@ -340,8 +349,8 @@ struct PairShape {
   static constexpr int THREADS = 96 + 32 * EPI_WARPS;
   static constexpr int COPY_WARP = 2 + EPI_WARPS;
   // Output staging per epilogue warp: one 32 x 64 bf16 box (4 KB) in the TMA
-  // 128-byte swizzle.
-  static constexpr int OUT_STAGE_BYTES = 4096;
+  // 128-byte swizzle (none for direct stores).
+  static constexpr int OUT_STAGE_BYTES = DIRECT ? 0 : 4096;
   static constexpr size_t SMEM_BYTES =
       1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EPI_WARPS * OUT_STAGE_BYTES + 256;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -353,10 +362,17 @@ __device__ __forceinline__ void stage_chunk(uint8_t* box, int row, int chunk, ui
   *reinterpret_cast<uint4*>(box + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
 }
 
+// Writes 16 bytes to global memory.
+__device__ __forceinline__ void st_global_v4(uint16_t* ptr, uint4 v) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 template <int EPI, bool REP>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI == EPI_SWIGLU>::THREADS, 1)
     gemm_nvfp4_pair_kernel(const __grid_constant__ GemmParams p) {
-  using S = PairShape<REP>;
+  constexpr bool DIRECT = EPI == EPI_SWIGLU;
+  using S = PairShape<REP, DIRECT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -566,12 +582,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
       const int here_valid = min(max(t.valid - 128 * (int)rank, 0), 128);
       const bool live = t.pad - 128 * (int)rank > 0;  // this CTA's 128 rows are in live tiles
       const bool valid = row_in_tile < here_valid;
+      const int64_t grow = (int64_t)t.row0 + 128 * (int)rank + row_in_tile;
+      uint16_t* const orow = p.out + grow * p.out_cols;  // used by direct stores of live rows only
+      const bool store_row = live && grow < p.out_rows;
       const uint32_t tbase = tmem + ((quad * 32u) << 16) + (odd ? S::ACC_ALT_COL : 0u);
       const float mult = (EPI == EPI_PLAIN) ? 1.0f : expert_multiplier(p, t.expert);
       __nv_bfloat162 hmax = __floats2bfloat162_rn(0.0f, 0.0f);  // max |h| per column parity
-      // the staging boxes are free once this warp's previous stores read them
-      if (lane == 0) bulk_wait_group_read0();
-      __syncwarp();
+      if constexpr (!DIRECT) {
+        // the staging boxes are free once this warp's previous stores read them
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int i = 0; i < 2; ++i) {
         const int blk = i == 0 ? first_blk : first_blk ^ 2;
@@ -585,7 +606,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
           // block = 32 gate columns then the matching 32 up columns -> 32
           // hidden columns. The gate/up interleave maps blocks (0, 2) to
           // hidden chunks (0, 1) and (1, 3) to (2, 3) of the tile, so the two
-          // blocks of a warp fill its 64-column box: chunks 4*bl .. 4*bl+3.
+          // blocks of a warp fill its 64 hidden columns 64*half .. 64*half+63
+          // of the tile: 8-column chunks 4*bl .. 4*bl+3.
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t w[4];
@@ -598,7 +620,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
               hmax = __hmax2(hmax, __habs2(*reinterpret_cast<__nv_bfloat162*>(&h)));
               w[j] = h;
             }
-            stage_chunk(stg, (int)lane, 4 * bl + c, make_uint4(w[0], w[1], w[2], w[3]));
+            if (store_row)
+              st_global_v4(orow + n * (S::BN / 2) + 64 * half + 8 * (4 * bl + c), make_uint4(w[0], w[1], w[2], w[3]));
           }
         } else {
           // one 32 x 64 box per block: reuse the staging box once the
@@ -625,14 +648,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP>::THRE
             tma_store_2d(&p.tmap_out, stg, n * S::BN + 64 * blk, t.row0 + 128 * (int)rank + (int)quad * 32);
             bulk_commit_group();
           }
-        }
-      }
-      if constexpr (EPI == EPI_SWIGLU) {
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0 && live) {
-          tma_store_2d(&p.tmap_out, stg, n * (S::BN / 2) + 64 * half, t.row0 + 128 * (int)rank + (int)quad * 32);
-          bulk_commit_group();
         }
       }
       if constexpr (EPI == EPI_SWIGLU) {
@@ -735,7 +750,7 @@ static int gemm_variant() {
 
 template <int EPI, bool REP>
 static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t stream) {
-  using S = PairShape<REP>;
+  using S = PairShape<REP, EPI == EPI_SWIGLU>;
   auto kernel = gemm_nvfp4_pair_kernel<EPI, REP>;
   static int max_clusters[8] = {0};
   int dev = 0;
@@ -819,6 +834,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.K = k;
   p.out = out;
   p.out_cols = out_cols;
+  p.out_rows = rows_padded;
   p.act_global = act_global;
   p.act_amax = act_amax;
   p.w_global = w_global;

@@ -28,6 +28,7 @@ struct GemmParams {
   int32_t K;
   uint16_t* out;
   int32_t out_cols;
+  int64_t out_rows;  // rows of the output (direct stores stay below)
   const float* act_global;
   const uint32_t* act_amax;
   const float* w_global;

@@ -161,7 +161,8 @@ int praxis_b200_quantize_rows(const void* x, int32_t k, const int32_t* tiles, co
  * (zero for padding written by the quantize entry points; EPI_SWIGLU stores 0).
  * Replaces praxis/kernels/nvfp4.py:355-419 (grouped_nvfp4_mm) with
  * praxis/kernels/nvfp4_moe.py:102-158 (EPI_SWIGLU) or the rescale of
- * praxis/kernels/nvfp4_moe.py:236-247 (EPI_RESCALE) fused. N, K % 128 == 0. */
+ * praxis/kernels/nvfp4_moe.py:236-247 (EPI_RESCALE) fused. N, K % 128 == 0.
+ * Scale buffers and out are 16-byte aligned; the EPI_SWIGLU out 32-byte. */
 /* (A tile whose expert index is >= experts uses weights index % experts.) */
 int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf,
                              const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles,

@@ -14,6 +14,9 @@
 
 namespace praxis {
 
+// KMAX: slots held per lane (top_k <= KMAX); U: 8-column chunks per lane per
+// pass, so that KMAX * U 16-byte loads are in flight per lane.
+template <int KMAX, int U>
 __global__ void __launch_bounds__(256) combine_kernel(
     const uint16_t* __restrict__ rows, int cols, const int64_t* __restrict__ inverse,
     const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate, const int32_t* __restrict__ csr,
@@ -43,16 +46,15 @@ __global__ void __launch_bounds__(256) combine_kernel(
     s_mult[warp][lane] = mult;
   }
   __syncwarp();
-  // Two 8-column chunks per lane per pass: every routed-row load of the pass
-  // is issued before any arithmetic (2 * top_k 16-byte loads in flight).
-  constexpr int U = 2;
+  // U 8-column chunks per lane per pass: every routed-row load of the pass
+  // is issued before any arithmetic (U * top_k 16-byte loads in flight).
   for (int c0 = lane * 8; c0 < cols; c0 += 256 * U) {
-    uint4 v[U][8];
+    uint4 v[U][KMAX];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int c = c0 + u * 256;
 #pragma unroll
-      for (int s = 0; s < 8; ++s)
+      for (int s = 0; s < KMAX; ++s)
         if (s < top_k && c < cols) v[u][s] = ldg_stream(reinterpret_cast<const uint4*>(rows + s_src[warp][s] * cols + c));
     }
 #pragma unroll
@@ -67,7 +69,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[a][j] = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
+      for (int s = 0; s < KMAX; ++s) {
         if (s < top_k) {
           const uint32_t wv[4] = {v[u][s].x, v[u][s].y, v[u][s].z, v[u][s].w};
           const float2 sc = make_float2(s_scale[warp][s], s_scale[warp][s]);
@@ -109,9 +111,16 @@ int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const in
     return set_error(PRAXIS_B200_EINVAL, "combine needs global scales to rescale raw rows");
   if (tokens == 0) return PRAXIS_B200_OK;
   const int64_t blocks = (tokens + 7) / 8;
-  combine_kernel<<<(unsigned)blocks, 256, 0, stream>>>(rows, cols, inverse, top_idx, gate, csr, pcsr, h_global, h_amax,
-                                                        w_global, rows_rescaled, scaling, shared, out, tokens, top_k,
-                                                        experts);
+  // eight 16-byte loads in flight per lane for every top_k
+#define PRAXIS_COMBINE(KMAX, U)                                                                                    \
+  combine_kernel<KMAX, U><<<(unsigned)blocks, 256, 0, stream>>>(rows, cols, inverse, top_idx, gate, csr, pcsr,      \
+                                                               h_global, h_amax, w_global, rows_rescaled, scaling, \
+                                                               shared, out, tokens, top_k, experts)
+  if (top_k == 1) PRAXIS_COMBINE(1, 8);
+  else if (top_k == 2) PRAXIS_COMBINE(2, 4);
+  else if (top_k <= 4) PRAXIS_COMBINE(4, 2);
+  else PRAXIS_COMBINE(8, 1);
+#undef PRAXIS_COMBINE
   return check_launch("combine");
 }
 

@@ -222,9 +222,12 @@ __device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, fl
   const float2 g = unpack_bf16x2(rescale_pair(g0, g1, mult));
   const float2 u = unpack_bf16x2(rescale_pair(u0, u1, mult));
   const float2 t = mul2_rn(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  // The flush-to-zero form gives the same d = 1 + 2^t as the reference's
+  // ex2.approx.f32: a subnormal t gives 2^t = 1 either way, and a subnormal
+  // 2^t (t < -126) vanishes in 1 + 2^t either way.
   float e0, e1;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(e0) : "f"(t.x));
-  asm("ex2.approx.f32 %0, %1;" : "=f"(e1) : "f"(t.y));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(t.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(t.y));
   const float2 one = make_float2(1.0f, 1.0f);
   const float2 d = add2_rn(one, make_float2(e0, e1));
   float2 s;

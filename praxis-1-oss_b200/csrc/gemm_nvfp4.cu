@@ -362,9 +362,10 @@ __device__ __forceinline__ void stage_chunk(uint8_t* box, int row, int chunk, ui
   *reinterpret_cast<uint4*>(box + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
 }
 
-// Writes 16 bytes to global memory.
-__device__ __forceinline__ void st_global_v4(uint16_t* ptr, uint4 v) {
-  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+// Writes 32 bytes (16 bf16) to global memory; ptr is 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(uint16_t* ptr, uint4 a, uint4 b) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(a.x), "r"(a.y), "r"(a.z),
+               "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
                : "memory");
 }
 
@@ -608,6 +609,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
           // hidden chunks (0, 1) and (1, 3) to (2, 3) of the tile, so the two
           // blocks of a warp fill its 64 hidden columns 64*half .. 64*half+63
           // of the tile: 8-column chunks 4*bl .. 4*bl+3.
+          uint4 prev = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t w[4];
@@ -620,8 +622,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
               hmax = __hmax2(hmax, __habs2(*reinterpret_cast<__nv_bfloat162*>(&h)));
               w[j] = h;
             }
-            if (store_row)
-              st_global_v4(orow + n * (S::BN / 2) + 64 * half + 8 * (4 * bl + c), make_uint4(w[0], w[1], w[2], w[3]));
+            // two chunks (32 bytes, one sector) per store
+            if (c & 1) {
+              if (store_row)
+                st_global_v8(orow + n * (S::BN / 2) + 64 * half + 8 * (4 * bl + c - 1), prev,
+                             make_uint4(w[0], w[1], w[2], w[3]));
+            } else {
+              prev = make_uint4(w[0], w[1], w[2], w[3]);
+            }
           }
         } else {
           // one 32 x 64 box per block: reuse the staging box once the
@@ -819,6 +827,8 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
     return set_error(PRAXIS_B200_EINVAL, "the replicated scale layout needs N %% 256 == 0");
   if (((uintptr_t)a_sf | (uintptr_t)b_sf | (uintptr_t)out) & 15)
     return set_error(PRAXIS_B200_EINVAL, "scale and output buffers must be 16-byte aligned");
+  if (epilogue == EPI_SWIGLU && ((uintptr_t)out & 31))
+    return set_error(PRAXIS_B200_EINVAL, "the SwiGLU output must be 32-byte aligned");
   if (rows_padded == 0 || max_tiles == 0) return PRAXIS_B200_OK;
   GemmParams p;
   memset(&p, 0, sizeof(p));

@@ -74,6 +74,10 @@ def parse():
     ap.add_argument("--config", default=None, choices=sorted(CONFIGS),
                     help="default: 2 on one GPU, 4 (expert parallel) on several")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ep-chunks", type=int, default=None,
+                    help="expert groups per source in the expert-parallel exchange (N > 1)")
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel row exchange (N > 1): copy engines into IPC-mapped peer buffers, or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override the config's token count (small profiling cases)")
@@ -367,7 +371,8 @@ def run_b200(args, cfg):
 def run_expert_parallel(args, cfg):
     """N > 1: the layer expert-parallel over the N GPUs of one node (config 4:
     each rank routes its own tokens; experts sharded 64/N per rank; NVFP4 rows
-    and scales out, bf16 rows back over NCCL all-to-all)."""
+    and scales out, bf16 rows back; by default on the copy engines into
+    IPC-mapped peer buffers, ``--transport nccl`` for NCCL transfers)."""
     import datetime
 
     import torch
@@ -397,7 +402,7 @@ def run_expert_parallel(args, cfg):
     bank = pkg.pack_routed_experts(gu.contiguous(), down.contiguous(), keep_on_device=True)
     del gu, down
     bank.prepare()
-    ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e)
+    ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e, transport=args.transport, chunks=args.ep_chunks)
     grouter = torch.Generator().manual_seed(11)
     router = (torch.randn(e, c, generator=grouter) * (1.0 / c) ** 0.5).to(dev)
     terms = ops.split_router_weight(router)
@@ -491,7 +496,8 @@ def run_expert_parallel(args, cfg):
         "config": {"workload": f"BASELINE config {args.config}: expert-parallel MoE layer forward incl. router",
                    "tokens_per_rank": t, "dim": c, "experts": e, "experts_per_rank": el, "top_k": k,
                    "expert_hidden": f, "router": "sigmoid+renorm", "parallelism": f"ep{world}",
-                   "exchange": "NCCL all-to-all: FP4 rows + UE4M3 scales out, bf16 rows back",
+                   "exchange": ("copy engines into IPC-mapped peer buffers" if args.transport == "peer" else
+                                "NCCL point-to-point") + ": FP4 rows + UE4M3 scales out, bf16 rows back",
                    "l2": "per-rank inputs and weights exceed the 126 MB L2; no flush"},
         "layer_tflops": flops * world / (ms / 1e3) / 1e12,
         "roofline": roofline,
@@ -503,6 +509,7 @@ def run_expert_parallel(args, cfg):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    ep.close()
     dist.barrier()
     dist.destroy_process_group()
 

@@ -327,6 +327,24 @@ int praxis_b200_dispatch_noalloc(const int64_t* top_idx, const void* gate, const
                                  int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles, int32_t* num_tiles,
                                  float* act_global, uint32_t* act_amax, int device, void* stream);
 
+/* Peer buffers for the expert-parallel exchange (one process per GPU on one
+ * node). No counterpart in the reference (it has no expert parallelism).
+ * A rank allocates a buffer with praxis_b200_ipc_alloc, exports it with
+ * praxis_b200_ipc_handle, and every other rank maps it with
+ * praxis_b200_ipc_open (CUDA IPC, peer access enabled on first use); the
+ * mapped pointer is valid on the opening rank's device until
+ * praxis_b200_ipc_close. praxis_b200_copy_async copies device bytes on a
+ * stream (a copy engine moves them; either side may be a mapped peer
+ * buffer). The exporting rank must keep its buffer until every peer has
+ * closed its mapping. */
+#define PRAXIS_B200_IPC_HANDLE_BYTES 64
+int praxis_b200_ipc_alloc(size_t bytes, int device, void** ptr);
+int praxis_b200_ipc_free(void* ptr, int device);
+int praxis_b200_ipc_handle(const void* ptr, int device, void* handle);
+int praxis_b200_ipc_open(const void* handle, int device, void** ptr);
+int praxis_b200_ipc_close(void* ptr, int device);
+int praxis_b200_copy_async(void* dst, const void* src, size_t bytes, int device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -133,7 +133,15 @@ SIGNATURES: dict[str, tuple] = {
         C.c_int,
         [P, P, P, I64, I32, I32, P, P, P, P, P, P, P, P, P, I32, P, P, P, C.c_int, P],
     ),
+    "praxis_b200_ipc_alloc": (C.c_int, [C.c_size_t, C.c_int, C.POINTER(C.c_void_p)]),
+    "praxis_b200_ipc_free": (C.c_int, [P, C.c_int]),
+    "praxis_b200_ipc_handle": (C.c_int, [P, C.c_int, P]),
+    "praxis_b200_ipc_open": (C.c_int, [P, C.c_int, C.POINTER(C.c_void_p)]),
+    "praxis_b200_ipc_close": (C.c_int, [P, C.c_int]),
+    "praxis_b200_copy_async": (C.c_int, [P, P, C.c_size_t, C.c_int, P]),
 }
+
+IPC_HANDLE_BYTES = 64
 
 
 class PraxisB200Error(RuntimeError):

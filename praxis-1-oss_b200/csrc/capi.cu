@@ -532,4 +532,69 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
                      a->top_k, a->experts, s);
 }
 
+// ---------------------------------------------------------------------------
+// Peer buffers (CUDA IPC) and copies for the expert-parallel exchange
+// ---------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == PRAXIS_B200_IPC_HANDLE_BYTES, "IPC handle size");
+
+int praxis_b200_ipc_alloc(size_t bytes, int device, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return set_error(PRAXIS_B200_EINVAL, "ipc_alloc: null pointer or zero size");
+  int rc = use_device(device);
+  if (rc) return rc;
+  *ptr = nullptr;
+  const cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "ipc_alloc(%zu): %s", bytes, cudaGetErrorString(e));
+  return PRAXIS_B200_OK;
+}
+
+int praxis_b200_ipc_free(void* ptr, int device) {
+  int rc = use_device(device);
+  if (rc) return rc;
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "ipc_free: %s", cudaGetErrorString(e));
+  return PRAXIS_B200_OK;
+}
+
+int praxis_b200_ipc_handle(const void* ptr, int device, void* handle) {
+  if (ptr == nullptr || handle == nullptr) return set_error(PRAXIS_B200_EINVAL, "ipc_handle: null pointer");
+  int rc = use_device(device);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "ipc_handle: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  return PRAXIS_B200_OK;
+}
+
+int praxis_b200_ipc_open(const void* handle, int device, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return set_error(PRAXIS_B200_EINVAL, "ipc_open: null pointer");
+  int rc = use_device(device);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "ipc_open: %s", cudaGetErrorString(e));
+  return PRAXIS_B200_OK;
+}
+
+int praxis_b200_ipc_close(void* ptr, int device) {
+  int rc = use_device(device);
+  if (rc) return rc;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "ipc_close: %s", cudaGetErrorString(e));
+  return PRAXIS_B200_OK;
+}
+
+int praxis_b200_copy_async(void* dst, const void* src, size_t bytes, int device, void* stream) {
+  if (bytes == 0) return PRAXIS_B200_OK;
+  if (dst == nullptr || src == nullptr) return set_error(PRAXIS_B200_EINVAL, "copy_async: null pointer");
+  int rc = use_device(device);
+  if (rc) return rc;
+  const cudaError_t e =
+      cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "copy_async: %s", cudaGetErrorString(e));
+  return PRAXIS_B200_OK;
+}
+
 }  // extern "C"

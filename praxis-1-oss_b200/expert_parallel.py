@@ -42,7 +42,9 @@ import torch
 import torch.distributed as dist
 from torch import Tensor
 
-from . import ops
+import ctypes as C
+
+from . import capi, ops
 from .bank import B200NVFP4RoutedExperts
 
 
@@ -206,6 +208,255 @@ def exchange_forward(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: i
     return backend.combine(rows_back, routing, scaling, shared)
 
 
+def _padded(rows: int) -> int:
+    return (rows + 127) // 128 * 128
+
+
+class _DeviceBytes:
+    """A raw device allocation seen by torch as a uint8 tensor (no copy)."""
+
+    def __init__(self, ptr: int, nbytes: int) -> None:
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3}
+
+
+class PeerExchange:
+    """Buffers of this rank that every other rank of ``group`` writes into
+    directly (CUDA IPC mappings), and the copy streams that move rows between
+    ranks on the GPUs' copy engines, so the expert GEMMs keep every SM.
+
+    * ``recv``: one slot per source rank for the FP4 rows and compact scale
+      atoms that source sends to this rank's experts;
+    * ``back``: this rank's padded routed rows (bf16), written by the expert
+      ranks with their results.
+
+    Buffers grow (collectively: every rank derives the same capacity from the
+    exchanged token counts) and are never shrunk. Ordering between ranks uses
+    two one-element all-reduces per forward: after them every rank's copies
+    into this rank's buffers have landed, and every reader of the previous
+    forward's data is done.
+    """
+
+    def __init__(self, group, device: torch.device, copy_streams: int = 4) -> None:
+        self.group = group
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slot_rows = 0
+        self.back_rows = 0
+        self.q_cols = self.sf_cols = self.dim = 0
+        self._local: dict[str, tuple[int, int]] = {}  # name -> (pointer, bytes)
+        self._peer: dict[str, list[int]] = {}  # name -> pointer per rank (own rank: local)
+        self.streams = [torch.cuda.Stream(self.device) for _ in range(copy_streams)]
+        self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.ready: torch.cuda.Event | None = None  # the previous forward's last barrier
+
+    # -- buffers ------------------------------------------------------------
+    def _release(self) -> None:
+        lib = capi.load()
+        dev = self.device.index
+        for name, ptrs in self._peer.items():
+            for r, ptr in enumerate(ptrs):
+                if r != self.rank and ptr:
+                    capi.check(lib.praxis_b200_ipc_close(C.c_void_p(ptr), dev))
+        self._peer = {}
+        if self._local:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)  # every peer has closed its mappings
+            for ptr, _ in self._local.values():
+                capi.check(lib.praxis_b200_ipc_free(C.c_void_p(ptr), dev))
+        self._local = {}
+
+    def ensure(self, slot_rows: int, back_rows: int, q_cols: int, sf_cols: int, dim: int) -> None:
+        """Collective when the buffers grow: every rank must call it with the
+        same arguments."""
+        if (slot_rows <= self.slot_rows and back_rows <= self.back_rows and (q_cols, sf_cols, dim) ==
+                (self.q_cols, self.sf_cols, self.dim)):
+            return
+        self._release()
+        lib = capi.load()
+        dev = self.device.index
+        sizes = {"recv": self.world * slot_rows * (q_cols + sf_cols), "back": back_rows * dim * 2}
+        handles = {}
+        for name, nbytes in sizes.items():
+            ptr = C.c_void_p()
+            capi.check(lib.praxis_b200_ipc_alloc(nbytes, dev, C.byref(ptr)))
+            self._local[name] = (int(ptr.value), nbytes)
+            h = (C.c_ubyte * capi.IPC_HANDLE_BYTES)()
+            capi.check(lib.praxis_b200_ipc_handle(ptr, dev, h))
+            handles[name] = bytes(h)
+        gathered: list = [None] * self.world
+        dist.all_gather_object(gathered, handles, group=self.group)
+        for name in sizes:
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self._local[name][0])
+                    continue
+                h = (C.c_ubyte * capi.IPC_HANDLE_BYTES).from_buffer_copy(gathered[r][name])
+                ptr = C.c_void_p()
+                capi.check(lib.praxis_b200_ipc_open(h, dev, C.byref(ptr)))
+                ptrs.append(int(ptr.value))
+            self._peer[name] = ptrs
+        self.slot_rows, self.back_rows = slot_rows, back_rows
+        self.q_cols, self.sf_cols, self.dim = q_cols, sf_cols, dim
+        self.ready = None
+
+    def recv_views(self, s: int, rows: int) -> tuple[Tensor, Tensor]:
+        """The FP4 rows and scale atoms source ``s`` wrote into this rank's slot."""
+        ptr, _ = self._local["recv"]
+        base = ptr + s * self.slot_rows * (self.q_cols + self.sf_cols)
+        q = torch.as_tensor(_DeviceBytes(base, rows * self.q_cols), device=self.device)
+        sf = torch.as_tensor(_DeviceBytes(base + self.slot_rows * self.q_cols, rows * self.sf_cols),
+                             device=self.device)
+        return q.view(rows, self.q_cols), sf.view(rows, self.sf_cols)
+
+    def back_view(self, rows: int) -> Tensor:
+        ptr, _ = self._local["back"]
+        t = torch.as_tensor(_DeviceBytes(ptr, rows * self.dim * 2), device=self.device)
+        return t.view(torch.bfloat16).view(rows, self.dim)
+
+    def recv_slot(self, d: int, s: int) -> tuple[int, int]:
+        """Device addresses (on this rank) of rank d's slot for source s: rows, scales."""
+        base = self._peer["recv"][d] + s * self.slot_rows * (self.q_cols + self.sf_cols)
+        return base, base + self.slot_rows * self.q_cols
+
+    def back_row(self, d: int, row: int) -> int:
+        return self._peer["back"][d] + row * self.dim * 2
+
+    def copy(self, dst: int, src: int, nbytes: int, stream: torch.cuda.Stream) -> None:
+        capi.check(capi.load().praxis_b200_copy_async(C.c_void_p(dst), C.c_void_p(src), nbytes,
+                                                       self.device.index, C.c_void_p(stream.cuda_stream)))
+
+    def barrier(self, stream: torch.cuda.Stream) -> None:
+        """All ranks' work enqueued before this point (on ``stream``) is done
+        when ``stream`` continues."""
+        with torch.cuda.stream(stream):
+            dist.all_reduce(self.flag, group=self.group)
+
+    def close(self) -> None:
+        self._release()
+        self.slot_rows = self.back_rows = 0
+
+
+def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: int, scaling: float,
+                          backend, peers: PeerExchange, shared: Tensor | None = None, chunks: int = 2) -> Tensor:
+    """``exchange_forward`` with the rows moved by copy engines into the
+    peers' mapped buffers (``PeerExchange``) instead of NCCL point-to-point
+    transfers: the same routing, segments, arithmetic and results. Collective
+    over ``peers.group``; ``chunks`` expert groups per source (same on every
+    rank)."""
+    world, rank = peers.world, peers.rank
+    e_local = num_experts // world
+    if e_local * world != num_experts:
+        raise ValueError(f"{num_experts} experts do not shard evenly over {world} ranks")
+    dev = x.device
+    compute = torch.cuda.current_stream(dev)
+    top_k = top_idx.shape[1]
+    chunks = max(1, min(e_local, chunks))
+
+    routing = backend.route_rows(x, top_idx, gate, num_experts)
+    q, sf = backend.quantize(x, routing)
+    csr = routing.csr.to(torch.int64)
+    pcsr = routing.pcsr.to(torch.int64)
+    counts = (csr[1:] - csr[:-1]).view(world, e_local)
+    bounds = pcsr[::e_local]  # [world + 1]
+    rel = pcsr[:-1].view(world, e_local) - bounds[:-1].unsqueeze(1)
+    block = (bounds[1:] - bounds[:-1]).unsqueeze(1)
+    ag_bits = routing.act_global.contiguous().view(torch.int32).view(world, e_local).to(torch.int64)
+    # per destination: counts, padded starts in the block, global scales,
+    # block rows, the block's first row here (where the results go back) and
+    # this rank's token count (buffer capacity)
+    tok = torch.full((world, 1), x.shape[0], dtype=torch.int64, device=dev)
+    meta_send = torch.cat([counts, rel, ag_bits, block, bounds[:-1].unsqueeze(1), tok], dim=1)
+    meta_send = meta_send.to(torch.int32).contiguous()
+    meta_recv = torch.empty_like(meta_send)
+    dist.all_to_all_single(meta_recv, meta_send, group=peers.group)
+    # one device-to-host read: block rows to each destination, rows from each
+    # source, where they go back in the source, token counts, block bounds,
+    # and each source's per-expert row starts inside its block
+    host = torch.cat([block.squeeze(1), meta_recv[:, 3 * e_local:].t().reshape(-1).to(torch.int64), bounds,
+                      meta_recv[:, e_local:2 * e_local].reshape(-1).to(torch.int64)]).cpu().tolist()
+    send_rows, recv_rows = host[:world], host[world:2 * world]
+    src_row0, tokens_all = host[2 * world:3 * world], host[3 * world:4 * world]
+    lo = host[4 * world:5 * world + 1]
+    rel_host = [host[5 * world + 1 + i * e_local:5 * world + 1 + (i + 1) * e_local] for i in range(world)]
+    max_tokens = max(tokens_all)
+    peers.ensure(_padded(max_tokens * top_k + 127 * e_local), _padded(max_tokens * top_k + 127 * num_experts),
+                 q.shape[1], sf.shape[1], x.shape[1])
+
+    # outbound rows, on the copy engines, into every destination's slot for this rank
+    quantized = torch.cuda.Event()
+    quantized.record(compute)
+    streams = peers.streams
+    for k, d in enumerate(d for d in range(world) if d != rank and send_rows[d]):
+        st = streams[k % len(streams)]
+        st.wait_event(quantized)
+        if peers.ready is not None:
+            st.wait_event(peers.ready)
+        dq, dsf = peers.recv_slot(d, rank)
+        peers.copy(dq, q.data_ptr() + lo[d] * q.shape[1], send_rows[d] * q.shape[1], st)
+        peers.copy(dsf, sf.data_ptr() + lo[d] * sf.shape[1], send_rows[d] * sf.shape[1], st)
+    for st in streams:
+        q.record_stream(st)
+        sf.record_stream(st)
+
+    seg_counts = meta_recv[:, :e_local]
+    seg_starts = torch.cat([meta_recv[:, e_local:2 * e_local], meta_recv[:, 3 * e_local:3 * e_local + 1]], dim=1)
+    seg_global = meta_recv[:, 2 * e_local:3 * e_local].contiguous().view(torch.float32)
+    back = peers.back_view(lo[world])
+    returned = [0]
+
+    def run(src: int, a: int, b: int) -> None:
+        """Local experts [a, b) on the rows of source ``src``; the results go
+        to their rows of the source's padded layout."""
+        r0 = rel_host[src][a]
+        r1 = rel_host[src][b] if b < e_local else recv_rows[src]
+        if r1 <= r0:
+            return
+        if src == rank:
+            sq, ssf = q[lo[rank] + r0:lo[rank] + r1], sf[lo[rank] + r0:lo[rank] + r1]
+        else:
+            rq, rsf = peers.recv_views(src, recv_rows[src])
+            sq, ssf = rq[r0:r1], rsf[r0:r1]
+        res = backend.experts(sq, ssf, seg_counts[src, a:b].contiguous(),
+                              (seg_starts[src, a:b + 1] - r0).to(torch.int32), seg_global[src, a:b].contiguous(),
+                              a, b)
+        if src == rank:
+            back[lo[rank] + r0:lo[rank] + r1].copy_(res)
+            return
+        done = torch.cuda.Event()
+        done.record(compute)
+        st = streams[returned[0] % len(streams)]
+        returned[0] += 1
+        st.wait_event(done)
+        peers.copy(peers.back_row(src, src_row0[src] + r0), res.data_ptr(), (r1 - r0) * x.shape[1] * 2, st)
+        res.record_stream(st)
+
+    # most of this rank's own rows while its rows travel out (half on 2
+    # ranks, three quarters on more, where more rows leave); the other
+    # sources in rotating order, in `chunks` expert groups so each result
+    # travels back while the next group computes; the rest of the own rows
+    # last, while the final results travel
+    tail = e_local // (2 if world <= 2 else 4)
+    half = e_local - tail
+    run(rank, 0, half)
+    for st in streams:
+        compute.wait_stream(st)
+    peers.barrier(compute)  # every slot of this rank is filled
+    groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
+    for j in range(1, world):
+        for a, b in groups:
+            run((rank + j) % world, a, b)
+    run(rank, half, e_local)
+    for st in streams:
+        compute.wait_stream(st)
+    peers.barrier(compute)  # every result for this rank's rows has landed
+    peers.ready = torch.cuda.Event()
+    peers.ready.record(compute)
+    return backend.combine(back, routing, scaling, shared)
+
+
 class ExpertParallelRoutedExperts(torch.nn.Module):
     """The routed-bank protocol (``routed_forward`` /
     ``routed_forward_with_shared``) over an expert-sharded bank: this rank holds
@@ -216,39 +467,59 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
     backend = "b200_sm100a_tcgen05_nvfp4_expert_parallel"
     ACCEPTS_DISPATCH = False
 
-    def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *, transfer_sms: int = 16,
-                 chunks: int | None = None) -> None:
+    def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *, transport: str = "peer",
+                 transfer_sms: int = 16, chunks: int | None = None) -> None:
+        """``transport="peer"``: rows move on the copy engines into the peers'
+        mapped buffers (``exchange_forward_peer``); ``"nccl"``: NCCL
+        point-to-point transfers (``exchange_forward``), with ``transfer_sms``
+        SMs kept free of the expert GEMMs for NCCL's kernels."""
         super().__init__()
         world = dist.get_world_size(group)
         if bank.num_experts * world != num_experts:
             raise ValueError("the local bank must hold num_experts / world experts")
+        if transport not in ("peer", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
         self.bank = bank
         self.num_experts = num_experts
         self.group = group
         self.chunks = chunks
-        self._backend = CudaBackend(bank, transfer_sms if world > 1 else 0)
+        self.transport = transport if world > 1 else "nccl"
+        self._backend = CudaBackend(bank, transfer_sms if world > 1 and self.transport == "nccl" else 0)
+        self._peers = PeerExchange(group, bank.gate_up_q.device) if self.transport == "peer" else None
 
     @classmethod
-    def from_packed(cls, state: Mapping[str, Tensor], group=None) -> ExpertParallelRoutedExperts:
+    def from_packed(cls, state: Mapping[str, Tensor], group=None, **kwargs) -> ExpertParallelRoutedExperts:
         """Shard a full packed bank (reference buffer layout) over ``group``."""
         rank, world = dist.get_rank(group), dist.get_world_size(group)
         e = state["gate_up_q"].shape[0]
-        return cls(B200NVFP4RoutedExperts.from_packed(shard_packed_state(state, rank, world)), e, group)
+        return cls(B200NVFP4RoutedExperts.from_packed(shard_packed_state(state, rank, world)), e, group, **kwargs)
 
     def prepare(self) -> None:
         self.bank.prepare()
 
+    def _forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, scaling: float, shared: Tensor | None) -> Tensor:
+        if self._peers is not None:
+            return exchange_forward_peer(x, top_idx, gate, num_experts=self.num_experts, scaling=scaling,
+                                         backend=self._backend, peers=self._peers, shared=shared,
+                                         chunks=self.chunks or 2)
+        return exchange_forward(x, top_idx, gate, num_experts=self.num_experts, scaling=scaling,
+                                backend=self._backend, group=self.group, shared=shared, chunks=self.chunks)
+
     def routed_forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int = 0,
                        dispatch=None) -> Tensor:
         self.bank._check(x, top_idx, gate, scaling, max(chunk_size, x.shape[0], 1))
-        return exchange_forward(x, top_idx, gate, num_experts=self.num_experts, scaling=float(scaling),
-                                backend=self._backend, group=self.group, chunks=self.chunks)
+        return self._forward(x, top_idx, gate, float(scaling), None)
 
     def routed_forward_with_shared(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float,
                                    chunk_size: int = 0, shared: Tensor, dispatch=None) -> Tensor:
         self.bank._check(x, top_idx, gate, scaling, max(chunk_size, x.shape[0], 1))
-        return exchange_forward(x, top_idx, gate, num_experts=self.num_experts, scaling=float(scaling),
-                                backend=self._backend, group=self.group, shared=shared, chunks=self.chunks)
+        return self._forward(x, top_idx, gate, float(scaling), shared)
+
+    def close(self) -> None:
+        """Unmap and free the peer buffers (collective over ``group``)."""
+        if self._peers is not None:
+            self._peers.close()
 
 
-__all__ = ["CudaBackend", "ExpertParallelRoutedExperts", "exchange_forward", "shard_packed_state"]
+__all__ = ["CudaBackend", "ExpertParallelRoutedExperts", "PeerExchange", "exchange_forward", "exchange_forward_peer",
+           "shard_packed_state"]

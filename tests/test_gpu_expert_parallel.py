@@ -5,7 +5,10 @@
   the bank); after the emulated return and combine, every source's output must
   equal the single-GPU bank forward of its tokens bit for bit;
 * the real exchange (``exchange_forward``) over NCCL with one rank;
-* the real exchange over NCCL with two ranks when two GPUs are visible.
+* the real exchange over NCCL with two ranks when two GPUs are visible;
+* the copy-engine exchange into IPC-mapped peer buffers with two ranks when
+  two GPUs are visible: several forwards with changing token counts (buffer
+  reuse and growth), each bit for bit equal to the single-GPU bank.
 """
 
 from __future__ import annotations
@@ -140,7 +143,8 @@ def _nccl_worker(rank, world, port, results):
         t, c, e, k, f = 900, 512, 8, 2, 256
         state = _packed(e, c, f)
         dev = torch.device("cuda", rank)
-        ep = p.expert_parallel.ExpertParallelRoutedExperts.from_packed({n: v.to(dev) for n, v in state.items()})
+        ep = p.expert_parallel.ExpertParallelRoutedExperts.from_packed({n: v.to(dev) for n, v in state.items()},
+                                                                      transport="nccl")
         full = p.B200NVFP4RoutedExperts.from_packed({n: v.clone() for n, v in state.items()}).to(dev)
         x, top, gate, shared = (v.to(dev) for v in _tokens(20 + rank, t, c, e, k, skew=rank == 1))
         got = ep.routed_forward_with_shared(x, top, gate, scaling=2.5, shared=shared)
@@ -161,6 +165,55 @@ def test_exchange_forward_two_ranks_nccl(P):
     results = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, results)) for r in range(2)]
+    for proc in procs:
+        proc.start()
+    res = {}
+    for _ in range(2):
+        rank, ok, info = results.get(timeout=300)
+        res[rank] = (ok, info)
+    for proc in procs:
+        proc.join(timeout=120)
+    assert all(ok for ok, _ in res.values()), res
+
+
+def _peer_worker(rank, world, port, results):
+    try:
+        torch.cuda.set_device(rank)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=60))
+        dist.init_process_group("nccl", store=store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        p = pkg()
+        c, e, k, f = 512, 8, 2, 256
+        state = _packed(e, c, f)
+        dev = torch.device("cuda", rank)
+        ep = p.expert_parallel.ExpertParallelRoutedExperts.from_packed({n: v.to(dev) for n, v in state.items()})
+        assert ep.transport == "peer"
+        full = p.B200NVFP4RoutedExperts.from_packed({n: v.clone() for n, v in state.items()}).to(dev)
+        ok = True
+        # token counts differ between ranks and grow (buffer growth), then shrink (reuse)
+        for it, t in enumerate([(900, 700), (640, 1500), (300, 200), (1500, 1500)]):
+            x, top, gate, shared = (v.to(dev) for v in _tokens(40 + 7 * it + rank, t[rank], c, e, k, skew=rank == 1))
+            got = ep.routed_forward_with_shared(x, top, gate, scaling=2.5, shared=shared)
+            want = full.routed_forward_with_shared(x, top, gate, scaling=2.5, chunk_size=t[rank], shared=shared)
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(got.view(torch.int16), want.view(torch.int16)))
+        ep.close()
+        results.put((rank, ok and p.capi.device_error(rank) == 0, ""))
+        dist.barrier()
+    except Exception:
+        results.put((rank, False, traceback.format_exc()[-600:]))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_two_ranks(P):
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, results)) for r in range(2)]
     for proc in procs:
         proc.start()
     res = {}

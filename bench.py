@@ -76,6 +76,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ep-chunks", type=int, default=None,
                     help="expert groups per source in the expert-parallel exchange (N > 1)")
+    ap.add_argument("--copy-streams", type=int, default=4, help="copy streams of the peer exchange (N > 1)")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel row exchange (N > 1): copy engines into IPC-mapped peer buffers, or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -402,7 +403,8 @@ def run_expert_parallel(args, cfg):
     bank = pkg.pack_routed_experts(gu.contiguous(), down.contiguous(), keep_on_device=True)
     del gu, down
     bank.prepare()
-    ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e, transport=args.transport, chunks=args.ep_chunks)
+    ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e, transport=args.transport, chunks=args.ep_chunks,
+                                                         copy_streams=args.copy_streams)
     grouter = torch.Generator().manual_seed(11)
     router = (torch.randn(e, c, generator=grouter) * (1.0 / c) ** 0.5).to(dev)
     terms = ops.split_router_weight(router)

@@ -74,8 +74,9 @@ class CudaBackend:
         return ops.quantize_gather(x, routing, routing.act_global)
 
     def experts(self, q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
-                first: int, last: int) -> Tensor:
-        """Segments of local experts [first, last) (segment v: expert first + v % (last - first))."""
+                first: int, last: int, out_ptr: int | None = None) -> Tensor | None:
+        """Segments of local experts [first, last) (segment v: expert first + v % (last - first));
+        with ``out_ptr`` the rows are written to that device address instead."""
         kw = self.bank.kernel_weights()
         b = self.bank
         n = b.num_experts
@@ -86,7 +87,7 @@ class CudaBackend:
         return ops.expert_forward(q, sf, counts, starts, act_global, part(kw.gate_up_q), part(kw.gate_up_sf),
                                   b.gate_up_global[first:last], part(b.down_q), part(kw.down_sf),
                                   b.down_global[first:last], gate_up_sf_layout=kw.gate_up_sf_layout,
-                                  down_sf_layout=kw.down_sf_layout, sm_limit=self.sm_limit)
+                                  down_sf_layout=kw.down_sf_layout, sm_limit=self.sm_limit, out_ptr=out_ptr)
 
     def combine(self, rows: Tensor, routing, scaling: float, shared: Tensor | None) -> Tensor:
         return ops.combine(rows, routing, scaling, rows_rescaled=True, shared=shared)
@@ -419,12 +420,16 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
         else:
             rq, rsf = peers.recv_views(src, recv_rows[src])
             sq, ssf = rq[r0:r1], rsf[r0:r1]
-        res = backend.experts(sq, ssf, seg_counts[src, a:b].contiguous(),
-                              (seg_starts[src, a:b + 1] - r0).to(torch.int32), seg_global[src, a:b].contiguous(),
-                              a, b)
-        if src == rank:
-            back[lo[rank] + r0:lo[rank] + r1].copy_(res)
+        counts, starts = seg_counts[src, a:b].contiguous(), (seg_starts[src, a:b + 1] - r0).to(torch.int32)
+        ag = seg_global[src, a:b].contiguous()
+        if src == rank:  # own rows: the down GEMM writes into the combine's buffer
+            backend.experts(sq, ssf, counts, starts, ag, a, b, out_ptr=peers.back_row(rank, lo[rank] + r0))
             return
+        # other sources: local result, then a copy engine writes it into the
+        # source's mapped buffer while the next group computes (the down GEMM
+        # storing into the peer's buffer itself measured slower: its epilogue
+        # becomes bound by the NVLink writes)
+        res = backend.experts(sq, ssf, counts, starts, ag, a, b)
         done = torch.cuda.Event()
         done.record(compute)
         st = streams[returned[0] % len(streams)]
@@ -468,7 +473,7 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
     ACCEPTS_DISPATCH = False
 
     def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *, transport: str = "peer",
-                 transfer_sms: int = 16, chunks: int | None = None) -> None:
+                 transfer_sms: int = 16, chunks: int | None = None, copy_streams: int = 4) -> None:
         """``transport="peer"``: rows move on the copy engines into the peers'
         mapped buffers (``exchange_forward_peer``); ``"nccl"``: NCCL
         point-to-point transfers (``exchange_forward``), with ``transfer_sms``
@@ -485,7 +490,8 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
         self.chunks = chunks
         self.transport = transport if world > 1 else "nccl"
         self._backend = CudaBackend(bank, transfer_sms if world > 1 and self.transport == "nccl" else 0)
-        self._peers = PeerExchange(group, bank.gate_up_q.device) if self.transport == "peer" else None
+        self._peers = (PeerExchange(group, bank.gate_up_q.device, copy_streams) if self.transport == "peer"
+                       else None)
 
     @classmethod
     def from_packed(cls, state: Mapping[str, Tensor], group=None, **kwargs) -> ExpertParallelRoutedExperts:

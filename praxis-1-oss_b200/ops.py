@@ -327,11 +327,14 @@ def interleave_gate_up(q: Tensor, sf: Tensor) -> tuple[Tensor, Tensor]:
 def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
                    gate_up_q: Tensor, gate_up_sf: Tensor, gate_up_global: Tensor, down_q: Tensor,
                    down_sf: Tensor, down_global: Tensor, *, gate_up_sf_layout: int, down_sf_layout: int,
-                   sm_limit: int = 0) -> Tensor:
+                   sm_limit: int = 0, out_ptr: int | None = None) -> Tensor | None:
     """The expert-rank half of an expert-parallel layer
     (``praxis_b200_expert_forward``): received NVFP4 rows in padded segments
     (segment v = source * E_local + local expert, ``counts[v]`` rows from
-    ``starts[v]``) -> rescaled bf16 down-projection rows in the same layout."""
+    ``starts[v]``) -> rescaled bf16 down-projection rows in the same layout.
+    With ``out_ptr`` (a 16-byte aligned device address of ``rows`` x C bf16,
+    e.g. in a peer's mapped buffer) the down GEMM writes the rows there and
+    nothing is returned."""
     _need(q, "q", torch.uint8, 2)
     rows, c_half = q.shape
     c = c_half * 2
@@ -343,7 +346,7 @@ def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_gl
     _need(act_global, "act_global", torch.float32, 1, q.device)
     if starts.numel() != segments + 1 or act_global.numel() != segments:
         raise ValueError("starts / act_global do not match the segment count")
-    out = torch.empty(rows, c, dtype=BF16, device=q.device)
+    out = torch.empty(rows, c, dtype=BF16, device=q.device) if out_ptr is None else None
     lib = capi.load()
     ws_size = int(lib.praxis_b200_expert_workspace_size(rows, segments, c, f))
     ws = torch.empty(max(ws_size, 1), dtype=torch.uint8, device=q.device)
@@ -353,7 +356,8 @@ def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_gl
         gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(), down_q=down_q.data_ptr(),
         down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(), gate_up_sf_layout=int(gate_up_sf_layout),
         down_sf_layout=int(down_sf_layout),
-        dim=c, hidden=f, experts=e_local, sm_limit=int(sm_limit), rows_out=out.data_ptr(), workspace=ws.data_ptr(),
+        dim=c, hidden=f, experts=e_local, sm_limit=int(sm_limit),
+        rows_out=out.data_ptr() if out is not None else int(out_ptr), workspace=ws.data_ptr(),
         workspace_size=ws.numel(), device=_dev(q), stream=torch.cuda.current_stream(q.device).cuda_stream,
     )
     capi.check(lib.praxis_b200_expert_forward(C.byref(args)))

@@ -11,11 +11,14 @@ rank (its own tokens are one dispatch chunk):
 2. NVFP4 quantization of the outbound rows on the source rank;
 3. exchange of the per-(destination, expert) counts, padded offsets and
    global scales (one small all-to-all), then of the FP4 rows and their
-   compact scale atoms (one batch of point-to-point transfers): destination
-   d receives rows [pcsr[d * E/R], pcsr[(d + 1) * E/R]) of every source,
-   whole 128-row tiles, so the swizzled scale atoms travel as contiguous
-   bytes; the rank's own rows for its own experts do not move and are
-   computed while the transfers run;
+   compact scale atoms: destination d receives rows [pcsr[d * E/R],
+   pcsr[(d + 1) * E/R]) of every source, whole 128-row tiles, so the
+   swizzled scale atoms travel as contiguous bytes; the rank's own rows for
+   its own experts do not move and are computed while the transfers run.
+   ``exchange_forward_peer`` (the default on GPUs) writes the rows with the
+   copy engines into the destinations' IPC-mapped buffers
+   (``PeerExchange``); ``exchange_forward`` uses NCCL point-to-point
+   transfers (and runs over gloo for the CPU tests);
 4. on the expert rank, per source: gate/up GEMM + SwiGLU, hidden quantize with
    one global scale per (source, expert) segment, down GEMM + rescale
    (``praxis_b200_expert_forward``);

@@ -469,27 +469,10 @@ def run_expert_parallel(args, cfg):
                              "through its local experts' weights, one launch sequence"}
     e2e = None
     if not args.no_e2e:
-        host_in = x_cpu.pin_memory()
-        host_out = torch.empty(t, c, dtype=torch.bfloat16).pin_memory()
-        xin = torch.empty_like(x)
-        for _ in range(2):
-            xin.copy_(host_in, non_blocking=True)
-            host_out.copy_(step(xin), non_blocking=True)
         torch.cuda.synchronize()
         dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            xin.copy_(host_in, non_blocking=True)
-            host_out.copy_(step(xin), non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1) / args.steps
-        te = torch.tensor([ems], device=dev)
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        ems = float(te.item())
-        e2e = {"value": t * world / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems,
-               "h2d_bytes_per_step": host_in.numel() * 2 * world, "d2h_bytes_per_step": host_out.numel() * 2 * world}
+        out = torch.empty(t, c, dtype=torch.bfloat16, device=dev)
+        e2e = time_e2e(pkg, lambda xin, yout: yout.copy_(step(xin)), x_cpu, out, args, dev, t, world)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -628,7 +611,7 @@ def time_e2e(pkg, layer, x_cpu, out, args, dev, t, world):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
     return {"value": t * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-            "h2d_bytes_per_step": host_in.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 2}
+            "h2d_bytes_per_step": host_in.numel() * 2 * world, "d2h_bytes_per_step": host_out.numel() * 2 * world}
 
 
 def main():

@@ -237,9 +237,11 @@ __device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, fl
     float2 y0;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0.x) : "f"(d.x));
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0.y) : "f"(d.y));
+    // one residual correction of the estimate; d = 1 + 2^t takes one value
+    // per bf16 gate value, and every one of them is checked against the IEEE
+    // division (the exhaustive SwiGLU test)
     const float2 nd = make_float2(-d.x, -d.y);
-    const float2 y1 = fma2_rn(y0, fma2_rn(nd, y0, one), y0);
-    s = fma2_rn(fma2_rn(nd, y1, one), y1, y1);
+    s = fma2_rn(fma2_rn(nd, y0, one), y0, y0);
   }
   const float2 gs = mul2_rn(g, s);
   const float2 silu = unpack_bf16x2(cvt_bf16x2(gs.x, gs.y));

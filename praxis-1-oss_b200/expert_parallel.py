@@ -259,13 +259,16 @@ class PeerExchange:
     def _release(self) -> None:
         lib = capi.load()
         dev = self.device.index
+        if self._local:
+            # this rank's copies into the peers' buffers are done before the
+            # mappings go away
+            torch.cuda.synchronize(self.device)
         for name, ptrs in self._peer.items():
             for r, ptr in enumerate(ptrs):
                 if r != self.rank and ptr:
                     capi.check(lib.praxis_b200_ipc_close(C.c_void_p(ptr), dev))
         self._peer = {}
         if self._local:
-            torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)  # every peer has closed its mappings
             for ptr, _ in self._local.values():
                 capi.check(lib.praxis_b200_ipc_free(C.c_void_p(ptr), dev))

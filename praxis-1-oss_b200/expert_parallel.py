@@ -417,6 +417,8 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     def run(src: int, a: int, b: int) -> None:
         """Local experts [a, b) on the rows of source ``src``; the results go
         to their rows of the source's padded layout."""
+        if a >= b:
+            return
         r0 = rel_host[src][a]
         r1 = rel_host[src][b] if b < e_local else recv_rows[src]
         if r1 <= r0:

@@ -23,6 +23,8 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const int32_t* __restrict__ pcsr, const float* __restrict__ h_global, const uint32_t* __restrict__ h_amax,
     const float* __restrict__ w_global, int rows_rescaled, float scaling, const uint16_t* __restrict__ shared,
     uint16_t* __restrict__ out, int64_t tokens, int top_k, int experts) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   __shared__ int64_t s_src[8][8];
   __shared__ float s_scale[8][8], s_mult[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -113,9 +115,8 @@ int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const in
   const int64_t blocks = (tokens + 7) / 8;
   // eight 16-byte loads in flight per lane for every top_k
 #define PRAXIS_COMBINE(KMAX, U)                                                                                    \
-  combine_kernel<KMAX, U><<<(unsigned)blocks, 256, 0, stream>>>(rows, cols, inverse, top_idx, gate, csr, pcsr,      \
-                                                               h_global, h_amax, w_global, rows_rescaled, scaling, \
-                                                               shared, out, tokens, top_k, experts)
+  launch_pdl(combine_kernel<KMAX, U>, dim3((unsigned)blocks), dim3(256), 0, stream, rows, cols, inverse, top_idx, gate, \
+             csr, pcsr, h_global, h_amax, w_global, rows_rescaled, scaling, shared, out, tokens, top_k, experts)
   if (top_k == 1) PRAXIS_COMBINE(1, 8);
   else if (top_k == 2) PRAXIS_COMBINE(2, 4);
   else if (top_k <= 4) PRAXIS_COMBINE(4, 2);

@@ -34,6 +34,16 @@ __device__ __forceinline__ void record_error(unsigned int code) {
   atomicCAS(&g_device_error, 0u, code);
 }
 
+// Programmatic dependent launch. The hot-path kernels are launched with
+// launch_pdl (kernels.h): a kernel's CTAs may be scheduled while the previous
+// kernel of the stream is finishing, so its launch latency overlaps that
+// kernel's tail. pdl_wait(), the first statement of each such kernel, blocks
+// until the previous kernel has completed and its writes are visible (a no-op
+// for a kernel launched without the attribute); pdl_trigger() lets the next
+// kernel be scheduled once every CTA of this one has started.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool error_raised() {
   return *((volatile unsigned int*)&g_device_error) != 0u;
 }

@@ -38,6 +38,8 @@ __device__ __forceinline__ int clamp_expert(int64_t e, int experts) {
 // Row max |x| (bf16), praxis/kernels/nvfp4_moe.py:15-21
 // ---------------------------------------------------------------------------
 __global__ void row_amax_kernel(const uint16_t* __restrict__ x, int64_t rows, int cols, uint16_t* __restrict__ out) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   const int warps = blockDim.x >> 5;
   const int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -64,6 +66,8 @@ __global__ void row_amax_kernel(const uint16_t* __restrict__ x, int64_t rows, in
 __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ row_amax,
                                       int64_t positions, int top_k, int experts, int seg_len, int segments,
                                       int32_t* __restrict__ seg_count, uint32_t* __restrict__ seg_max) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   extern __shared__ uint32_t s_dc[];
   uint32_t* hist = s_dc;                                  // [warps][experts]
   uint32_t* hmax = s_dc + kDispatchWarps * experts;       // [warps][experts]
@@ -146,6 +150,8 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
     int64_t positions, int align, int32_t* __restrict__ offsets, int32_t* __restrict__ csr,
     int32_t* __restrict__ pcsr, TileEntry* __restrict__ tiles, int max_tiles, int32_t* __restrict__ num_tiles,
     float* __restrict__ act_global, uint32_t* __restrict__ act_amax_bits) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   __shared__ int s_warp[32];
   __shared__ int s_part[1024];
   __shared__ uint32_t s_pmax[1024];
@@ -259,6 +265,8 @@ __global__ void __launch_bounds__(1024) segment_tiles_kernel(const int32_t* __re
                                                              const int32_t* __restrict__ starts, int segments,
                                                              TileEntry* __restrict__ tiles, int max_tiles,
                                                              int32_t* __restrict__ num_tiles) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   __shared__ int s_warp[32];
   const int v = threadIdx.x;
   const int count = v < segments ? max(counts[v], 0) : 0;
@@ -300,7 +308,8 @@ __global__ void __launch_bounds__(1024) segment_tiles_kernel(const int32_t* __re
 int run_segment_tiles(const int32_t* counts, const int32_t* starts, int segments, TileEntry* tiles, int max_tiles,
                       int32_t* num_tiles, cudaStream_t stream) {
   if (segments < 1 || segments > 1024) return set_error(PRAXIS_B200_EINVAL, "segments must be 1..1024");
-  segment_tiles_kernel<<<1, 1024, 0, stream>>>(counts, starts, segments, tiles, max_tiles, num_tiles);
+  launch_pdl(segment_tiles_kernel, dim3(1), dim3(1024), 0, stream, counts, starts, segments, tiles, max_tiles,
+             num_tiles);
   return check_launch("segment_tiles");
 }
 
@@ -313,6 +322,8 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
                                         int64_t* __restrict__ order, int64_t* __restrict__ inverse,
                                         int64_t* __restrict__ tokens, int32_t* __restrict__ tokens32,
                                         uint16_t* __restrict__ sorted_gate) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   extern __shared__ int32_t s_cursor[];  // [warps][experts]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seg = blockIdx.x * kDispatchWarps + warp;
@@ -399,19 +410,19 @@ int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* r
     cudaFuncSetAttribute(dispatch_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDispatchWarps * kMaxExperts * 4);
     attr_done = true;
   }
-  dispatch_count_kernel<<<blocks, 32 * kDispatchWarps, smem_count, stream>>>(
-      top_idx, row_amax, positions, top_k, experts, seg_len, segments, seg_count, seg_max);
+  launch_pdl(dispatch_count_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_count, stream, top_idx, row_amax,
+             positions, top_k, experts, seg_len, segments, seg_count, seg_max);
   int rc = check_launch("dispatch_count");
   if (rc) return rc;
-  dispatch_scan_kernel<<<1, 1024, 0, stream>>>(seg_count, seg_max, segments, experts, positions, kTileRows, offsets,
-                                               csr, pcsr, tiles, max_tiles, num_tiles,
-                                               row_amax ? act_global : nullptr, row_amax ? act_amax_bits : nullptr);
+  launch_pdl(dispatch_scan_kernel, dim3(1), dim3(1024), 0, stream, seg_count, seg_max, segments, experts, positions,
+             (int)kTileRows, offsets, csr, pcsr, tiles, max_tiles, num_tiles, row_amax ? act_global : nullptr,
+             row_amax ? act_amax_bits : nullptr);
   rc = check_launch("dispatch_scan");
   if (rc) return rc;
   if (positions > 0) {
-    dispatch_scatter_kernel<<<blocks, 32 * kDispatchWarps, smem_scatter, stream>>>(
-        top_idx, gate, positions, top_k, experts, seg_len, segments, seg_count, csr, order, inverse, tokens_out,
-        tokens32, sorted_gate);
+    launch_pdl(dispatch_scatter_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_scatter, stream, top_idx, gate,
+               positions, top_k, experts, seg_len, segments, seg_count, csr, order, inverse, tokens_out, tokens32,
+               sorted_gate);
     rc = check_launch("dispatch_scatter");
   }
   return rc;
@@ -422,7 +433,7 @@ int run_row_amax(const uint16_t* x, int64_t rows, int cols, uint16_t* out, cudaS
   if (rows == 0) return PRAXIS_B200_OK;
   const int warps = 8;
   const int64_t blocks = (rows + warps - 1) / warps;
-  row_amax_kernel<<<(unsigned)blocks, 32 * warps, 0, stream>>>(x, rows, cols, out);
+  launch_pdl(row_amax_kernel, dim3((unsigned)blocks), dim3(32 * warps), 0, stream, x, rows, cols, out);
   return check_launch("row_amax");
 }
 

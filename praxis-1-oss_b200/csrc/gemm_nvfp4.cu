@@ -79,6 +79,8 @@ __host__ __device__ __forceinline__ int hidden_chunk(int blk) {
 
 template <int BLOCK_N, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constant__ GemmParams p) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   using S = GemmShape<BLOCK_N>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -372,6 +374,8 @@ __device__ __forceinline__ void st_global_v8(uint16_t* ptr, uint4 a, uint4 b) {
 template <int EPI, bool REP>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI == EPI_SWIGLU>::THREADS, 1)
     gemm_nvfp4_pair_kernel(const __grid_constant__ GemmParams p) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   constexpr bool DIRECT = EPI == EPI_SWIGLU;
   using S = PairShape<REP, DIRECT>;
   extern __shared__ uint8_t smem_raw[];
@@ -712,7 +716,7 @@ static int launch_gemm(const GemmParams& p, int max_tiles, cudaStream_t stream) 
   if (units <= 0) return PRAXIS_B200_OK;
   int grid = units < sm_count() ? units : sm_count();
   if (p.sm_limit > 0 && grid > p.sm_limit) grid = p.sm_limit;
-  kernel<<<grid, 192, S::SMEM_BYTES, stream>>>(p);
+  launch_pdl(kernel, dim3(grid), dim3(192), S::SMEM_BYTES, stream, p);
   return check_launch("gemm_nvfp4");
 }
 
@@ -787,7 +791,7 @@ static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t str
   if (units <= 0) return PRAXIS_B200_OK;
   int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
   if (p.sm_limit > 0 && clusters > p.sm_limit / 2) clusters = p.sm_limit / 2 > 0 ? p.sm_limit / 2 : 1;
-  kernel<<<2 * clusters, S::THREADS, S::SMEM_BYTES, stream>>>(p);
+  launch_pdl(kernel, dim3(2 * clusters), dim3(S::THREADS), S::SMEM_BYTES, stream, p);
   return check_launch("gemm_nvfp4_pair");
 }
 

@@ -7,6 +7,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace praxis {
@@ -40,6 +42,24 @@ struct GemmParams {
 // Records a message for praxis_b200_last_error and returns `code`.
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
+
+// Launch with programmatic stream serialization (the kernel starts with
+// pdl_wait(), common.cuh); returns the launch status.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 int sm_count();
 
 // f32(bf16(max(amax, 1e-12))) * f32(1/2688): the QAT global scale from the

@@ -130,6 +130,8 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
     const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int top_k, int experts,
     const TileEntry* __restrict__ tiles, const int32_t* __restrict__ num_tiles, int token_blocks,
     uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   __shared__ int64_t s_dest[8][8];
   __shared__ float s_g[8][8], s_ig[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -197,6 +199,8 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
     const uint16_t* __restrict__ x, int k_dim, const TileEntry* __restrict__ tiles,
     const int32_t* __restrict__ num_tiles, const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits,
     uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * 8 + warp;  // tile * 128 + row
   const int m = (int)(item / kTileRows);
@@ -292,6 +296,8 @@ __global__ void interleave_gate_up_kernel(const uint8_t* __restrict__ q, const u
 // ---------------------------------------------------------------------------
 __global__ void replicate_scales_kernel(const uint4* __restrict__ sf, int64_t chunks, int kb, int group_rows,
                                         uint4* __restrict__ out) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= chunks) return;
   const int64_t atom = i >> 5;
@@ -320,9 +326,9 @@ int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int6
   const int token_blocks = (int)((tokens + 7) / 8);
   const int grid = token_blocks + max_tiles;
   if (grid == 0) return PRAXIS_B200_OK;
-  quantize_gather_kernel<<<grid, 256, 0, stream>>>(x, tokens, k_dim, top_idx, inverse, csr, pcsr, globals, amax_bits,
-                                                   top_k, experts, tiles, num_tiles, token_blocks, q, sf,
-                                                   sf_layout == PRAXIS_B200_SF_REPLICATED);
+  launch_pdl(quantize_gather_kernel, dim3(grid), dim3(256), 0, stream, x, tokens, k_dim, top_idx, inverse, csr, pcsr,
+             globals, amax_bits, top_k, experts, tiles, num_tiles, token_blocks, q, sf,
+             sf_layout == PRAXIS_B200_SF_REPLICATED);
   return check_launch("quantize_gather");
 }
 
@@ -335,8 +341,8 @@ int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, cons
     return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
   const int64_t blocks = (int64_t)max_tiles * kTileRows / 8;
   if (blocks == 0) return PRAXIS_B200_OK;
-  quantize_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, k_dim, tiles, num_tiles, globals, amax_bits, q, sf,
-                                                             sf_layout == PRAXIS_B200_SF_REPLICATED);
+  launch_pdl(quantize_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, x, k_dim, tiles, num_tiles, globals,
+             amax_bits, q, sf, sf_layout == PRAXIS_B200_SF_REPLICATED);
   return check_launch("quantize_rows");
 }
 
@@ -374,8 +380,8 @@ int run_replicate_scales(const uint8_t* sf, int64_t rows, int k_dim, int group_r
                      group_rows);
   const int64_t chunks = rows * (k_dim / 16) / 16;
   if (chunks == 0) return PRAXIS_B200_OK;
-  replicate_scales_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const uint4*>(sf), chunks, k_dim / 16, group_rows, reinterpret_cast<uint4*>(out));
+  launch_pdl(replicate_scales_kernel, dim3((unsigned)((chunks + 255) / 256)), dim3(256), 0, stream,
+             reinterpret_cast<const uint4*>(sf), chunks, k_dim / 16, group_rows, reinterpret_cast<uint4*>(out));
   return check_launch("replicate_scales");
 }
 

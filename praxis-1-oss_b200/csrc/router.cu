@@ -38,6 +38,8 @@ __global__ void __launch_bounds__(192, 1) router_logits_kernel(
     const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w, int64_t tokens, int dim,
     int experts, int splits, int e_pad, int stages, uint32_t tmem_cols, float* __restrict__ logits,
     uint16_t* __restrict__ row_amax) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int b_bytes = splits * e_pad * 128;
@@ -226,6 +228,8 @@ template <int P>
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
                                                     int64_t tokens, int experts, int top_k, int activation,
                                                     int64_t* __restrict__ top_idx, uint16_t* __restrict__ gate) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
@@ -442,8 +446,8 @@ int run_router_logits(const uint16_t* x, const uint16_t* w, int splits, int64_t 
   rc = make_bf16_map(&mw, w, (int64_t)splits * experts, dim, e_pad);
   if (rc) return rc;
   const int64_t blocks = (tokens + kRouterBM - 1) / kRouterBM;
-  router_logits_kernel<<<(unsigned)blocks, 192, smem, stream>>>(mx, mw, tokens, dim, experts, splits, e_pad, stages,
-                                                                 tmem_cols, logits, row_amax);
+  launch_pdl(router_logits_kernel, dim3((unsigned)blocks), dim3(192), smem, stream, mx, mw, tokens, dim, experts,
+             splits, e_pad, stages, tmem_cols, logits, row_amax);
   return check_launch("router_logits");
 }
 
@@ -456,13 +460,17 @@ int run_route(const float* logits, const float* bias, int64_t tokens, int expert
   if (tokens == 0) return PRAXIS_B200_OK;
   const unsigned blocks = (unsigned)((tokens + 7) / 8);
   if (experts <= 32)
-    route_kernel<1><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+    launch_pdl(route_kernel<1>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
+               top_idx, gate);
   else if (experts <= 64)
-    route_kernel<2><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+    launch_pdl(route_kernel<2>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
+               top_idx, gate);
   else if (experts <= 128)
-    route_kernel<4><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+    launch_pdl(route_kernel<4>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
+               top_idx, gate);
   else
-    route_kernel<8><<<blocks, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, activation, top_idx, gate);
+    launch_pdl(route_kernel<8>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
+               top_idx, gate);
   return check_launch("route");
 }
 

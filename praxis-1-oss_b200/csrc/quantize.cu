@@ -62,12 +62,20 @@ __device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 
 // conversion. For finite inputs v * rc stays finite (|v| <= amax, the scale
 // is at least 2^-6), where the saturating conversion alone gives the same
 // codes; blocks holding an infinity or NaN (has_nan) take the clamp.
+// rc_table (optional): rc_table[b] = div_rn(inv_g, e4m3 value of byte b) for
+// the scale bytes 0x08..0x7E the clamp allows (rc_table_entry), one table per
+// global scale, replacing the second division.
+__device__ __forceinline__ float rc_table_entry(float inv_g, uint32_t byte) {
+  return div_rn(inv_g, e4m3_byte_to_f32(byte));
+}
+
 __device__ __forceinline__ void quantize16(const float (&v)[16], float amax, float g, float inv_g, bool has_nan,
-                                           uint32_t& lo, uint32_t& hi, uint32_t& sf) {
+                                           uint32_t& lo, uint32_t& hi, uint32_t& sf,
+                                           const float* rc_table = nullptr) {
   const float bs = mul_rn(amax, kOneSixth);
   const float sfv = fminf(fmaxf(div_rn(bs, g), 0.015625f), 448.0f);
   sf = f32_to_e4m3_byte(sfv);
-  const float rc = div_rn(inv_g, e4m3_byte_to_f32(sf));
+  const float rc = rc_table != nullptr ? rc_table[sf] : rc_table_entry(inv_g, sf);
   const float2 rc2 = make_float2(rc, rc);
   float2 n[8];
 #pragma unroll
@@ -209,6 +217,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
   const int64_t row = (int64_t)t.row0 + (item % kTileRows);
   const float g = expert_global(globals, amax_bits, t.expert);
   const float ig = div_rn(1.0f, g);
+  // the block's 8 rows share one expert (tiles are 128 rows): one table of
+  // the second division for all of them
+  __shared__ float s_rc[128];
+  if (threadIdx.x < 128) s_rc[threadIdx.x] = rc_table_entry(ig, threadIdx.x);
+  __syncthreads();
   const int kb = k_dim / 16;
   const uint16_t* xr = x + row * k_dim;
   for (int j0 = 0; j0 < kb; j0 += 32) {
@@ -220,7 +233,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
       float amax;
       bool has_nan;
       load16_bf16(xr + j * 16, v, amax, has_nan);
-      quantize16(v, amax, g, ig, has_nan, lo, hi, sfb);
+      quantize16(v, amax, g, ig, has_nan, lo, hi, sfb, s_rc);
       *reinterpret_cast<uint2*>(q + row * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
     }
     store_sf_group(sf, row, j, kb, sfb, active, rep);

@@ -77,6 +77,8 @@ def parse():
     ap.add_argument("--ep-chunks", type=int, default=None,
                     help="expert groups per source in the expert-parallel exchange (N > 1)")
     ap.add_argument("--copy-streams", type=int, default=4, help="copy streams of the peer exchange (N > 1)")
+    ap.add_argument("--sm-copy-fraction", type=float, default=0.0,
+                    help="share of the peer exchange's bytes moved by a copy kernel on 16 SMs (N > 1)")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel row exchange (N > 1): copy engines into IPC-mapped peer buffers, or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -404,7 +406,8 @@ def run_expert_parallel(args, cfg):
     del gu, down
     bank.prepare()
     ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e, transport=args.transport, chunks=args.ep_chunks,
-                                                         copy_streams=args.copy_streams)
+                                                         copy_streams=args.copy_streams,
+                                                         sm_copy_fraction=args.sm_copy_fraction)
     grouter = torch.Generator().manual_seed(11)
     router = (torch.randn(e, c, generator=grouter) * (1.0 / c) ** 0.5).to(dev)
     terms = ops.split_router_weight(router)

@@ -344,6 +344,10 @@ int praxis_b200_ipc_handle(const void* ptr, int device, void* handle);
 int praxis_b200_ipc_open(const void* handle, int device, void** ptr);
 int praxis_b200_ipc_close(void* ptr, int device);
 int praxis_b200_copy_async(void* dst, const void* src, size_t bytes, int device, void* stream);
+/* The same copy done by `ctas` CTAs of SMs (16-byte loads here, stores to dst,
+ * e.g. a mapped peer buffer over NVLink): runs beside the copy engines.
+ * dst, src and bytes multiples of 16. */
+int praxis_b200_sm_copy(void* dst, const void* src, size_t bytes, int ctas, int device, void* stream);
 
 #ifdef __cplusplus
 }

@@ -535,6 +535,30 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
 // ---------------------------------------------------------------------------
 // Peer buffers (CUDA IPC) and copies for the expert-parallel exchange
 // ---------------------------------------------------------------------------
+}  // extern "C"
+
+namespace praxis {
+// Copy by the SMs: 16-byte loads of this GPU's memory and stores to dst,
+// which may be a peer's mapped buffer (NVLink writes); four loads in flight
+// per thread.
+constexpr int kPeerCopyThreads = 512;
+__global__ void __launch_bounds__(kPeerCopyThreads) peer_copy_kernel(const uint4* __restrict__ src,
+                                                                     uint4* __restrict__ dst, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * kPeerCopyThreads;
+  int64_t i = (int64_t)blockIdx.x * kPeerCopyThreads + threadIdx.x;
+  for (; i + 3 * stride < n; i += 4 * stride) {
+    const uint4 a = ldg_stream(src + i), b = ldg_stream(src + i + stride);
+    const uint4 c = ldg_stream(src + i + 2 * stride), d = ldg_stream(src + i + 3 * stride);
+    dst[i] = a;
+    dst[i + stride] = b;
+    dst[i + 2 * stride] = c;
+    dst[i + 3 * stride] = d;
+  }
+  for (; i < n; i += stride) dst[i] = ldg_stream(src + i);
+}
+}  // namespace praxis
+
+extern "C" {
 static_assert(sizeof(cudaIpcMemHandle_t) == PRAXIS_B200_IPC_HANDLE_BYTES, "IPC handle size");
 
 int praxis_b200_ipc_alloc(size_t bytes, int device, void** ptr) {
@@ -584,6 +608,19 @@ int praxis_b200_ipc_close(void* ptr, int device) {
   const cudaError_t e = cudaIpcCloseMemHandle(ptr);
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "ipc_close: %s", cudaGetErrorString(e));
   return PRAXIS_B200_OK;
+}
+
+int praxis_b200_sm_copy(void* dst, const void* src, size_t bytes, int ctas, int device, void* stream) {
+  if (bytes == 0) return PRAXIS_B200_OK;
+  if (dst == nullptr || src == nullptr) return set_error(PRAXIS_B200_EINVAL, "sm_copy: null pointer");
+  if ((((uintptr_t)dst | (uintptr_t)src | bytes) & 15) != 0)
+    return set_error(PRAXIS_B200_EINVAL, "sm_copy: addresses and size must be multiples of 16 bytes");
+  if (ctas < 1 || ctas > 1024) return set_error(PRAXIS_B200_EINVAL, "sm_copy: ctas must be 1..1024");
+  int rc = use_device(device);
+  if (rc) return rc;
+  peer_copy_kernel<<<ctas, kPeerCopyThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), (int64_t)(bytes / 16));
+  return check_launch("sm_copy");
 }
 
 int praxis_b200_copy_async(void* dst, const void* src, size_t bytes, int device, void* stream) {

@@ -39,7 +39,7 @@ be exercised with CPU tensors over gloo.
 
 from __future__ import annotations
 
-from collections.abc import Mapping
+from collections.abc import Mapping, Sequence
 
 import torch
 import torch.distributed as dist
@@ -241,7 +241,13 @@ class PeerExchange:
     forward's data is done.
     """
 
-    def __init__(self, group, device: torch.device, copy_streams: int = 4) -> None:
+    def __init__(self, group, device: torch.device, copy_streams: int = 4, sm_copy_fraction: float = 0.0,
+                 copy_ctas: int = 16) -> None:
+        """``sm_copy_fraction`` of every transfer's bytes go through a copy
+        kernel on ``copy_ctas`` CTAs (SM-driven NVLink writes) beside the copy
+        engines, which move the rest."""
+        if not 0.0 <= sm_copy_fraction <= 1.0:
+            raise ValueError("sm_copy_fraction must be in [0, 1]")
         self.group = group
         self.device = torch.device(device)
         self.world = dist.get_world_size(group)
@@ -252,6 +258,9 @@ class PeerExchange:
         self._local: dict[str, tuple[int, int]] = {}  # name -> (pointer, bytes)
         self._peer: dict[str, list[int]] = {}  # name -> pointer per rank (own rank: local)
         self.streams = [torch.cuda.Stream(self.device) for _ in range(copy_streams)]
+        self.sm_copy_fraction = float(sm_copy_fraction)
+        self.copy_ctas = int(copy_ctas)
+        self.sm_stream = torch.cuda.Stream(self.device) if sm_copy_fraction > 0 else None
         self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ready: torch.cuda.Event | None = None  # the previous forward's last barrier
 
@@ -331,9 +340,29 @@ class PeerExchange:
     def back_row(self, d: int, row: int) -> int:
         return self._peer["back"][d] + row * self.dim * 2
 
-    def copy(self, dst: int, src: int, nbytes: int, stream: torch.cuda.Stream) -> None:
-        capi.check(capi.load().praxis_b200_copy_async(C.c_void_p(dst), C.c_void_p(src), nbytes,
-                                                       self.device.index, C.c_void_p(stream.cuda_stream)))
+    def copy(self, dst: int, src: int, nbytes: int, stream: torch.cuda.Stream,
+             after: Sequence[torch.cuda.Event] = ()) -> None:
+        """``nbytes`` from ``src`` to ``dst`` once the ``after`` events have
+        completed: the copy engines on ``stream``, and the ``sm_copy_fraction``
+        head of it by the copy kernel on the SM copy stream."""
+        lib = capi.load()
+        dev = self.device.index
+        for ev in after:
+            stream.wait_event(ev)
+        head = 0
+        if self.sm_stream is not None:
+            head = int(nbytes * self.sm_copy_fraction) // 16 * 16
+            if head:
+                for ev in after:
+                    self.sm_stream.wait_event(ev)
+                capi.check(lib.praxis_b200_sm_copy(C.c_void_p(dst), C.c_void_p(src), head, self.copy_ctas, dev,
+                                                   C.c_void_p(self.sm_stream.cuda_stream)))
+        capi.check(lib.praxis_b200_copy_async(C.c_void_p(dst + head), C.c_void_p(src + head), nbytes - head, dev,
+                                               C.c_void_p(stream.cuda_stream)))
+
+    def copy_streams(self) -> list[torch.cuda.Stream]:
+        """Every stream the copies run on."""
+        return self.streams + ([self.sm_stream] if self.sm_stream is not None else [])
 
     def barrier(self, stream: torch.cuda.Stream) -> None:
         """All ranks' work enqueued before this point (on ``stream``) is done
@@ -396,15 +425,13 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     quantized = torch.cuda.Event()
     quantized.record(compute)
     streams = peers.streams
+    after = [quantized] + ([peers.ready] if peers.ready is not None else [])
     for k, d in enumerate(d for d in range(world) if d != rank and send_rows[d]):
         st = streams[k % len(streams)]
-        st.wait_event(quantized)
-        if peers.ready is not None:
-            st.wait_event(peers.ready)
         dq, dsf = peers.recv_slot(d, rank)
-        peers.copy(dq, q.data_ptr() + lo[d] * q.shape[1], send_rows[d] * q.shape[1], st)
-        peers.copy(dsf, sf.data_ptr() + lo[d] * sf.shape[1], send_rows[d] * sf.shape[1], st)
-    for st in streams:
+        peers.copy(dq, q.data_ptr() + lo[d] * q.shape[1], send_rows[d] * q.shape[1], st, after)
+        peers.copy(dsf, sf.data_ptr() + lo[d] * sf.shape[1], send_rows[d] * sf.shape[1], st, after)
+    for st in peers.copy_streams():
         q.record_stream(st)
         sf.record_stream(st)
 
@@ -442,9 +469,9 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
         done.record(compute)
         st = streams[returned[0] % len(streams)]
         returned[0] += 1
-        st.wait_event(done)
-        peers.copy(peers.back_row(src, src_row0[src] + r0), res.data_ptr(), (r1 - r0) * x.shape[1] * 2, st)
-        res.record_stream(st)
+        peers.copy(peers.back_row(src, src_row0[src] + r0), res.data_ptr(), (r1 - r0) * x.shape[1] * 2, st, [done])
+        for cs in peers.copy_streams():
+            res.record_stream(cs)
 
     # most of this rank's own rows while its rows travel out (half on 2
     # ranks, three quarters on more, where more rows leave); the other
@@ -454,7 +481,7 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     tail = e_local // (2 if world <= 2 else 4)
     half = e_local - tail
     run(rank, 0, half)
-    for st in streams:
+    for st in peers.copy_streams():
         compute.wait_stream(st)
     peers.barrier(compute)  # every slot of this rank is filled
     groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
@@ -462,7 +489,7 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
         for a, b in groups:
             run((rank + j) % world, a, b)
     run(rank, half, e_local)
-    for st in streams:
+    for st in peers.copy_streams():
         compute.wait_stream(st)
     peers.barrier(compute)  # every result for this rank's rows has landed
     peers.ready = torch.cuda.Event()
@@ -481,11 +508,15 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
     ACCEPTS_DISPATCH = False
 
     def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *, transport: str = "peer",
-                 transfer_sms: int = 16, chunks: int | None = None, copy_streams: int = 4) -> None:
+                 transfer_sms: int = 16, chunks: int | None = None, copy_streams: int = 4,
+                 sm_copy_fraction: float = 0.0) -> None:
         """``transport="peer"``: rows move on the copy engines into the peers'
         mapped buffers (``exchange_forward_peer``); ``"nccl"``: NCCL
         point-to-point transfers (``exchange_forward``), with ``transfer_sms``
-        SMs kept free of the expert GEMMs for NCCL's kernels."""
+        SMs kept free of the expert GEMMs for NCCL's kernels. With the peer
+        transport, ``sm_copy_fraction`` > 0 moves that share of the bytes with
+        a copy kernel on ``transfer_sms`` CTAs beside the copy engines (and
+        keeps those SMs free of the GEMMs)."""
         super().__init__()
         world = dist.get_world_size(group)
         if bank.num_experts * world != num_experts:
@@ -497,9 +528,10 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
         self.group = group
         self.chunks = chunks
         self.transport = transport if world > 1 else "nccl"
-        self._backend = CudaBackend(bank, transfer_sms if world > 1 and self.transport == "nccl" else 0)
-        self._peers = (PeerExchange(group, bank.gate_up_q.device, copy_streams) if self.transport == "peer"
-                       else None)
+        reserve = self.transport == "nccl" or sm_copy_fraction > 0
+        self._backend = CudaBackend(bank, transfer_sms if world > 1 and reserve else 0)
+        self._peers = (PeerExchange(group, bank.gate_up_q.device, copy_streams, sm_copy_fraction, transfer_sms)
+                       if self.transport == "peer" else None)
 
     @classmethod
     def from_packed(cls, state: Mapping[str, Tensor], group=None, **kwargs) -> ExpertParallelRoutedExperts:

@@ -7,8 +7,9 @@
 * the real exchange (``exchange_forward``) over NCCL with one rank;
 * the real exchange over NCCL with two ranks when two GPUs are visible;
 * the copy-engine exchange into IPC-mapped peer buffers with two ranks when
-  two GPUs are visible: several forwards with changing token counts (buffer
-  reuse and growth), each bit for bit equal to the single-GPU bank.
+  two GPUs are visible, alone and with half of every transfer done by the SM
+  copy kernel: several forwards with changing token counts (buffer reuse and
+  growth), each bit for bit equal to the single-GPU bank.
 """
 
 from __future__ import annotations
@@ -176,7 +177,7 @@ def test_exchange_forward_two_ranks_nccl(P):
     assert all(ok for ok, _ in res.values()), res
 
 
-def _peer_worker(rank, world, port, results):
+def _peer_worker(rank, world, port, results, sm_copy_fraction=0.0):
     try:
         torch.cuda.set_device(rank)
         os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -187,7 +188,8 @@ def _peer_worker(rank, world, port, results):
         c, e, k, f = 512, 8, 2, 256
         state = _packed(e, c, f)
         dev = torch.device("cuda", rank)
-        ep = p.expert_parallel.ExpertParallelRoutedExperts.from_packed({n: v.to(dev) for n, v in state.items()})
+        ep = p.expert_parallel.ExpertParallelRoutedExperts.from_packed({n: v.to(dev) for n, v in state.items()},
+                                                                      sm_copy_fraction=sm_copy_fraction)
         assert ep.transport == "peer"
         full = p.B200NVFP4RoutedExperts.from_packed({n: v.clone() for n, v in state.items()}).to(dev)
         ok = True
@@ -209,11 +211,12 @@ def _peer_worker(rank, world, port, results):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_exchange_two_ranks(P):
+@pytest.mark.parametrize("sm_copy_fraction", [0.0, 0.5])
+def test_peer_exchange_two_ranks(P, sm_copy_fraction):
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, results)) for r in range(2)]
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, results, sm_copy_fraction)) for r in range(2)]
     for proc in procs:
         proc.start()
     res = {}

@@ -41,15 +41,22 @@ class KernelWeights(NamedTuple):
     down_sf_layout: int     # capi.SF_COMPACT
 
 
-def _validate(state: Mapping[str, Tensor]) -> tuple[int, int, int]:
-    """praxis/quantization/nvfp4.py:163-213."""
+def _validate(state: Mapping[str, Tensor], require_cpu: bool = True) -> tuple[int, int, int]:
+    """praxis/quantization/nvfp4.py:163-213 (``require_cpu``: the reference's
+    rule that reconstruction starts from CPU buffers; this library's own
+    packers build banks from device buffers)."""
     if not isinstance(state, Mapping) or set(state) != _BUFFER_NAMES:
         raise ValueError("Unexpected NVFP4 packed buffer keys")
     if any(
-        not isinstance(v, Tensor) or v.layout != torch.strided or not v.is_contiguous() or v.requires_grad
+        not isinstance(v, Tensor)
+        or (require_cpu and v.device.type != "cpu")
+        or v.layout != torch.strided
+        or not v.is_contiguous()
+        or v.requires_grad
         for v in state.values()
     ):
-        raise ValueError("Reconstruction requires contiguous detached buffers")
+        raise ValueError("Reconstruction requires contiguous detached CPU buffers" if require_cpu else
+                         "Reconstruction requires contiguous detached buffers")
     gu = state["gate_up_q"]
     if gu.ndim != 3:
         raise ValueError("Expected grouped gate/up packed matrix")
@@ -95,11 +102,15 @@ class B200NVFP4RoutedExperts(nn.Module):
 
     format = "nvfp4"
     backend = "b200_sm100a_tcgen05_nvfp4"
-    ACCEPTS_DISPATCH = True
+    # The routing kernels here build their own dispatch metadata (tile tables,
+    # padded offsets, global scales) in the same launch sequence as the
+    # experts, so a ``router_fused.Routing`` from the caller is not needed and
+    # ``MoEFeedForward._routed_tail`` (praxis/layers.py:2245-2250) passes none.
+    ACCEPTS_DISPATCH = False
 
-    def __init__(self, state: Mapping[str, Tensor]) -> None:
+    def __init__(self, state: Mapping[str, Tensor], *, _device_state: bool = False) -> None:
         super().__init__()
-        e, c, h = _validate(state)
+        e, c, h = _validate(state, require_cpu=not _device_state)
         self.num_experts, self.in_features, self.hidden_features = e, c, h
         for name in sorted(_BUFFER_NAMES):
             self.register_buffer(name, state[name].detach())
@@ -108,7 +119,15 @@ class B200NVFP4RoutedExperts(nn.Module):
 
     @classmethod
     def from_packed(cls, state: Mapping[str, Tensor]) -> B200NVFP4RoutedExperts:
+        """The reference's reconstruction (praxis/quantization/nvfp4.py:149-227):
+        contiguous detached CPU buffers; move the bank with ``.to(device)``."""
         return cls(state)
+
+    @classmethod
+    def from_device_state(cls, state: Mapping[str, Tensor]) -> B200NVFP4RoutedExperts:
+        """The same validation for buffers already on a device (this library's
+        GPU packer and the expert-parallel shards), without a host copy."""
+        return cls(state, _device_state=True)
 
     def train(self, mode: bool = True) -> B200NVFP4RoutedExperts:
         if mode:
@@ -203,9 +222,11 @@ class B200NVFP4RoutedExperts(nn.Module):
         if isinstance(scaling, bool) or not isinstance(scaling, float | int) or not math.isfinite(scaling):
             raise ValueError("Routed scaling must be finite")
         top_k = top_idx.shape[1]
+        # the reference's bound (praxis/quantization/nvfp4.py:677-682), kept so
+        # that the same calls are rejected; the kernels here index with 64 bits
         if (min(chunk_size, x.shape[0]) * top_k + 127 * self.num_experts) * max(
             self.in_features, 2 * self.hidden_features
-        ) >= 2**31 * 8:
+        ) >= 2**31:
             raise ValueError("Routed chunk exceeds NVFP4 kernel indexing bounds")
 
     def _routed_forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int,
@@ -256,5 +277,5 @@ def pack_routed_experts(gate_up_weight: Tensor, down_weight: Tensor, *, keep_on_
             state[name + "_q"], state[name + "_sf"], state[name + "_global"] = q, sf, g
         state["_unit_alpha"] = torch.ones(e, dtype=torch.float32, device=dev)
     if not keep_on_device:
-        state = {k: v.cpu() for k, v in state.items()}
-    return B200NVFP4RoutedExperts.from_packed(state)
+        return B200NVFP4RoutedExperts.from_packed({k: v.cpu() for k, v in state.items()})
+    return B200NVFP4RoutedExperts.from_device_state(state)

@@ -61,8 +61,6 @@ int check_launch(const char* what) {
   return PRAXIS_B200_OK;
 }
 
-static constexpr int kMaxDevices = 64;
-
 int sm_count() {
   static int cache[kMaxDevices] = {0};
   int dev = 0;
@@ -224,7 +222,7 @@ int64_t praxis_b200_padded_rows(int64_t routed_rows, int32_t experts) { return p
 int praxis_b200_router_logits(const void* x, const void* weight, int32_t weight_splits, int64_t tokens, int32_t dim,
                               int32_t experts, float* logits, void* row_amax, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
-  if (!x || !weight || !logits) return set_error(PRAXIS_B200_EINVAL, "router_logits: null pointer");
+  if (!weight || (tokens > 0 && (!x || !logits))) return set_error(PRAXIS_B200_EINVAL, "router_logits: null pointer");
   return run_router_logits(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(weight), weight_splits,
                            tokens, dim, experts, logits, static_cast<uint16_t*>(row_amax), PRAXIS_STREAM(stream));
 }
@@ -232,14 +230,14 @@ int praxis_b200_router_logits(const void* x, const void* weight, int32_t weight_
 int praxis_b200_route(const float* logits, const float* bias, int64_t tokens, int32_t experts, int32_t top_k,
                       int32_t activation, int64_t* top_idx, void* gate, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
-  if (!logits || !top_idx || !gate) return set_error(PRAXIS_B200_EINVAL, "route: null pointer");
+  if (tokens > 0 && (!logits || !top_idx || !gate)) return set_error(PRAXIS_B200_EINVAL, "route: null pointer");
   return run_route(logits, bias, tokens, experts, top_k, activation, top_idx, static_cast<uint16_t*>(gate),
                    PRAXIS_STREAM(stream));
 }
 
 int praxis_b200_row_amax(const void* x, int64_t rows, int32_t cols, void* out, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
-  if (!x || !out) return set_error(PRAXIS_B200_EINVAL, "row_amax: null pointer");
+  if (rows > 0 && (!x || !out)) return set_error(PRAXIS_B200_EINVAL, "row_amax: null pointer");
   return run_row_amax(static_cast<const uint16_t*>(x), rows, cols, static_cast<uint16_t*>(out), PRAXIS_STREAM(stream));
 }
 
@@ -253,9 +251,9 @@ int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* r
                          int32_t* offsets, int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles,
                          int32_t* num_tiles, float* act_global, uint32_t* act_amax, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
-  if (!top_idx || !csr || !pcsr || !tiles || !num_tiles || !workspace)
+  if ((tokens > 0 && !top_idx) || !csr || !pcsr || !tiles || !num_tiles || !workspace)
     return set_error(PRAXIS_B200_EINVAL, "dispatch: null pointer");
-  if (sorted_gate && !gate) return set_error(PRAXIS_B200_EINVAL, "dispatch: sorted_gate needs gate");
+  if (tokens > 0 && sorted_gate && !gate) return set_error(PRAXIS_B200_EINVAL, "dispatch: sorted_gate needs gate");
   if (max_tiles < padded_rows(tokens * top_k, experts) / 128)
     return set_error(PRAXIS_B200_EINVAL, "dispatch: max_tiles below padded_rows/128");
   int32_t* off = offsets;
@@ -293,7 +291,7 @@ int praxis_b200_quantize_gather(const void* x, int64_t tokens, int32_t dim, cons
                                 const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles, void* q, void* sf,
                                 int32_t sf_layout, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
-  if (!x || !top_idx || !inverse || !csr || !pcsr || !tiles || !num_tiles || !q || !sf)
+  if ((tokens > 0 && (!x || !top_idx || !inverse)) || !csr || !pcsr || !tiles || !num_tiles || !q || !sf)
     return set_error(PRAXIS_B200_EINVAL, "quantize_gather: null pointer");
   return run_quantize_gather(static_cast<const uint16_t*>(x), tokens, dim, top_idx, inverse, csr, pcsr, act_global,
                              act_amax, top_k, experts, reinterpret_cast<const TileEntry*>(tiles), num_tiles,
@@ -349,6 +347,7 @@ int praxis_b200_combine(const void* rows, int32_t cols, const int64_t* inverse, 
                         const void* shared, void* out, int64_t tokens, int32_t top_k, int32_t experts, int device,
                         void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
+  if (tokens == 0) return PRAXIS_B200_OK;
   if (!rows || !inverse || !top_idx || !gate || !csr || !pcsr || !out)
     return set_error(PRAXIS_B200_EINVAL, "combine: null pointer");
   return run_combine(static_cast<const uint16_t*>(rows), cols, inverse, top_idx, static_cast<const uint16_t*>(gate),

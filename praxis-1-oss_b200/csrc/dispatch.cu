@@ -404,15 +404,21 @@ int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* r
   const int blocks = (segments + kDispatchWarps - 1) / kDispatchWarps;
   const size_t smem_count = (size_t)2 * kDispatchWarps * experts * 4;
   const size_t smem_scatter = (size_t)kDispatchWarps * experts * 4;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaFuncSetAttribute(dispatch_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kDispatchWarps * kMaxExperts * 4);
-    cudaFuncSetAttribute(dispatch_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDispatchWarps * kMaxExperts * 4);
-    attr_done = true;
-  }
+  static DeviceOnce attr;
+  int rc = device_once(attr, [](int dev) {
+    cudaError_t e = cudaFuncSetAttribute(dispatch_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         2 * kDispatchWarps * kMaxExperts * 4);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(dispatch_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kDispatchWarps * kMaxExperts * 4);
+    if (e != cudaSuccess)
+      return set_error(PRAXIS_B200_ECUDA, "dispatch smem attribute (device %d): %s", dev, cudaGetErrorString(e));
+    return (int)PRAXIS_B200_OK;
+  });
+  if (rc) return rc;
   launch_pdl(dispatch_count_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_count, stream, top_idx, row_amax,
              positions, top_k, experts, seg_len, segments, seg_count, seg_max);
-  int rc = check_launch("dispatch_count");
+  rc = check_launch("dispatch_count");
   if (rc) return rc;
   launch_pdl(dispatch_scan_kernel, dim3(1), dim3(1024), 0, stream, seg_count, seg_max, segments, experts, positions,
              (int)kTileRows, offsets, csr, pcsr, tiles, max_tiles, num_tiles, row_amax ? act_global : nullptr,

@@ -705,14 +705,15 @@ template <int BLOCK_N, int EPI>
 static int launch_gemm(const GemmParams& p, int max_tiles, cudaStream_t stream) {
   using S = GemmShape<BLOCK_N>;
   auto kernel = gemm_nvfp4_kernel<BLOCK_N, EPI>;
-  static bool configured[8] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 8 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM_BYTES);
-    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  static DeviceOnce attr;
+  const int rc = device_once(attr, [&](int dev) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM_BYTES);
+    if (e != cudaSuccess)
+      return set_error(PRAXIS_B200_ECUDA, "gemm smem attribute (device %d): %s", dev, cudaGetErrorString(e));
+    return (int)PRAXIS_B200_OK;
+  });
+  if (rc) return rc;
   const int units = max_tiles * (p.N / BLOCK_N);
   if (units <= 0) return PRAXIS_B200_OK;
   int grid = units < sm_count() ? units : sm_count();
@@ -765,13 +766,12 @@ template <int EPI, bool REP>
 static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t stream) {
   using S = PairShape<REP, EPI == EPI_SWIGLU>;
   auto kernel = gemm_nvfp4_pair_kernel<EPI, REP>;
-  static int max_clusters[8] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 8) return set_error(PRAXIS_B200_EINVAL, "device index %d", dev);
-  if (max_clusters[dev] == 0) {
+  static DeviceOnce attr;
+  static int max_clusters[kMaxDevices] = {0};
+  const int rc = device_once(attr, [&](int dev) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM_BYTES);
-    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "pair gemm smem attribute: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess)
+      return set_error(PRAXIS_B200_ECUDA, "pair gemm smem attribute (device %d): %s", dev, cudaGetErrorString(e));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (sm_count() / 2));
     cfg.blockDim = dim3(S::THREADS);
@@ -787,7 +787,11 @@ static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t str
     e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
     if (e != cudaSuccess || n <= 0) n = sm_count() / 2;
     max_clusters[dev] = n;
-  }
+    return (int)PRAXIS_B200_OK;
+  });
+  if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
   const int units = max_tiles * (p.N / S::BN);
   if (units <= 0) return PRAXIS_B200_OK;
   int clusters = units < max_clusters[dev] ? units : max_clusters[dev];

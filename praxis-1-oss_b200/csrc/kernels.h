@@ -7,11 +7,15 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "common.cuh"
 
 namespace praxis {
+
+constexpr int kMaxDevices = 64;
 
 enum Epilogue : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESCALE = 2 };
 
@@ -61,6 +65,29 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 int sm_count();
+
+// Per-device, thread-safe one-time set-up. Kernel attributes such as the
+// dynamic shared-memory limit belong to each device's context, so a process
+// that drives several GPUs sets them once per device. device_once runs
+// `init(device)` (with that device current) the first time `once` is used on
+// it; a failed init returns its code and is retried on the next call.
+struct DeviceOnce {
+  std::mutex mu;
+  std::atomic<bool> done[kMaxDevices];
+};
+
+template <class F>
+inline int device_once(DeviceOnce& once, F&& init) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return set_error(PRAXIS_B200_EINVAL, "device index %d outside 0..%d", dev, kMaxDevices - 1);
+  if (once.done[dev].load(std::memory_order_acquire)) return PRAXIS_B200_OK;
+  std::lock_guard<std::mutex> lock(once.mu);
+  if (once.done[dev].load(std::memory_order_relaxed)) return PRAXIS_B200_OK;
+  const int rc = init(dev);
+  if (rc == PRAXIS_B200_OK) once.done[dev].store(true, std::memory_order_release);
+  return rc;
+}
 
 // f32(bf16(max(amax, 1e-12))) * f32(1/2688): the QAT global scale from the
 // float bits of a bf16-valued maximum (praxis/kernels/nvfp4_moe.py:55-57).

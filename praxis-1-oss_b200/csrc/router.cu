@@ -433,15 +433,17 @@ int run_router_logits(const uint16_t* x, const uint16_t* w, int splits, int64_t 
   int stages = kRouterSmemBudget / stage_bytes;
   stages = stages < 2 ? 2 : stages > 6 ? 6 : stages;
   const size_t smem = 1024 + (size_t)stages * stage_bytes + (2 * stages + 2) * 8;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  int rc = device_once(attr, [](int dev) {
     const cudaError_t e =
         cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "router smem attribute: %s", cudaGetErrorString(e));
-    attr = true;
-  }
+    if (e != cudaSuccess)
+      return set_error(PRAXIS_B200_ECUDA, "router smem attribute (device %d): %s", dev, cudaGetErrorString(e));
+    return (int)PRAXIS_B200_OK;
+  });
+  if (rc) return rc;
   CUtensorMap mx, mw;
-  int rc = make_bf16_map(&mx, x, tokens, dim, kRouterBM);
+  rc = make_bf16_map(&mx, x, tokens, dim, kRouterBM);
   if (rc) return rc;
   rc = make_bf16_map(&mw, w, (int64_t)splits * experts, dim, e_pad);
   if (rc) return rc;

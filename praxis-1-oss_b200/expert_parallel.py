@@ -497,6 +497,35 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     return backend.combine(back, routing, scaling, shared)
 
 
+def chunked_forward(one_chunk, x: Tensor, top_idx: Tensor, gate: Tensor, shared: Tensor | None, chunk_size: int,
+                    group=None) -> Tensor:
+    """The dispatch-chunk loop of ``NVFP4RoutedExperts._routed_forward``
+    (praxis/quantization/nvfp4.py:683-747) over an expert-parallel exchange:
+    each rank splits its own tokens into chunks of ``chunk_size`` and every
+    chunk is one exchange, so activation and hidden global scales are taken
+    per (chunk, expert) as on one GPU. Ranks may hold different token counts;
+    they agree on the largest chunk count (one all-reduce) and a rank with
+    fewer chunks joins the remaining exchanges with an empty chunk, so every
+    rank runs the same collectives in the same order. ``chunk_size <= 0``
+    takes each rank's whole batch as one chunk (no agreement needed)."""
+    t = x.shape[0]
+    if chunk_size <= 0:
+        return one_chunk(x, top_idx, gate, shared)
+    mine = -(-t // chunk_size)
+    count = torch.tensor([mine], dtype=torch.int64, device=x.device)
+    dist.all_reduce(count, op=dist.ReduceOp.MAX, group=group)
+    n = int(count.item())
+    if n <= 1:
+        return one_chunk(x, top_idx, gate, shared)
+    out = torch.empty_like(x)
+    for i in range(n):
+        a, b = min(i * chunk_size, t), min((i + 1) * chunk_size, t)
+        res = one_chunk(x[a:b], top_idx[a:b], gate[a:b], None if shared is None else shared[a:b])
+        if b > a:
+            out[a:b] = res
+    return out
+
+
 class ExpertParallelRoutedExperts(torch.nn.Module):
     """The routed-bank protocol (``routed_forward`` /
     ``routed_forward_with_shared``) over an expert-sharded bank: this rank holds
@@ -538,7 +567,11 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
         """Shard a full packed bank (reference buffer layout) over ``group``."""
         rank, world = dist.get_rank(group), dist.get_world_size(group)
         e = state["gate_up_q"].shape[0]
-        return cls(B200NVFP4RoutedExperts.from_packed(shard_packed_state(state, rank, world)), e, group, **kwargs)
+        shard = shard_packed_state(state, rank, world)
+        on_host = all(v.device.type == "cpu" for v in shard.values())
+        bank = (B200NVFP4RoutedExperts.from_packed(shard) if on_host
+                else B200NVFP4RoutedExperts.from_device_state(shard))
+        return cls(bank, e, group, **kwargs)
 
     def prepare(self) -> None:
         self.bank.prepare()
@@ -553,13 +586,22 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
 
     def routed_forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int = 0,
                        dispatch=None) -> Tensor:
-        self.bank._check(x, top_idx, gate, scaling, max(chunk_size, x.shape[0], 1))
-        return self._forward(x, top_idx, gate, float(scaling), None)
+        """The bank protocol's ``routed_forward``; ``chunk_size`` splits this
+        rank's tokens into dispatch chunks as the reference does (see
+        ``chunked_forward``; 0 = the whole batch is one chunk)."""
+        return self._chunked(x, top_idx, gate, scaling, chunk_size, None)
 
     def routed_forward_with_shared(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float,
                                    chunk_size: int = 0, shared: Tensor, dispatch=None) -> Tensor:
-        self.bank._check(x, top_idx, gate, scaling, max(chunk_size, x.shape[0], 1))
-        return self._forward(x, top_idx, gate, float(scaling), shared)
+        return self._chunked(x, top_idx, gate, scaling, chunk_size, shared)
+
+    def _chunked(self, x, top_idx, gate, scaling, chunk_size, shared) -> Tensor:
+        if type(chunk_size) is not int or chunk_size < 0:
+            raise ValueError("chunk_size must be a non-negative int (0: one chunk per rank)")
+        self.bank._check(x, top_idx, gate, scaling, chunk_size if chunk_size > 0 else max(x.shape[0], 1))
+        scaling = float(scaling)
+        return chunked_forward(lambda xc, tc, gc, sc: self._forward(xc, tc, gc, scaling, sc), x, top_idx, gate,
+                               shared, chunk_size, self.group)
 
     def close(self) -> None:
         """Unmap and free the peer buffers (collective over ``group``)."""
@@ -567,5 +609,5 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
             self._peers.close()
 
 
-__all__ = ["CudaBackend", "ExpertParallelRoutedExperts", "PeerExchange", "exchange_forward", "exchange_forward_peer",
-           "shard_packed_state"]
+__all__ = ["CudaBackend", "ExpertParallelRoutedExperts", "PeerExchange", "chunked_forward", "exchange_forward",
+           "exchange_forward_peer", "shard_packed_state"]

@@ -53,9 +53,16 @@ class SharedExpert(nn.Module):
 
 class B200MoEFeedForward(nn.Module):
     """Router (sigmoid or softmax) + top-k routed NVFP4 experts + optional
-    shared expert, inference only."""
+    shared expert, inference only.
+
+    ``routing_hook`` (praxis/layers.py:1595-1602): None at inference; a
+    callable ``hook(layer, logits, top_idx)`` set by training or diagnostics
+    code is called after the routing and before the experts with the float32
+    router logits and the picked experts.
+    """
 
     expert_bias: Tensor
+    routing_hook = None
 
     def __init__(
         self,
@@ -142,12 +149,41 @@ class B200MoEFeedForward(nn.Module):
             logits, _ = ops.router_logits(x_flat, self.router_terms())
         with _Range("topk_dispatch"):
             bias = self.expert_bias.to(device=x_flat.device, dtype=torch.float32).contiguous()
-            return ops.route(logits, bias, self.top_k, self.router_activation)
+            top_idx, gate = ops.route(logits, bias, self.top_k, self.router_activation)
+        if self.routing_hook is not None:
+            self.routing_hook(self, logits, top_idx)
+        return top_idx, gate
+
+    @staticmethod
+    def _check_router_rows(x: Tensor, router_rows) -> None:
+        """``router_rows = (r0, r1, total)`` (praxis/layers.py:2122-2165): x
+        holds query rows r0..r1 of a sequence of ``total`` tokens whose context
+        rows were left out. The reference pads x back to ``total`` rows with
+        zeros so that its fp32 router GEMM keeps the full call's row-chunk
+        shapes; the logits kernel here computes every row on its own, in an
+        order that does not depend on the number of rows, so the query rows'
+        logits are those of the padded call and no padding is needed."""
+        if (
+            not isinstance(router_rows, tuple)
+            or len(router_rows) != 3
+            or not all(isinstance(v, int) and not isinstance(v, bool) for v in router_rows)
+        ):
+            raise ValueError("router_rows must be a tuple (r0, r1, total) of ints")
+        r0, r1, total = router_rows
+        if not 0 <= r0 <= r1 <= total:
+            raise ValueError(f"router_rows {router_rows}: need 0 <= r0 <= r1 <= total")
+        if x.dim() < 2 or x.shape[-2] != r1 - r0:
+            raise ValueError(f"router_rows {router_rows}: x must hold r1 - r0 = {r1 - r0} rows per sequence")
 
     @torch.no_grad()
-    def forward(self, x: Tensor) -> Tensor:
+    def forward(self, x: Tensor, *, router_rows: tuple[int, int, int] | None = None) -> Tensor:
+        """``MoEFeedForward.forward`` (praxis/layers.py:2122-2199), the same
+        keyword (called as ``self.ffn(normed, router_rows=rows)`` by the
+        reference's transformer block, praxis/layers.py:2515)."""
         if self.routed is None:
             raise RuntimeError("routed experts are not set (set_routed_weights / from_reference)")
+        if router_rows is not None:
+            self._check_router_rows(x, router_rows)
         shape = x.shape
         x_flat = x.reshape(-1, x.size(-1)).contiguous()
         top_idx, gate = self.route(x_flat)

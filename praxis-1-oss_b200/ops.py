@@ -172,11 +172,50 @@ def dispatch_noalloc(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tens
     if gate.shape != top_idx.shape:
         raise ValueError("gate / top_idx shape mismatch")
     t, k = top_idx.shape
+    _check_dispatch_outputs(t, k, num_experts, top_idx.device, amax, order=order, inverse=inverse, tokens=tokens,
+                            tokens32=tokens32, sorted_gate=sorted_gate, offsets=offsets, csr=csr, pcsr=pcsr,
+                            tiles=tiles, num_tiles=num_tiles, act_global=act_global, act_amax=act_amax)
     max_tiles = tiles.shape[0] // 2
     capi.check(capi.load().praxis_b200_dispatch_noalloc(
         _p(top_idx), _p(gate), _p(amax), t, k, num_experts, _p(order), _p(inverse), _p(tokens), _p(tokens32),
         _p(sorted_gate), _p(offsets), _p(csr), _p(pcsr), _p(tiles), max_tiles, _p(num_tiles), _p(act_global),
         _p(act_amax), _dev(top_idx), _stream(top_idx)))
+
+
+def _check_dispatch_outputs(t: int, k: int, e: int, device, amax: Tensor | None, *, order: Tensor, inverse: Tensor,
+                            tokens: Tensor, tokens32: Tensor, sorted_gate: Tensor, offsets: Tensor, csr: Tensor,
+                            pcsr: Tensor, tiles: Tensor, num_tiles: Tensor, act_global: Tensor | None,
+                            act_amax: Tensor | None) -> None:
+    """Caller-owned dispatch outputs: dtype, contiguity, device and size of
+    every buffer the kernels write, checked before any launch (an undersized
+    or mistyped buffer would be written out of bounds on the device)."""
+    r = t * k
+    if e < 1:
+        raise ValueError("num_experts must be positive")
+
+    def need(ten, name, dtype, numel):
+        if not isinstance(ten, Tensor) or ten.dtype != dtype or not ten.is_contiguous() or ten.device != device:
+            raise ValueError(f"{name}: expected a contiguous {dtype} tensor on {device}")
+        if ten.numel() < numel:
+            raise ValueError(f"{name}: needs at least {numel} elements, got {ten.numel()}")
+
+    for name, ten, dtype, numel in (
+        ("order", order, torch.int64, r), ("inverse", inverse, torch.int64, r), ("tokens", tokens, torch.int64, r),
+        ("tokens32", tokens32, torch.int32, r), ("sorted_gate", sorted_gate, BF16, r),
+        ("offsets", offsets, torch.int32, e), ("csr", csr, torch.int32, e + 1), ("pcsr", pcsr, torch.int32, e + 1),
+        ("num_tiles", num_tiles, torch.int32, 2),
+    ):
+        need(ten, name, dtype, numel)
+    need(tiles, "tiles", torch.int32, 0)
+    want_tiles = max(padded_rows(r, e) // 128, 1)
+    if tiles.ndim != 2 or tiles.shape[1] != 4 or tiles.shape[0] % 2 or tiles.shape[0] // 2 < want_tiles:
+        raise ValueError(f"tiles: expected int32 [2 * max_tiles, 4] with max_tiles >= {want_tiles}")
+    if amax is not None:
+        need(amax, "row amax", BF16, t)
+    if act_global is not None:
+        need(act_global, "act_global", torch.float32, e)
+    if act_amax is not None:
+        need(act_amax, "act_amax", torch.int32, e)
 
 
 def route_dispatch(logits: Tensor, bias: Tensor, rows: tuple, top_k: int = 8,

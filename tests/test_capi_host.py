@@ -148,3 +148,36 @@ def test_shared_output_fallback_preserves_native_addition(monkeypatch, kind):
 def test_ops_refuse_cpu_tensors():
     with pytest.raises(ValueError, match="CUDA"):
         pkg().ops.row_amax(torch.zeros(4, 128, dtype=torch.bfloat16))
+
+
+def test_from_packed_requires_cpu_buffers_like_the_reference():
+    # praxis/quantization/nvfp4.py:163-177: reconstruction starts from CPU buffers
+    state = {name: v.to("meta") for name, v in packed_state().items()}
+    with pytest.raises(ValueError, match="CPU"):
+        pkg().B200NVFP4RoutedExperts.from_packed(state)
+    assert pkg().B200NVFP4RoutedExperts.ACCEPTS_DISPATCH is False
+
+
+@pytest.mark.parametrize("rows,ok", [
+    ((0, 4, 4), True), ((2, 6, 10), True), ((3, 2, 10), False), ((0, 4, 3), False), ((0, 5, 8), False),
+    ([0, 4, 4], False), ((0, 4), False), ((0.0, 4, 4), False),
+])
+def test_module_router_rows_keyword(rows, ok):
+    """``forward(x, router_rows=(r0, r1, total))`` as the reference's block
+    calls it (praxis/layers.py:2515): x holds r1 - r0 query rows."""
+    x = torch.zeros(2, 4, 128, dtype=torch.bfloat16)
+    check = pkg().B200MoEFeedForward._check_router_rows
+    if ok:
+        check(x, rows)
+    else:
+        with pytest.raises(ValueError):
+            check(x, rows)
+
+
+def test_module_forward_signature_matches_the_reference():
+    import inspect
+
+    sig = inspect.signature(pkg().B200MoEFeedForward.forward)
+    assert list(sig.parameters) == ["self", "x", "router_rows"]
+    assert sig.parameters["router_rows"].kind is inspect.Parameter.KEYWORD_ONLY
+    assert pkg().B200MoEFeedForward.routing_hook is None

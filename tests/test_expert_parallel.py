@@ -96,21 +96,31 @@ def _bank(e: int, c: int, f: int):
     return O.pack_routed_experts(gu, down)
 
 
-def _worker(rank, world, port, shape, fail_rank, results, chunks=None):
+def _worker(rank, world, port, shape, fail_rank, results, chunks=None, chunk_size=None, tokens=None):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
         ep = pkg().expert_parallel
         t, c, e, k, f = shape
+        if tokens is not None:
+            t = tokens[rank]
         bank = _bank(e, c, f)
         local = ep.shard_packed_state(bank, rank, world)
         x, top_idx, gate, shared = _case(rank, t, c, e, k, f)
         if rank == fail_rank:
             raise RuntimeError("planted failure before the exchange")
-        out = ep.exchange_forward(x, top_idx, gate, num_experts=e, scaling=2.5,
-                                  backend=OracleBackend(local, k), shared=shared, chunks=chunks)
-        want = O.routed_forward(x, top_idx, gate, bank, 2.5, t, shared=shared)
+        backend = OracleBackend(local, k)
+
+        def one(xc, tc, gc, sc):
+            return ep.exchange_forward(xc, tc, gc, num_experts=e, scaling=2.5, backend=backend, shared=sc,
+                                       chunks=chunks)
+
+        if chunk_size is None:
+            out = one(x, top_idx, gate, shared)
+        else:
+            out = ep.chunked_forward(one, x, top_idx, gate, shared, chunk_size)
+        want = O.routed_forward(x, top_idx, gate, bank, 2.5, chunk_size or t, shared=shared)
         results.put((rank, "ok", bool(torch.equal(out.view(torch.int16), want.view(torch.int16))),
                      float(O.rel_l2(out, want))))
     except Exception as exc:  # reported to the parent
@@ -120,11 +130,11 @@ def _worker(rank, world, port, shape, fail_rank, results, chunks=None):
             dist.destroy_process_group()
 
 
-def _run(world, shape, fail_rank=-1, chunks=None):
+def _run(world, shape, fail_rank=-1, chunks=None, chunk_size=None, tokens=None):
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fail_rank, results, chunks))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fail_rank, results, chunks, chunk_size, tokens))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -147,6 +157,23 @@ def _run(world, shape, fail_rank=-1, chunks=None):
 ])
 def test_exchange_matches_single_rank_layer(world, shape, chunks):
     res = _run(world, shape, chunks=chunks)
+    for rank in range(world):
+        status, *info = res[rank]
+        assert status == "ok", info
+        equal, err = info
+        assert equal, (rank, err)
+
+
+@pytest.mark.parametrize("world,tokens,chunk_size", [
+    (2, (70, 40), 32),       # 3 chunks on rank 0, 2 on rank 1: rank 1 joins the last exchange empty
+    (2, (50, 50), 64),       # one chunk each
+    (4, (33, 0, 65, 17), 16),  # a rank without tokens joins every exchange empty
+])
+def test_dispatch_chunks_match_the_single_rank_chunk_loop(world, tokens, chunk_size):
+    """Each rank's tokens go through the reference's dispatch-chunk loop
+    (global scales per chunk and expert); ranks with fewer chunks still take
+    part in every exchange, so no collective is left unmatched."""
+    res = _run(world, (max(tokens), 256, 8, 2, 128), chunk_size=chunk_size, tokens=tokens)
     for rank in range(world):
         status, *info = res[rank]
         assert status == "ok", info

@@ -49,3 +49,50 @@ def test_bench_configs_cover_the_baseline_shapes():
     for name in ("1", "2", "3", "4", "5", "ckpt"):
         cfg = b.CONFIGS[name]
         assert cfg["dim"] % 64 == 0 and cfg["hidden"] % 128 == 0 and cfg["top_k"] <= cfg["experts"]
+
+
+def _noalloc_outputs(t, k, e, **override):
+    import torch
+
+    r = t * k
+    mt = max(pkg().ops.padded_rows(r, e) // 128, 1)
+    out = dict(order=torch.empty(r, dtype=torch.int64), inverse=torch.empty(r, dtype=torch.int64),
+               tokens=torch.empty(r, dtype=torch.int64), tokens32=torch.empty(r, dtype=torch.int32),
+               sorted_gate=torch.empty(r, dtype=torch.bfloat16), offsets=torch.empty(e, dtype=torch.int32),
+               csr=torch.empty(e + 1, dtype=torch.int32), pcsr=torch.empty(e + 1, dtype=torch.int32),
+               tiles=torch.empty(2 * mt, 4, dtype=torch.int32), num_tiles=torch.empty(2, dtype=torch.int32),
+               act_global=torch.empty(e), act_amax=torch.empty(e, dtype=torch.int32))
+    out.update(override)
+    return out
+
+
+@pytest.mark.parametrize("bad", [
+    ("order", "short"), ("inverse", "dtype"), ("tokens32", "dtype"), ("sorted_gate", "short"), ("offsets", "short"),
+    ("csr", "short"), ("pcsr", "dtype"), ("num_tiles", "short"), ("tiles", "short"), ("tiles", "cols"),
+    ("act_global", "dtype"), ("act_amax", "short"), ("order", "strided"),
+])
+def test_noalloc_dispatch_outputs_are_checked_before_launch(bad):
+    """Every caller-owned output of the no-allocation dispatch is checked for
+    dtype, layout and size on the host; the check needs no GPU."""
+    import torch
+
+    t, k, e = 300, 4, 16
+    ops = pkg().ops
+    good = _noalloc_outputs(t, k, e)
+    ops._check_dispatch_outputs(t, k, e, torch.device("cpu"), None, **good)  # accepted as is
+    name, kind = bad
+    ref = good[name]
+    if kind == "short":
+        ten = ref.reshape(-1)[:-1] if ref.ndim == 1 else ref[:-2]
+    elif kind == "dtype":
+        ten = ref.to(torch.float64 if ref.dtype != torch.float64 else torch.int32)
+    elif kind == "cols":
+        ten = torch.empty(ref.shape[0], 3, dtype=torch.int32)
+    else:
+        ten = torch.empty(2 * ref.numel(), dtype=ref.dtype)[::2]
+    with pytest.raises(ValueError, match=name):
+        ops._check_dispatch_outputs(t, k, e, torch.device("cpu"), None, **dict(good, **{name: ten}))
+    # the public op refuses host tensors before it gets that far
+    with pytest.raises(ValueError):
+        ops.dispatch_noalloc(torch.zeros(t, k, dtype=torch.int64), torch.zeros(t, k, dtype=torch.bfloat16), e,
+                             **good)

@@ -10,15 +10,21 @@ layer (whole job: tokens of all ranks / max-over-ranks step time).
 
 Inputs are synthetic and seeded (x ~ N(0,1) bf16, expert weights ~ N(0,0.02)
 packed to NVFP4 on the GPU, router weight ~ N(0, 1/C) so the logits are
-~N(0,1)); x (100 MB) plus the packed weights (510 MB) exceed the 126 MB L2,
-so no L2 flush is needed between steps.
+~N(0,1)); no public dataset stands behind the BASELINE configs.
 
-N > 1 (torchrun): every rank runs the full layer on its own tokens (expert
-weights replicated): weak scaling, no data-path collective.
+N = 1 runs BASELINE config 2 (16,384 tokens) and, as extra keys of the same
+line, config 3 (Zipf-skewed routing with its per-expert histogram), config 5
+(CUDA-graph latency over 10 Euler steps) and config 4's per-rank shape
+(65,536 tokens) on one GPU, the like-for-like base of the scaling run.
+N > 1 (torchrun) runs config 4: the layer expert-parallel over the N GPUs of
+one node, 65,536 tokens per rank (weak scaling), each rank's output checked
+bit for bit against the single-GPU bank on the same tokens.
 
---impl reference: the CPU port of the reference path (the oracle's NVFP4
-chain with weights dequantised once, float32 GEMMs, all host threads) on a
-bounded sample of tokens of the same layer; rank 0 only.
+The CPU leg (``cpu_baseline`` at N = 1, and ``--impl reference``) times the
+CPU port of the reference path (the oracle's NVFP4 chain with weights
+dequantised once, float32 GEMMs) on the same full batch with all host
+threads, plus a one-thread figure on a token sample; at N = 1 it also checks
+the GPU output against that chain (``parity``).
 """
 
 from __future__ import annotations
@@ -48,6 +54,24 @@ CONFIGS = {
     "ckpt": dict(tokens=16384, dim=3072, experts=128, top_k=8, hidden=1280, skew=False),
 }
 METRIC = "routed-expert tokens/sec per MoE layer"
+# Zipf(s=1.2) expert popularity of config 3 enters through the routing bias
+# (the reference's expert_bias: it changes which experts are picked, not their
+# gates); this strength makes the most popular expert be picked by about 30%
+# of the tokens (calibrated on N(0,1) logits, 16,384 tokens, top-4).
+ZIPF_S = 1.2
+ZIPF_BETA = 0.052
+
+
+def zipf_selection_bias(experts: int, beta: float = ZIPF_BETA, seed: int = 0):
+    """float32 expert bias beta * log p_e with p_e proportional to rank^-1.2
+    over a fixed random permutation of the expert ids (seed 0)."""
+    import torch
+
+    perm = torch.randperm(experts, generator=torch.Generator().manual_seed(seed))
+    rank = torch.empty(experts)
+    rank[perm] = torch.arange(1, experts + 1, dtype=torch.float32)
+    logp = -ZIPF_S * torch.log(rank)
+    return beta * (logp - torch.logsumexp(logp, 0))
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate/up GEMM
 # launch, from one single-pass ncu capture of the full-size bench workload:
@@ -82,6 +106,7 @@ def parse():
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel row exchange (N > 1): copy engines into IPC-mapped peer buffers, or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the extra config keys of the default line")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override the config's token count (small profiling cases)")
     return ap.parse_args()
@@ -98,14 +123,7 @@ def make_inputs(cfg, seed, device):
     import torch
 
     t, c, e, k, f = cfg["tokens"], cfg["dim"], cfg["experts"], cfg["top_k"], cfg["hidden"]
-    g = torch.Generator().manual_seed(seed)
-    x = torch.randn(t, c, generator=g).to(torch.bfloat16)
-    router = torch.randn(e, c, generator=g) * (1.0 / c) ** 0.5
-    bias = torch.zeros(e)
-    if cfg["skew"]:
-        # Zipf(s=1.2) expert popularity through the routing bias
-        ranks = torch.randperm(e, generator=torch.Generator().manual_seed(0)).float() + 1
-        bias = -1.2 * torch.log(ranks) * 0.08
+    x, router, bias = make_host_inputs(cfg, seed)
     gw = torch.Generator(device=device).manual_seed(seed + 1)
     gu = (torch.randn(e, c, 2 * f, generator=gw, device=device) * 0.02).to(torch.bfloat16)
     down = (torch.randn(e, f, c, generator=gw, device=device) * 0.02).to(torch.bfloat16)
@@ -165,15 +183,21 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_port_forward(prep, x, router, bias, cfg):
-    """The oracle's NVFP4 chain with dequantised fp32 weights (CPU port)."""
+def cpu_port_forward(prep, x, router, bias, cfg, routing=None):
+    """The oracle's NVFP4 chain with dequantised fp32 weights (CPU port of the
+    reference path): router, routing, dispatch, activation quantize, gate/up
+    GEMM, rescale + SwiGLU, hidden quantize, down GEMM, rescale + combine.
+    ``routing`` = (top_idx, gate) replaces the port's own router."""
     import torch
 
     from oracle import nvfp4_moe_oracle as O
 
     e, k, c, f = cfg["experts"], cfg["top_k"], cfg["dim"], cfg["hidden"]
-    logits = O.router_logits(x, router)
-    top, gate = O.route(logits, bias, k)
+    if routing is None:
+        logits = O.router_logits(x, router)
+        top, gate = O.route(logits, bias, k)
+    else:
+        top, gate = routing
     order, inverse, tokens, _sg, offsets, csr = O.dispatch(top, gate, e)
     pcsr = O.pad_csr(csr)
     m = tokens.numel()
@@ -197,80 +221,146 @@ def cpu_port_forward(prep, x, router, bias, cfg):
     return O.rescale_combine(raw, inverse, top, gate, csr, pcsr, hg, prep["dng"], 2.5)
 
 
-def cpu_baseline(cfg, budget_s=12.0, sample_tokens=None):
-    """Time the CPU port on a bounded token sample of the layer; tokens/s."""
+def port_weights(state, cfg):
+    """Packed bank buffers (CPU) -> the port's fp32 dequantised matrices and
+    global scales (load-time work, not timed)."""
+    from oracle import nvfp4_moe_oracle as O
+
+    c, f = cfg["dim"], cfg["hidden"]
+    n = state["gate_up_q"].shape[0]
+    return {"gu": [O.dequant_matrix(state["gate_up_q"][ex], state["gate_up_sf"][ex], 2 * f, c) for ex in range(n)],
+            "dn": [O.dequant_matrix(state["down_q"][ex], state["down_sf"][ex], c, f) for ex in range(n)],
+            "gug": state["gate_up_global"].float(), "dng": state["down_global"].float()}
+
+
+def port_weights_synthetic(cfg, distinct=8):
+    """The port's weights without a GPU: ``distinct`` experts' bf16 weights
+    ~ N(0, 0.02) packed with the oracle's recipe, expert e using those of
+    e % distinct (the CPU work per expert does not depend on the values)."""
     import torch
 
     from oracle import nvfp4_moe_oracle as O
 
-    threads = os.cpu_count() or 1
+    e, c, f = cfg["experts"], cfg["dim"], cfg["hidden"]
+    g = torch.Generator().manual_seed(8)
+    base = {"gu": [], "dn": [], "gug": [], "dng": []}
+    for _ in range(min(distinct, e)):
+        for key, (n, k) in (("gu", (2 * f, c)), ("dn", (c, f))):
+            w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+            q, sf, gg = O.pack_matrix(w)
+            base[key].append(O.dequant_matrix(q, sf, n, k))
+            base[key + "g"].append(float(gg))
+    d = len(base["gu"])
+    return {"gu": [base["gu"][ex % d] for ex in range(e)], "dn": [base["dn"][ex % d] for ex in range(e)],
+            "gug": torch.tensor([base["gug"][ex % d] for ex in range(e)]),
+            "dng": torch.tensor([base["dng"][ex % d] for ex in range(e)])}
+
+
+def time_port(prep, x, router, bias, cfg, threads, budget_s, max_runs, min_runs=1):
+    """Median seconds per forward of the CPU port on ``threads`` threads,
+    and the last output."""
+    import torch
+
     torch.set_num_threads(threads)
-    c, e, f = cfg["dim"], cfg["experts"], cfg["hidden"]
-    t = sample_tokens or min(cfg["tokens"], 1024)
-    sub = dict(cfg, tokens=t)
-    g = torch.Generator().manual_seed(7)
-    x = torch.randn(t, c, generator=g).to(torch.bfloat16)
-    router = torch.randn(e, c, generator=g) * (1.0 / c) ** 0.5
-    bias = torch.zeros(e)
-    # packed weights -> dequantised once (load-time work, not timed)
-    gw = torch.Generator().manual_seed(8)
-    prep = {"gu": [], "dn": [], "gug": torch.empty(e), "dng": torch.empty(e)}
-    for ex in range(e):
-        w1 = (torch.randn(2 * f, c, generator=gw) * 0.02).to(torch.bfloat16)
-        q, sf, gg = O.pack_matrix(w1)
-        prep["gu"].append(O.dequant_matrix(q, sf, 2 * f, c))
-        prep["gug"][ex] = gg
-        w2 = (torch.randn(c, f, generator=gw) * 0.02).to(torch.bfloat16)
-        q, sf, gg = O.pack_matrix(w2)
-        prep["dn"].append(O.dequant_matrix(q, sf, c, f))
-        prep["dng"][ex] = gg
-    times = []
+    times, out = [], None
     start = time.perf_counter()
-    while True:
+    while len(times) < max_runs:
         t0 = time.perf_counter()
-        cpu_port_forward(prep, x, router, bias, sub)
+        out = cpu_port_forward(prep, x, router, bias, cfg)
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() - start > budget_s or len(times) >= 5:
+        if len(times) >= min_runs and time.perf_counter() - start > budget_s:
             break
-    med = statistics.median(times)
+    return statistics.median(times), len(times), out
+
+
+def cpu_baseline(cfg, prep, x, router, bias, budget_s=30.0, max_runs=3, single_thread_tokens=2048):
+    """The CPU port on the full batch with every host thread, plus one thread
+    on the first ``single_thread_tokens`` tokens; tokens/s."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    t = x.shape[0]
+    med, runs, out = time_port(prep, x, router, bias, cfg, threads, budget_s, max_runs)
+    sub = min(t, single_thread_tokens)
+    med1, runs1, _ = time_port(prep, x[:sub].contiguous(), router, bias, dict(cfg, tokens=sub), 1, 10.0, 2)
+    torch.set_num_threads(threads)
     return {"value": t / med, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{t} tokens of the layer (C={c}, E={e}, k={cfg['top_k']}, F={f}), median of {len(times)} "
-                      f"forwards, weights dequantised once outside the timing"}
+            "sample": f"the full batch: {t} tokens (C={cfg['dim']}, E={cfg['experts']}, k={cfg['top_k']}, "
+                      f"F={cfg['hidden']}), median of {runs} forwards incl. the router, weights dequantised once "
+                      f"outside the timing",
+            "single_thread": {"value": sub / med1, "unit": "tokens/s", "cores": 1,
+                              "sample": f"first {sub} tokens of the batch, median of {runs1} forwards"}}, out
+
+
+def workload_config(cfg, name, world):
+    """The ``config`` object of a bench line (shared by both arms so that the
+    driver sees the same workload)."""
+    t = cfg["tokens"]
+    in_bytes = t * cfg["dim"] * 2
+    weights = cfg["experts"] * 3 * cfg["hidden"] * cfg["dim"] * (1 / 2 + 1 / 16)
+    fits = in_bytes + weights < 126e6
+    return {"workload": f"BASELINE config {name}: one MoE layer forward incl. router" +
+                        (" (expert parallel)" if world > 1 else ""),
+            "tokens" if world == 1 else "tokens_per_rank": t, "dim": cfg["dim"], "experts": cfg["experts"],
+            "top_k": cfg["top_k"], "expert_hidden": cfg["hidden"],
+            "router": "sigmoid+renorm" + (", Zipf(1.2) selection bias" if cfg["skew"] else ""),
+            "parallelism": f"ep{world}" if world > 1 else "single-gpu",
+            "l2": (f"activations + packed weights ({(in_bytes + weights) / 1e6:.0f} MB) fit in the 126 MB L2 "
+                   "(steady-state serving: weights stay resident)") if fits else
+                  (f"activations + packed weights ({(in_bytes + weights) / 1e6:.0f} MB) exceed the 126 MB L2; "
+                   "no flush")}
 
 
 def run_reference(args, cfg):
+    """``--impl reference``: the CPU port of the reference path on the box's
+    host cores, on the same workload as the GPU arm; rank 0 only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    cb = cpu_baseline(cfg, budget_s=max(5.0, 2.0 * args.steps))
-    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": f"config {args.config}", **cfg}, "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    import torch
+
+    c, e = cfg["dim"], cfg["experts"]
+    x, router, bias = make_host_inputs(cfg, 1000)
+    prep = port_weights_synthetic(cfg)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    for _ in range(min(args.warmup, 1)):
+        cpu_port_forward(prep, x, router, bias, cfg)
+    med, runs, _ = time_port(prep, x, router, bias, cfg, threads, budget_s=120.0, max_runs=args.steps,
+                             min_runs=min(args.steps, 3))
+    value = cfg["tokens"] / med
+    sample = (f"the full batch of {cfg['tokens']} tokens per forward, median of {runs} of the {args.steps} "
+              f"requested forwards (capped at ~2 min of CPU time), 1 warm-up forward")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, fp32 accumulate)",
+            "data": "synthetic", "config": workload_config(cfg, args.config, world),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_b200(args, cfg):
+def make_host_inputs(cfg, seed):
+    """x, router weight and routing bias of a config on the host (the seeds
+    of make_inputs)."""
     import torch
-    import torch.distributed as dist
 
-    rank, world, local = dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local if world > 1 else 0)
-    torch.cuda.set_device(dev)
-    pkg = importlib.import_module("praxis-1-oss_b200")
-    pkg.capi.load()
-    peaks = {}
-    pfile = ROOT / "MEASURED_PEAKS.json"
-    if pfile.exists():
-        peaks = json.loads(pfile.read_text())
+    t, c, e = cfg["tokens"], cfg["dim"], cfg["experts"]
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(t, c, generator=g).to(torch.bfloat16)
+    router = torch.randn(e, c, generator=g) * (1.0 / c) ** 0.5
+    bias = zipf_selection_bias(e) if cfg["skew"] else torch.zeros(e)
+    return x, router, bias
+
+
+def build_layer(pkg, cfg, seed, dev):
+    """A B200MoEFeedForward of the config with seeded weights; returns the
+    module, its bank, kernel weights, router terms, host inputs and the
+    layer call (x, out) -> (out, top_idx, gate) through the public op."""
+    import torch
 
     t, c, e, k, f = cfg["tokens"], cfg["dim"], cfg["experts"], cfg["top_k"], cfg["hidden"]
-    x_cpu, router, bias, gu, down = make_inputs(cfg, 1000 + rank, dev)
+    x_cpu, router, bias, gu, down = make_inputs(cfg, seed, dev)
     mod = pkg.B200MoEFeedForward(c, f, e, k, 2.5, dispatch_chunk_size=t, shared_expert=False).to(dev)
     with torch.no_grad():
         mod.router.weight.copy_(router.to(dev))
@@ -281,8 +371,6 @@ def run_b200(args, cfg):
     bank.prepare()
     terms = mod.router_terms()
     kw = bank.kernel_weights()
-    x = x_cpu.to(dev)
-    out = torch.empty_like(x)
     ops = pkg.ops
 
     def layer(xin, yout):
@@ -291,22 +379,89 @@ def run_b200(args, cfg):
                                top_k=k, out=yout, gate_up_sf_layout=kw.gate_up_sf_layout,
                                down_sf_layout=kw.down_sf_layout)
 
-    def step():
-        return layer(x, out)
+    return dict(mod=mod, bank=bank, kw=kw, terms=terms, x_cpu=x_cpu, router=router, bias=bias, layer=layer)
 
-    # correctness guard of the measured path: routing and output vs the
-    # stage-by-stage ops path (same kernels, separate launches)
+
+def time_steps(step, dev, steps, warmup):
+    """ms per step: CUDA events on the launching stream around ``steps``
+    back-to-back steps after ``warmup`` untimed ones."""
+    import torch
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return ev0.elapsed_time(ev1) / steps
+
+
+def gpu_parity(pkg, L, x, cfg):
+    """The measured path (one fused praxis_b200_moe_forward with the router)
+    against the same kernels launched stage by stage through the ops: routing
+    and output bit for bit (GPU only; the oracle check is in the CPU leg)."""
+    import torch
+
+    ops, capi = pkg.ops, pkg.capi
+    bank, kw, mod = L["bank"], L["kw"], L["mod"]
+    e, k = cfg["experts"], cfg["top_k"]
+    out_f, top_f, gate_f = L["layer"](x, torch.empty_like(x))
+    logits, amax = ops.router_logits(x, L["terms"])
+    top, gate = ops.route(logits, mod.expert_bias, k)
+    r = ops.dispatch(top, gate, e, amax, full=False)
+    aq, asf = ops.quantize_gather(x, r, r.act_global)
+    hamax = torch.zeros(e, dtype=torch.int32, device=x.device)
+    hidden = ops.grouped_gemm(aq, ops.replicate_scales(asf, 128), kw.gate_up_q, kw.gate_up_sf, r,
+                              epilogue=capi.EPI_SWIGLU, act_global=r.act_global, w_global=bank.gate_up_global,
+                              amax_out=hamax, sf_layout=kw.gate_up_sf_layout)
+    hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
+    rows = ops.grouped_gemm(hq, hsf, bank.down_q, kw.down_sf, r, epilogue=capi.EPI_RESCALE, act_amax=hamax,
+                            w_global=bank.down_global, sf_layout=kw.down_sf_layout)
+    out_s = ops.combine(rows, r, 2.5, rows_rescaled=True)
+    # the reference's stock routing ops (praxis/layers.py:2167-2173) by torch on this GPU
+    scores = torch.sigmoid(logits)
+    ref_top = torch.topk(scores + mod.expert_bias, k, dim=-1).indices
+    picked = scores.gather(-1, ref_top)
+    ref_gate = (picked / picked.sum(-1, keepdim=True)).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    same = lambda a, b: bool(torch.equal(a.view(torch.uint8), b.view(torch.uint8)))  # noqa: E731
+    err = capi.device_error(x.device.index or 0)
+    res = {"fused_vs_stage_ops_bit_exact": same(out_f, out_s) and same(top_f, top) and same(gate_f, gate),
+           "routing_bit_exact_vs_torch_stock_ops": same(top, ref_top) and same(gate, ref_gate),
+           "device_error_word": err}
+    counts = torch.bincount(top.flatten(), minlength=e).cpu()
+    return res, dict(logits=logits.cpu(), top=top.cpu(), gate=gate.cpu(), out=out_f.cpu()), counts
+
+
+def run_b200(args, cfg):
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module("praxis-1-oss_b200")
+    pkg.capi.load()
+    peaks = {}
+    pfile = ROOT / "MEASURED_PEAKS.json"
+    if pfile.exists():
+        peaks = json.loads(pfile.read_text())
+
+    t, c, e, k, f = cfg["tokens"], cfg["dim"], cfg["experts"], cfg["top_k"], cfg["hidden"]
+    L = build_layer(pkg, cfg, 1000, dev)
+    x = L["x_cpu"].to(dev)
+    out = torch.empty_like(x)
+    parity, gpu_res, counts = gpu_parity(pkg, L, x, cfg)
+
+    def step():
+        return L["layer"](x, out)
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     stream = torch.cuda.current_stream(dev)
-    barrier()
-    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
         ev0.record(stream)
@@ -314,21 +469,12 @@ def run_b200(args, cfg):
             step()
         ev1.record(stream)
         torch.cuda.synchronize()
-    barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    value = t * world / (ms / 1e3)
-
-    latency = None
-    if args.config == "5":
-        latency = graph_latency(step, dev, calls=max(20, args.steps * 5))
+    value = t / (ms / 1e3)
 
     # per-stage timing (same kernels launched stage by stage, events on the
     # launching stream) for the roofline of the dominant kernel
-    stages = time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=max(3, min(args.steps, 10)))
+    stages = time_stages(pkg, x, L["terms"], L["mod"], L["bank"], L["kw"], cfg, reps=max(3, min(args.steps, 10)))
     gemm1_ms = stages["gemm1_swiglu"]
     flops1 = 2.0 * t * k * c * 2 * f
     bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
@@ -341,34 +487,120 @@ def run_b200(args, cfg):
                 "algorithmic_bytes": gemm1_bytes(t, k, c, f, e),
                 "peak_note": ("dense FP4 peak = 4 x measured cuBLAS bf16 burst "
                               f"({bf16_peak} TFLOP/s, MEASURED_PEAKS.json); nominal dense FP4 9000 TFLOP/s")}
+    gemm2_ms = stages["gemm2_rescale"]
+    roofline["down_gemm"] = {"kernel": "gemm_nvfp4_pair_kernel<EPI_RESCALE> (down)",
+                             "achieved": 2.0 * t * k * f * c / (gemm2_ms / 1e3) / 1e12,
+                             "frac": 2.0 * t * k * f * c / (gemm2_ms / 1e3) / 1e12 / fp4_peak}
     layer_flops = 6.0 * t * k * c * f
     e2e = None
     if not args.no_e2e:
-        e2e = time_e2e(pkg, layer, x_cpu, out, args, dev, t, world)
+        e2e = time_e2e(pkg, L["layer"], L["x_cpu"], out, args, dev, t, 1)
+
+    extra = {}
+    if args.config == "2" and not args.no_extra:
+        extra = extra_configs(pkg, L, args, dev)
+
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 block16 scales, fp32 accumulate), bf16 I/O",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) expert weights packed to NVFP4)",
-        "config": {"workload": f"BASELINE config {args.config}: one MoE layer forward incl. router", "tokens": t,
-                   "dim": c, "experts": e, "top_k": k, "expert_hidden": f, "router": "sigmoid+renorm",
-                   "parallelism": "replicas" if world > 1 else "single-gpu",
-                   "l2": "inputs + packed weights (610 MB) exceed the 126 MB L2; no flush"},
+        "config": workload_config(cfg, args.config, 1),
         "layer_tflops": layer_flops / (ms / 1e3) / 1e12,
         "stages_ms": stages,
         "roofline": roofline,
-        "graph_latency": latency,
+        "expert_rows": {"max": int(counts.max()), "min": int(counts.min()), "top_expert_token_share": float(
+            counts.max()) / t},
         "clocks": clk.summary(),
-        # router 2, dispatch 3, quantize 2 + scale replication 1, GEMM 2, combine 1
+        # router 2, dispatch 3, quantize 1 + scale replication 1, GEMM 2, hidden quantize 1, combine 1
         "gpu_launches": 11 * args.steps,
         "e2e": e2e,
+        "parity": parity,
+        **extra,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    if args.config == "5":
+        line["graph_latency"] = graph_latency(step, dev, calls=max(20, args.steps * 5))
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"], port_out = cpu_leg_with_parity(L, cfg, gpu_res)
+        parity.update(port_out)
+    parity["ok"] = bool(parity["fused_vs_stage_ops_bit_exact"] and parity["device_error_word"] == 0 and
+                        parity["routing_bit_exact_vs_torch_stock_ops"] and
+                        parity.get("topk_agreement_oracle_on_gpu_logits", 1.0) >= 0.9999 and
+                        parity.get("gate_max_bf16_ulp_vs_oracle", 0) <= 1 and
+                        parity.get("out_rel_l2_vs_port", 0.0) <= 1e-2)
+    print(json.dumps(line), flush=True)
+
+
+def cpu_leg_with_parity(L, cfg, gpu_res):
+    """The CPU baseline on the GPU arm's own packed weights and inputs, and
+    the parity of the GPU results with it: routing on the GPU's logits
+    (bit for bit) and the layer output (relative L2, bar 1e-2)."""
+    import torch
+
+    from oracle import nvfp4_moe_oracle as O
+
+    bank = L["bank"]
+    state = {n: getattr(bank, n).cpu() for n in ("gate_up_q", "gate_up_sf", "gate_up_global", "down_q", "down_sf",
+                                                 "down_global")}
+    prep = port_weights(state, cfg)
+    cb, port_out = cpu_baseline(cfg, prep, L["x_cpu"], L["router"], L["bias"])
+    top, gate = O.route(gpu_res["logits"], L["bias"], cfg["top_k"], tie_order="cuda")
+    port_top = O.route(O.router_logits(L["x_cpu"], L["router"]), L["bias"], cfg["top_k"])[0]
+    gd = (gate.view(torch.int16).int() - gpu_res["gate"].view(torch.int16).int()).abs()
+    res = {"topk_agreement_oracle_on_gpu_logits": float((top == gpu_res["top"]).all(-1).float().mean()),
+           "gate_max_bf16_ulp_vs_oracle": int(gd.max()),
+           "topk_agreement_port_router": float((port_top == gpu_res["top"]).all(-1).float().mean()),
+           "out_rel_l2_vs_port": O.rel_l2(gpu_res["out"], port_out),
+           "bar": ("routing bit-exact against torch's stock routing ops on the GPU; against the CPU oracle (CPU "
+                   "sigmoid) >= 99.99% of tokens and gates within 1 bf16 ulp; output relative L2 <= 1e-2 against "
+                   "the CPU port (dequantised fp32 chain, its own router)")}
+    return cb, res
+
+
+def extra_configs(pkg, L, args, dev):
+    """Extra keys of the default line: config 3 (same weights, Zipf-skewed
+    routing bias), config 4's per-rank shape on one GPU, config 5 (own
+    weights, CUDA-graph latency)."""
+    import torch
+
+    out = {}
+    steps, warm = max(5, args.steps // 2), 3
+    mod, cfg2 = L["mod"], CONFIGS["2"]
+    # config 3: the same layer with the calibrated Zipf(1.2) selection bias
+    cfg3 = CONFIGS["3"]
+    x3, _r, bias3 = make_host_inputs(cfg3, 1003)
+    xd3, y3 = x3.to(dev), torch.empty(x3.shape, dtype=torch.bfloat16, device=dev)
+    keep = mod.expert_bias.clone()
+    with torch.no_grad():
+        mod.expert_bias.copy_(bias3.to(dev))
+    ms3 = time_steps(lambda: L["layer"](xd3, y3), dev, steps, warm)
+    _, top3, _ = L["layer"](xd3, y3)
+    cnt = torch.bincount(top3.flatten(), minlength=cfg3["experts"]).cpu()
+    with torch.no_grad():
+        mod.expert_bias.copy_(keep)
+    out["config3"] = {"workload": "BASELINE config 3: config 2 shapes, Zipf(1.2) expert popularity through the "
+                                  f"routing bias (strength {ZIPF_BETA})",
+                      "ms_per_step": ms3, "value": cfg3["tokens"] / (ms3 / 1e3), "unit": "tokens/s",
+                      "top_expert_token_share": float(cnt.max()) / cfg3["tokens"],
+                      "expert_rows_sorted": sorted(cnt.tolist(), reverse=True), "steps": steps}
+    # config 4's per-rank load on one GPU (65,536 tokens, the same weights)
+    cfg4 = CONFIGS["4"]
+    x4, _r, _b = make_host_inputs(cfg4, 1000)
+    xd4, y4 = x4.to(dev), torch.empty(x4.shape, dtype=torch.bfloat16, device=dev)
+    ms4 = time_steps(lambda: L["layer"](xd4, y4), dev, steps, warm)
+    out["config4_single_gpu"] = {"workload": "config 4's per-rank shape (65,536 tokens) on one GPU: the "
+                                             "like-for-like base of the expert-parallel scaling run",
+                                 "ms_per_step": ms4, "value": cfg4["tokens"] / (ms4 / 1e3), "unit": "tokens/s",
+                                 "steps": steps}
+    del xd4, y4
+    # config 5: its own layer, whole forward in one CUDA graph, 10 Euler steps
+    cfg5 = CONFIGS["5"]
+    L5 = build_layer(pkg, cfg5, 1005, dev)
+    x5 = L5["x_cpu"].to(dev)
+    y5 = torch.empty_like(x5)
+    lat = graph_latency(lambda: L5["layer"](x5, y5), dev, calls=max(20, args.steps * 2))
+    out["config5_graph_latency"] = dict(lat, workload="BASELINE config 5: T=512, C=1024, E=32, k=2, F=2048")
+    return out
 
 
 def run_expert_parallel(args, cfg):
@@ -400,10 +632,15 @@ def run_expert_parallel(args, cfg):
     # generated from one seed, each rank packs its own experts)
     x_cpu, router, bias, _gu, _dn = make_inputs(dict(cfg, experts=0), 1000 + rank, dev)
     gw = torch.Generator(device=dev).manual_seed(7)
-    gu = (torch.randn(e, c, 2 * f, generator=gw, device=dev) * 0.02).to(torch.bfloat16)[rank * el:(rank + 1) * el]
-    down = (torch.randn(e, f, c, generator=gw, device=dev) * 0.02).to(torch.bfloat16)[rank * el:(rank + 1) * el]
-    bank = pkg.pack_routed_experts(gu.contiguous(), down.contiguous(), keep_on_device=True)
+    gu = (torch.randn(e, c, 2 * f, generator=gw, device=dev) * 0.02).to(torch.bfloat16)
+    down = (torch.randn(e, f, c, generator=gw, device=dev) * 0.02).to(torch.bfloat16)
+    # the whole bank on every rank, for the parity check against one GPU; the
+    # expert-parallel layer keeps this rank's shard of the same bytes
+    full = pkg.pack_routed_experts(gu, down, keep_on_device=True)
     del gu, down
+    names = ("gate_up_q", "gate_up_sf", "gate_up_global", "down_q", "down_sf", "down_global", "_unit_alpha")
+    shard = pkg.expert_parallel.shard_packed_state({n: getattr(full, n) for n in names}, rank, world)
+    bank = pkg.B200NVFP4RoutedExperts.from_device_state(shard)
     bank.prepare()
     ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e, transport=args.transport, chunks=args.ep_chunks,
                                                          copy_streams=args.copy_streams,
@@ -419,6 +656,22 @@ def run_expert_parallel(args, cfg):
         logits, _amax = ops.router_logits(xin, terms)
         top, gate = ops.route(logits, bias, k)
         return ep.routed_forward(xin, top, gate, scaling=2.5)
+
+    # parity: this rank's expert-parallel output against the single-GPU bank
+    # on the same tokens and routing, bit for bit (every rank checks its own;
+    # the result is all-reduced so rank 0 reports whether all ranks agree)
+    logits0, _ = ops.router_logits(x, terms)
+    top0, gate0 = ops.route(logits0, bias, k)
+    got = ep.routed_forward(x, top0, gate0, scaling=2.5)
+    want = full.routed_forward(x, top0, gate0, scaling=2.5, chunk_size=t)
+    torch.cuda.synchronize()
+    ok = torch.tensor([int(torch.equal(got.view(torch.int16), want.view(torch.int16))),
+                       int(pkg.capi.device_error(dev.index) == 0)], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    ep_parity = {"bit_exact_vs_single_gpu_all_ranks": bool(ok[0].item()), "device_error_free": bool(ok[1].item()),
+                 "check": "each rank's output vs the single-GPU bank on its tokens (all 64 experts on one GPU)"}
+    del got, want, full
+    torch.cuda.empty_cache()
 
     for _ in range(args.warmup):
         step()
@@ -470,6 +723,19 @@ def run_expert_parallel(args, cfg):
                 "frac": flops / (exp_ms / 1e3) / 1e12 / fp4_peak, "traffic": None,
                 "peak_note": "4 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json); rows of this rank's own tokens "
                              "through its local experts' weights, one launch sequence"}
+    # bytes this rank's tokens move over NVLink per step: FP4 rows + scales of
+    # whole padded tiles to the other ranks' experts, bf16 rows back; by
+    # symmetry each direction of a rank's links carries about this much
+    blocks = (pc[el::el] - pc[:-1:el]).tolist()
+    off = sum(b for d, b in enumerate(blocks) if d != rank)
+    xbytes = torch.tensor([float(off * (c // 2 + c // 16 + 2 * c))], device=dev)
+    dist.all_reduce(xbytes, op=dist.ReduceOp.MAX)
+    exchange = {"bytes_per_rank_per_step": float(xbytes.item()),
+                "gbs_per_rank": float(xbytes.item()) / (ms / 1e3) / 1e9,
+                "nvlink_peer_copy_gbs_measured": 770.0,
+                "transport": ("copy engines into IPC-mapped peer buffers" if args.transport == "peer" else
+                              "NCCL point-to-point") + ": FP4 rows + UE4M3 scales out, bf16 rows back",
+                "experts_per_rank": el, "sm_copy_fraction": args.sm_copy_fraction}
     e2e = None
     if not args.no_e2e:
         torch.cuda.synchronize()
@@ -481,12 +747,9 @@ def run_expert_parallel(args, cfg):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 block16 scales, fp32 accumulate), bf16 I/O",
         "data": "synthetic (seeded N(0,1) activations per rank, N(0,0.02) expert weights packed to NVFP4)",
-        "config": {"workload": f"BASELINE config {args.config}: expert-parallel MoE layer forward incl. router",
-                   "tokens_per_rank": t, "dim": c, "experts": e, "experts_per_rank": el, "top_k": k,
-                   "expert_hidden": f, "router": "sigmoid+renorm", "parallelism": f"ep{world}",
-                   "exchange": ("copy engines into IPC-mapped peer buffers" if args.transport == "peer" else
-                                "NCCL point-to-point") + ": FP4 rows + UE4M3 scales out, bf16 rows back",
-                   "l2": "per-rank inputs and weights exceed the 126 MB L2; no flush"},
+        "config": workload_config(cfg, args.config, world),
+        "exchange": exchange,
+        "ep_parity": ep_parity,
         "layer_tflops": flops * world / (ms / 1e3) / 1e12,
         "roofline": roofline,
         "clocks": clk.summary() if clk is not None else None,
@@ -532,9 +795,24 @@ def graph_latency(step, dev, calls=50, euler_steps=10):
         torch.cuda.synchronize()
         times += [evs[i].elapsed_time(evs[i + 1]) for i in range(euler_steps)]
     times.sort()
-    del graph
+    # the same replays with L2 flushed before each one (a 256 MB write outside
+    # the events): the cold-cache latency of a layer whose weights were evicted
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    cold = []
+    for _ in range(max(10, calls)):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        cold.append(e0.elapsed_time(e1))
+    cold.sort()
+    del graph, flush
     return {"p50_ms": times[len(times) // 2], "p90_ms": times[(len(times) * 9) // 10], "calls": len(times),
-            "euler_steps_per_loop": euler_steps, "capture": "whole layer incl. router in one CUDA graph"}
+            "euler_steps_per_loop": euler_steps, "capture": "whole layer incl. router in one CUDA graph",
+            "l2": "back-to-back replays of the Euler loop reuse the weights (113 MB, L2-resident)",
+            "p50_ms_l2_flushed": cold[len(cold) // 2], "p90_ms_l2_flushed": cold[(len(cold) * 9) // 10]}
 
 
 def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):

@@ -313,6 +313,46 @@ def gate_sum(picked: torch.Tensor) -> torch.Tensor:
     return lanes[0]
 
 
+def exp_softmax(x: torch.Tensor) -> torch.Tensor:
+    """e^x (x <= 0) of the softmax router, defined op by op so that the CUDA
+    kernel and this restatement give the same bits: Cody and Waite's range
+    reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
+    Functions", 1980), x = n ln2 + r with n = rint(x log2 e) and ln2 = C1 + C2,
+    then e^r by its degree-7 Taylor polynomial in Horner form, then 2^n; each
+    step one float32 multiply or add rounded to nearest. x < -87 -> 0."""
+    x = x.to(_F32)
+    c = lambda h: torch.tensor(float.fromhex(h), dtype=_F32)  # noqa: E731
+    n = torch.round(x * c("0x1.715476p+0"))  # half to even, as rint
+    r = x + (-n) * c("0x1.63p-1")
+    r = r + (-n) * c("-0x1.bd0106p-13")
+    q = c("0x1.a01a02p-13").expand_as(r)
+    for h in ("0x1.6c16c2p-10", "0x1.111112p-7", "0x1.555556p-5", "0x1.555556p-3", "0x1.0p-1", "0x1.0p+0",
+              "0x1.0p+0"):
+        q = q * r + c(h)
+    scale = ((n.clamp(-126, 127).to(torch.int32) + 127) << 23).view(_F32)
+    out = q * scale
+    out = torch.where(x < -87.0, torch.zeros_like(out), out)
+    return torch.where(x != x, x, out)
+
+
+def softmax_rows(logits: torch.Tensor) -> torch.Tensor:
+    """Softmax over the experts in the routing kernel's order (one warp per
+    token, expert e on lane e % 32): p = exp_softmax(l - max); lane l sums
+    its experts l, l + 32, ... in that order, a butterfly over lane distances
+    16, 8, 4, 2, 1 adds the 32 lane sums; score = p / sum (IEEE division)."""
+    logits = logits.to(_F32)
+    t, e = logits.shape
+    p = exp_softmax(logits - logits.amax(-1, keepdim=True))
+    lanes = torch.zeros(t, 32, dtype=_F32)
+    for i in range((e + 31) // 32):
+        chunk = p[:, 32 * i: 32 * (i + 1)]
+        lanes[:, : chunk.shape[1]] = lanes[:, : chunk.shape[1]] + chunk
+    lane = torch.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        lanes = lanes + lanes[:, lane ^ o]
+    return p / lanes[:, :1]
+
+
 def route(
     logits: torch.Tensor,
     bias: torch.Tensor | None,
@@ -321,8 +361,10 @@ def route(
     tie_order: str = "cuda",
 ):
     """Stock routing: praxis/layers.py:1647-1653 (sigmoid, the reference's
-    only router). ``activation="softmax"`` is this build's extension:
-    softmax over the experts, then the same bias / top-k / renormalisation.
+    only router). ``activation="softmax"`` is this build's extension
+    (BASELINE config 1's softmax router): ``softmax_rows`` (an explicit
+    exponential and sum order, see there), then the same bias / top-k /
+    renormalisation.
 
     ``tie_order="cuda"`` emulates torch.topk's CUDA slot order and ATen's CUDA
     sum order; ``"torch"`` calls the torch ops of the reference on the CPU.
@@ -331,7 +373,7 @@ def route(
     if activation == "sigmoid":
         scores = torch.sigmoid(logits)
     elif activation == "softmax":
-        scores = torch.softmax(logits, dim=-1)
+        scores = softmax_rows(logits) if tie_order == "cuda" else torch.softmax(logits, dim=-1)
     else:
         raise ValueError(activation)
     biased = scores if bias is None else scores + bias.to(_F32)

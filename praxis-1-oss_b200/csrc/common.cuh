@@ -113,6 +113,35 @@ __device__ __forceinline__ float sigmoid_triton(float x) {
   return div_rn(1.0f, add_rn(1.0f, e));
 }
 
+// e^x for x <= 0, the softmax router's exponential (x = logit - row max).
+// Cody and Waite's range reduction (W. J. Cody, W. Waite, "Software Manual
+// for the Elementary Functions", 1980): x = n ln2 + r with n = rint(x log2 e)
+// and ln2 split as C1 + C2 (C1 = 355/512 has 9 significant bits, so n * C1 is
+// exact for |n| <= 127), then e^r (|r| <= ln2 / 2) by its Taylor polynomial
+// to degree 7 in Horner form (truncation below 2^-27 relative), then 2^n by
+// exponent arithmetic. Every step is one IEEE-rounded float32 multiply or add
+// with no contraction, so a float32 restatement on the CPU gives the same
+// bits (the oracle's route(activation="softmax") does). Within 2 ulp of e^x;
+// x < -87 gives 0 (below every softmax probability that can reach a top-k
+// slot), NaN stays NaN.
+__device__ __forceinline__ float exp_softmax(float x) {
+  if (x != x) return x;
+  if (x < -87.0f) return 0.0f;
+  // float32 constants as exact hex literals: log2 e, C1, C2, 1/5040 .. 1/6
+  const float n = rintf(__fmul_rn(x, 0x1.715476p+0f));
+  float r = __fadd_rn(x, __fmul_rn(-n, 0x1.63p-1f));
+  r = __fadd_rn(r, __fmul_rn(-n, -0x1.bd0106p-13f));
+  float q = 0x1.a01a02p-13f;
+  q = __fadd_rn(__fmul_rn(q, r), 0x1.6c16c2p-10f);
+  q = __fadd_rn(__fmul_rn(q, r), 0x1.111112p-7f);
+  q = __fadd_rn(__fmul_rn(q, r), 0x1.555556p-5f);
+  q = __fadd_rn(__fmul_rn(q, r), 0x1.555556p-3f);
+  q = __fadd_rn(__fmul_rn(q, r), 0.5f);
+  q = __fadd_rn(__fmul_rn(q, r), 1.0f);
+  q = __fadd_rn(__fmul_rn(q, r), 1.0f);
+  return __fmul_rn(q, __int_as_float(((int)n + 127) << 23));
+}
+
 // ---------------------------------------------------------------------------
 // ALU-only variants for the GEMM epilogues. The conversion/transcendental
 // (XU) pipe is the epilogue's bottleneck, so roundings use integer ops and

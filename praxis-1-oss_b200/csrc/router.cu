@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 #pragma unroll
     for (int i = 0; i < P; ++i) {
       const int e = lane + 32 * i;
-      score[i] = e < experts ? expf(__fsub_rn(score[i], lmax)) : 0.0f;
+      score[i] = e < experts ? exp_softmax(__fsub_rn(score[i], lmax)) : 0.0f;
       sum = add_rn(sum, score[i]);
     }
 #pragma unroll

@@ -149,3 +149,33 @@ def test_nvfp4_chain_is_close_to_bf16_reference_layer():
     y, _, _ = O.moe_forward(x, params["router.weight"], torch.zeros(e), bank, k, 2.5, t,
                             shared=lay["shared"])
     assert O.rel_l2(y, lay["y"]) < 0.3
+
+
+def test_softmax_exponential_is_within_two_ulp():
+    """The routing kernel's softmax exponential (restated op by op here) is an
+    explicit Cody-Waite + Taylor evaluation: within 2 ulp of e^x on the range
+    a softmax uses, exactly 1 at 0, 0 below -87."""
+    g = torch.Generator().manual_seed(0)
+    x = torch.cat([-torch.rand(1_000_000, generator=g, dtype=torch.float64) * 87,
+                   -torch.rand(200_000, generator=g, dtype=torch.float64) * 0.5,
+                   torch.tensor([-0.0, -1e-30, -0.34657, -0.34658, -86.999, -87.0])]).float()
+    got = O.exp_softmax(x).double()
+    ref = torch.exp(x.double())
+    ulp = torch.nextafter(ref.float(), torch.tensor(float("inf"))).double() - ref.float().double()
+    assert ((got - ref).abs() / ulp).max().item() < 2.0
+    assert O.exp_softmax(torch.tensor([0.0])).item() == 1.0
+    assert O.exp_softmax(torch.tensor([-87.5, -1e30])).tolist() == [0.0, 0.0]
+    assert O.exp_softmax(torch.tensor([float("nan")])).isnan().all()
+
+
+def test_softmax_rows_sum_order_and_accuracy():
+    g = torch.Generator().manual_seed(1)
+    for e in (8, 32, 64, 100, 256):
+        logits = torch.randn(300, e, generator=g) * 4
+        got = O.softmax_rows(logits)
+        ref = torch.softmax(logits.double(), -1)
+        # float32 softmax: the rounding of l - max (|l - max| up to ~30 here)
+        # carries into e^x, as in torch's own float32 softmax
+        f32 = torch.softmax(logits, -1).double()
+        err, err_torch = ((got.double() - ref).abs() / ref).max().item(), ((f32 - ref).abs() / ref).max().item()
+        assert err < 4e-6 and err < 4 * err_torch + 1e-6, (e, err, err_torch)

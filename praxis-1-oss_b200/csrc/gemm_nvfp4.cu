@@ -302,16 +302,15 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
 // (columns 128..255). Each epilogue warp drains the 64-column block it owns
 // inside the overlap first and then releases, so the next tile's MMAs start
 // after one tensor-memory load per warp. Scales live in columns 384..479: two
-// slots of 48 columns (A scales at +0, B scales at +16), one per k-tile in
-// flight.
+// slots of 48 columns (A scales at +0, B scales at +16) used by alternate
+// k-tiles.
 //
 // Roles: warp 0 TMA (both CTAs; completion counted on the leader's barrier),
-// warp 1 MMA issuer (leader CTA only), warps 2..9 epilogue (both CTAs, two
-// warps per TMEM lane quadrant; the warps of half h take 64-column blocks h
-// and h + 2), warp 10 scale copier (leader CTA only). The scale copies run in
-// the tensor pipe like the MMAs; issued by their own warp into the slot the
-// MMAs are not reading, they overlap the MMAs (issued by the MMA thread, each
-// copy waits for the MMAs issued before it).
+// warp 1 MMA issuer and scale copier (leader CTA only), warps 2..9 epilogue
+// (both CTAs, two warps per TMEM lane quadrant; the warps of half h take
+// 64-column blocks h and h + 2). The scale copies run in the tensor pipe in
+// order with the MMAs; the MMA thread issues each k-tile's copies just
+// before its MMAs, so nothing waits on a copy's completion.
 //
 // Scale factors reach tensor memory in one of two ways:
 //  REP = false  the reference's compact layout (512-byte atom = 128 rows x 4
@@ -337,26 +336,36 @@ template <bool REP, bool DIRECT>
 struct PairShape {
   static constexpr int BN = 256;
   static constexpr int BK_BYTES = 128;
-  static constexpr int STAGES = REP ? (DIRECT ? 4 : 3) : 4;
   static constexpr int A_BYTES = 128 * BK_BYTES;
   static constexpr int B_BYTES = 128 * BK_BYTES;
   static constexpr int SF_COPIES = REP ? 4 : 1;
   static constexpr int SFA_BYTES = 4 * 512 * SF_COPIES;      // 4 k-blocks
   static constexpr int SFB_BYTES = 2 * 4 * 512 * SF_COPIES;  // 2 row-tiles x 4 k-blocks
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-  static constexpr int ACC_ALT_COL = 128;  // start of every other accumulator
-  static constexpr int SF_COL = 384;       // scale slot s: A at +48s, B at +48s + 16
-  static constexpr int SF_SLOT_COLS = 48;
-  static constexpr int TMEM_COLS = 512;
-  static constexpr int EPI_WARPS = 8;
-  static constexpr int THREADS = 96 + 32 * EPI_WARPS;
-  static constexpr int COPY_WARP = 2 + EPI_WARPS;
   // Output staging per epilogue warp: one 32 x 64 bf16 box (4 KB) in the TMA
   // 128-byte swizzle (none for direct stores).
   static constexpr int OUT_STAGE_BYTES = DIRECT ? 0 : 4096;
+  static constexpr int EPI_WARPS = 8;
+  // As many k-tile stages as fit beside the output staging (5 with compact
+  // scales, 3 or 4 with replicated ones).
+  static constexpr int STAGES_FIT = (232448 - 1024 - 256 - EPI_WARPS * OUT_STAGE_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 5 ? 5 : STAGES_FIT;
+  static constexpr int ACC_ALT_COL = 128;  // start of every other accumulator
+  // Scale slots: one per k-tile, A scales at +0 (16 columns), B scales at +16
+  // (32 columns); two slots in the columns 384..479 the accumulators leave
+  // free, used in turn.
+  static constexpr int SF_COL = 384;
+  static constexpr int SF_SLOT_COLS = 48;
+  static constexpr int SF_SLOTS = 2;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(SF_COL + SF_SLOTS * SF_SLOT_COLS <= TMEM_COLS, "tensor memory budget");
+  static constexpr int SF_WARP0 = 2 + EPI_WARPS;  // scale loaders: one warp per lane quadrant
+  static constexpr int SF_WARPS = 4;
+  static constexpr int THREADS = 32 * (SF_WARP0 + SF_WARPS);
   static constexpr size_t SMEM_BYTES =
       1024 + (size_t)STAGES * STAGE_BYTES + (size_t)EPI_WARPS * OUT_STAGE_BYTES + 256;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(STAGES >= 3, "pipeline depth");
 };
 
 // Writes 8 bf16 (16 bytes) of row `row` (0..31), 16-byte chunk `chunk` (0..7)
@@ -387,13 +396,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
   uint8_t* sSFB = sSFA + S::STAGES * S::SFA_BYTES;
   uint8_t* sOut = sSFB + S::STAGES * S::SFB_BYTES;  // 1 KB aligned (stage sizes are multiples of 1 KB)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + S::EPI_WARPS * S::OUT_STAGE_BYTES);
-  uint64_t* full = bars;                   // leader: both CTAs' loads of a stage
-  uint64_t* empty = bars + S::STAGES;      // each CTA: stage free again
-  uint64_t* acc_full = bars + 2 * S::STAGES;
-  uint64_t* acc_empty = acc_full + 1;      // leader: 16 epilogue warps of the pair
-  uint64_t* sf_ready = acc_empty + 1;     // leader: a scale slot holds its k-tile's scales
-  uint64_t* sf_free = sf_ready + 2;       // leader: the MMAs reading a scale slot are done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + 2);
+  uint64_t* full = bars;                    // leader: both CTAs' A/B loads of a stage
+  uint64_t* empty = bars + S::STAGES;       // each CTA: stage free again
+  uint64_t* sf_full = bars + 2 * S::STAGES;  // each CTA: its scale loads of a stage
+  uint64_t* acc_full = bars + 3 * S::STAGES;
+  uint64_t* acc_empty = acc_full + 1;       // leader: 16 epilogue warps of the pair
+  uint64_t* sf_ready = acc_empty + 1;       // leader: a scale slot written by the 8 loader warps
+  uint64_t* sf_free = sf_ready + S::SF_SLOTS;  // each CTA: the MMAs reading a scale slot are done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + S::SF_SLOTS);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
@@ -403,12 +413,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
     for (int s = 0; s < S::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&sf_full[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * S::EPI_WARPS);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sf_ready[b], 1);
-      mbar_init(&sf_free[b], 1);
+    for (int s = 0; s < S::SF_SLOTS; ++s) {
+      mbar_init(&sf_ready[s], 2 * S::SF_WARPS);
+      mbar_init(&sf_free[s], 1);
     }
     fence_barrier_init();
   }
@@ -459,17 +470,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
             break;
           }
           const uint32_t fb = full_leader + stage * 8;
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (S::A_BYTES + S::B_BYTES));
+          mbar_arrive_expect_tx(&sf_full[stage], S::SFA_BYTES + S::SFB_BYTES);
           tma_load_2d_pair(sA + stage * S::A_BYTES, &p.tmap_a, fb, kt * S::BK_BYTES, a_row);
           tma_load_2d_pair(sB + stage * S::B_BYTES, &p.tmap_b, fb, kt * S::BK_BYTES, b_row);
+          // the scales go to this CTA's loader warps (its own barrier)
           if constexpr (REP) {
             // [k-block][4 copies][512 B] for A; [k-block][row-tile][4 copies][512 B] for B
-            tma_load_2d_pair(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, fb, 0, sfa_row + kt * 32);
-            tma_load_2d_pair(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, fb, 0, sfb_row0 + kt * 64);
+            tma_load_2d(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, &sf_full[stage], 0, sfa_row + kt * 32);
+            tma_load_2d(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, &sf_full[stage], 0, sfb_row0 + kt * 64);
           } else {
-            tma_load_2d_pair(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, fb, 0, sfa_row + kt * 8);
-            tma_load_2d_pair(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, fb, 0, sfb_row0 + kt * 8);
-            tma_load_2d_pair(sSFB + stage * S::SFB_BYTES + 2048, &p.tmap_sfb, fb, 0, sfb_row1 + kt * 8);
+            // [k-block][512 B] for A; [row-tile][k-block][512 B] for B
+            tma_load_2d(sSFA + stage * S::SFA_BYTES, &p.tmap_sfa, &sf_full[stage], 0, sfa_row + kt * 8);
+            tma_load_2d(sSFB + stage * S::SFB_BYTES, &p.tmap_sfb, &sf_full[stage], 0, sfb_row0 + kt * 8);
+            tma_load_2d(sSFB + stage * S::SFB_BYTES + 2048, &p.tmap_sfb, &sf_full[stage], 0, sfb_row1 + kt * 8);
           }
           if (++stage == S::STAGES) {
             stage = 0;
@@ -481,22 +495,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (leader) ----------------
+      // Waits only on mbarriers that TMA and the loader warps' plain arrivals
+      // complete (none on a tcgen05 operation issued by another thread, which
+      // would queue behind the MMAs already issued and drain the pipe).
       constexpr uint32_t idesc = idesc_nvf4(256, S::BN);
-      uint32_t stage = 0, phase = 0, it = 0, g = 0;  // g: k-tiles consumed (scale slot g % 2)
+      uint32_t stage = 0, phase = 0, it = 0, slot = 0, slot_phase = 0;
       bool ok = true;
       for (int u = cluster; u < total && ok; u += nclusters, ++it) {
         if (!mbar_wait(acc_empty, (it & 1u) ^ 1u, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + ((it & 1u) ? S::ACC_ALT_COL : 0u);
-        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
-          const uint32_t slot = g & 1u;
+        for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&full[stage], phase, kErrTimeoutMma) ||
-              !mbar_wait(&sf_ready[slot], (g >> 1) & 1u, kErrTimeoutMma)) {
+              !mbar_wait(&sf_ready[slot], slot_phase, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int kb_n = min(4, kb_total - kt * 4);
+          const int kb_n = min(4, kb_total - kt * 4);  // 2 or 4 (K % 128 == 0)
           const uint32_t a_base = smem_u32(sA + stage * S::A_BYTES);
           const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
           const uint32_t sfa_t = tmem + S::SF_COL + S::SF_SLOT_COLS * slot, sfb_t = sfa_t + 16;
@@ -505,8 +521,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
             const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
             tc_mma_nvf4_pair(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * 8, (kt | kb) != 0 ? 1u : 0u);
           }
-          tc_commit_pair(&sf_free[slot], 0x1);
+          tc_commit_pair(&sf_free[slot], 0x3);
           tc_commit_pair(&empty[stage], 0x3);
+          if (++slot == S::SF_SLOTS) {
+            slot = 0;
+            slot_phase ^= 1u;
+          }
           if (++stage == S::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -516,46 +536,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
         tc_commit_pair(acc_full, 0x3);
       }
     }
-  } else if (warp == S::COPY_WARP) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- scale copier (leader) ----------------
-      // The A and B scales of one k-tile, shared memory -> tensor memory of
-      // both CTAs, into the slot the MMAs are not reading.
-      uint32_t stage = 0, phase = 0, g = 0;
-      bool ok = true;
-      for (int u = cluster; u < total && ok; u += nclusters) {
-        for (int kt = 0; kt < k_tiles; ++kt, ++g) {
-          const uint32_t slot = g & 1u;
-          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma) ||
-              !mbar_wait(&sf_free[slot], ((g >> 1) & 1u) ^ 1u, kErrTimeoutMma)) {
-            ok = false;
-            break;
+  } else if (warp >= S::SF_WARP0) {
+    // ---------------- scale loaders (warps 10..13, both CTAs) ----------------
+    // Each warp writes its lane quadrant of the next scale slot of its CTA's
+    // tensor memory from the stage's scale bytes in shared memory: lane l
+    // takes the 16 bytes at l * 16 of every 512-byte atom (scales of rows l,
+    // l + 32, l + 64, l + 96), the layout tcgen05.cp 32x128b.warpx4 writes,
+    // with one tcgen05.st of 16 columns (A: 4 k-blocks x 4) and one of 32
+    // (B: 4 k-blocks x 2 row-tiles x 4). tcgen05.st runs beside the MMAs,
+    // where tcgen05.cp would queue behind them.
+    const uint32_t lane_base = ((uint32_t)(warp & 3) * 32u) << 16;
+    const uint32_t sf_ready_leader = mapa_shared(smem_u32(sf_ready), 0);
+    uint32_t stage = 0, phase = 0, slot = 0, slot_phase = 0;
+    bool ok = true;
+    for (int u = cluster; u < total && ok; u += nclusters) {
+      for (int kt = 0; kt < k_tiles; ++kt) {
+        if (!mbar_wait(&sf_full[stage], phase, kErrTimeoutProducer) ||
+            !mbar_wait(&sf_free[slot], slot_phase ^ 1u, kErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* sa = sSFA + stage * S::SFA_BYTES + lane * 16;
+        const uint8_t* sb = sSFB + stage * S::SFB_BYTES + lane * 16;
+        uint32_t ra[16], rb[32];
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          const uint4 v = *reinterpret_cast<const uint4*>(sa + kb * 512 * S::SF_COPIES);
+          ra[4 * kb] = v.x;
+          ra[4 * kb + 1] = v.y;
+          ra[4 * kb + 2] = v.z;
+          ra[4 * kb + 3] = v.w;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const uint4 w = *reinterpret_cast<const uint4*>(sb + (REP ? kb * 4096 + t * 2048 : t * 2048 + kb * 512));
+            rb[8 * kb + 4 * t] = w.x;
+            rb[8 * kb + 4 * t + 1] = w.y;
+            rb[8 * kb + 4 * t + 2] = w.z;
+            rb[8 * kb + 4 * t + 3] = w.w;
           }
-          tc_fence_after();
-          const int kb_n = min(4, kb_total - kt * 4);
-          const uint32_t sfa_s = smem_u32(sSFA + stage * S::SFA_BYTES);
-          const uint32_t sfb_s = smem_u32(sSFB + stage * S::SFB_BYTES);
-          const uint32_t sfa_t = tmem + S::SF_COL + S::SF_SLOT_COLS * slot, sfb_t = sfa_t + 16;
-          if constexpr (REP) {
-            // 128 lanes x 32 bytes per copy: lane l reads line l of two
-            // replicated atoms (the two 16-byte halves are 2 KB apart).
-            for (int j = 0; j < (kb_n + 1) / 2; ++j)
-              tc_cp_128x256b_pair(sfa_t + 8 * j, smem_desc(sfa_s + j * 4096, 2048, 128, kLayoutSwizzleNone));
-            for (int kb = 0; kb < kb_n; ++kb)
-              tc_cp_128x256b_pair(sfb_t + 8 * kb, smem_desc(sfb_s + kb * 4096, 2048, 128, kLayoutSwizzleNone));
-          } else {
-            for (int kb = 0; kb < kb_n; ++kb) {
-              tc_cp_32x128b_warpx4_pair(sfa_t + kb * 4, smem_desc(sfa_s + kb * 512, 0, 128, kLayoutSwizzleNone));
-              tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8, smem_desc(sfb_s + kb * 512, 0, 128, kLayoutSwizzleNone));
-              tc_cp_32x128b_warpx4_pair(sfb_t + kb * 8 + 4,
-                                        smem_desc(sfb_s + 2048 + kb * 512, 0, 128, kLayoutSwizzleNone));
-            }
-          }
-          tc_commit_pair(&sf_ready[slot], 0x1);
-          if (++stage == S::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        }
+        const uint32_t sfa_t = tmem + lane_base + S::SF_COL + S::SF_SLOT_COLS * slot;
+        tc_st_32x32b_x16(sfa_t, ra);
+        tc_st_32x32b_x32(sfa_t + 16, rb);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(&sf_ready[slot]);
+          else mbar_arrive_cluster(sf_ready_leader + slot * 8);
+        }
+        if (++slot == S::SF_SLOTS) {
+          slot = 0;
+          slot_phase ^= 1u;
+        }
+        if (++stage == S::STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
     }

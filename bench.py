@@ -415,7 +415,8 @@ def gpu_parity(pkg, L, x, cfg):
     r = ops.dispatch(top, gate, e, amax, full=False)
     aq, asf = ops.quantize_gather(x, r, r.act_global)
     hamax = torch.zeros(e, dtype=torch.int32, device=x.device)
-    hidden = ops.grouped_gemm(aq, ops.replicate_scales(asf, 128), kw.gate_up_q, kw.gate_up_sf, r,
+    a_sf = ops.replicate_scales(asf, 128) if kw.gate_up_sf_layout == capi.SF_REPLICATED else asf
+    hidden = ops.grouped_gemm(aq, a_sf, kw.gate_up_q, kw.gate_up_sf, r,
                               epilogue=capi.EPI_SWIGLU, act_global=r.act_global, w_global=bank.gate_up_global,
                               amax_out=hamax, sf_layout=kw.gate_up_sf_layout)
     hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
@@ -512,8 +513,9 @@ def run_b200(args, cfg):
         "expert_rows": {"max": int(counts.max()), "min": int(counts.min()), "top_expert_token_share": float(
             counts.max()) / t},
         "clocks": clk.summary(),
-        # router 2, dispatch 3, quantize 1 + scale replication 1, GEMM 2, hidden quantize 1, combine 1
-        "gpu_launches": 11 * args.steps,
+        # router 2, dispatch 3, quantize 1 (+ scale replication 1 for replicated weight scales), GEMM 2,
+        # hidden quantize 1, combine 1
+        "gpu_launches": (10 + int(L["kw"].gate_up_sf_layout == pkg.capi.SF_REPLICATED)) * args.steps,
         "e2e": e2e,
         "parity": parity,
         **extra,
@@ -754,8 +756,10 @@ def run_expert_parallel(args, cfg):
         "roofline": roofline,
         "clocks": clk.summary() if clk is not None else None,
         # router 2, row max 1, dispatch 3, quantize 1, and per expert-forward call (one per source rank):
-        # tiles 1, scale replication 1, GEMM 2, hidden quantize 1; combine 1 (NCCL's own kernels not counted)
-        "gpu_launches": (8 + 5 * world) * args.steps,
+        # tiles 1, GEMM 2, hidden quantize 1 (+ scale replication 1 for replicated weight scales); combine 1
+        # (NCCL's own kernels not counted)
+        "gpu_launches": (8 + (4 + int(bank.kernel_weights().gate_up_sf_layout == pkg.capi.SF_REPLICATED)) * world)
+                        * args.steps,
         "e2e": e2e,
     }
     if rank == 0:

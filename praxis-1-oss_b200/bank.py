@@ -35,9 +35,9 @@ class KernelWeights(NamedTuple):
     """Device copies in the kernels' layouts (built by ``prepare()``)."""
 
     gate_up_q: Tensor       # rows interleaved in 64-row blocks (32 gate, 32 up)
-    gate_up_sf: Tensor      # same row order, replicated scale layout
+    gate_up_sf: Tensor      # same row order, compact (reference) scale layout
     down_sf: Tensor         # the bank's own compact scales of down_q
-    gate_up_sf_layout: int  # capi.SF_REPLICATED
+    gate_up_sf_layout: int  # capi.SF_COMPACT
     down_sf_layout: int     # capi.SF_COMPACT
 
 
@@ -151,15 +151,14 @@ class B200NVFP4RoutedExperts(nn.Module):
 
     def prepare(self) -> None:
         """Build the kernel-layout gate/up weights on the buffers' device:
-        rows interleaved for the fused SwiGLU epilogue, scales in the GEMM's
-        replicated layout (the gate/up GEMM is faster with them; the down GEMM
-        reads the bank's compact scales directly). The packed buffers stay in
-        the reference's layout."""
+        rows interleaved for the fused SwiGLU epilogue (their scales follow
+        the rows, still in the reference's compact layout; the down GEMM reads
+        the bank's own buffers). The packed buffers stay in the reference's
+        row order."""
         if self.gate_up_q.device.type != "cuda":
             raise RuntimeError("prepare() needs the bank on a CUDA device")
         gu_q, gu_sf = ops.interleave_gate_up(self.gate_up_q, self.gate_up_sf)
-        gu_sf = ops.replicate_scales(gu_sf, 256)
-        self._kernel = KernelWeights(gu_q, gu_sf, self.down_sf, capi.SF_REPLICATED, capi.SF_COMPACT)
+        self._kernel = KernelWeights(gu_q, gu_sf, self.down_sf, capi.SF_COMPACT, capi.SF_COMPACT)
 
     def kernel_weights(self) -> KernelWeights:
         """The kernel-layout weights (prepare() on first use)."""

@@ -495,19 +495,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (leader) ----------------
-      // Waits only on mbarriers that TMA and the loader warps' plain arrivals
-      // complete (none on a tcgen05 operation issued by another thread, which
-      // would queue behind the MMAs already issued and drain the pipe).
+      // One wait per k-tile: the leader's loader warps signal a scale slot
+      // only once the stage's A/B tiles of both CTAs have landed too. An
+      // mbarrier wait in this thread stalls the MMA issue while it is
+      // outstanding (the tensor pipe's queue holds few instructions), so it
+      // waits as seldom as it can, and never on a tcgen05 operation of
+      // another thread (which would queue behind the MMAs already issued).
       constexpr uint32_t idesc = idesc_nvf4(256, S::BN);
-      uint32_t stage = 0, phase = 0, it = 0, slot = 0, slot_phase = 0;
+      uint32_t stage = 0, it = 0, slot = 0, slot_phase = 0;
       bool ok = true;
       for (int u = cluster; u < total && ok; u += nclusters, ++it) {
         if (!mbar_wait(acc_empty, (it & 1u) ^ 1u, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + ((it & 1u) ? S::ACC_ALT_COL : 0u);
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, kErrTimeoutMma) ||
-              !mbar_wait(&sf_ready[slot], slot_phase, kErrTimeoutMma)) {
+          if (!mbar_wait(&sf_ready[slot], slot_phase, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -527,10 +529,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
             slot = 0;
             slot_phase ^= 1u;
           }
-          if (++stage == S::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (++stage == S::STAGES) stage = 0;
         }
         if (!ok) break;
         tc_commit_pair(acc_full, 0x3);
@@ -551,7 +550,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
     bool ok = true;
     for (int u = cluster; u < total && ok; u += nclusters) {
       for (int kt = 0; kt < k_tiles; ++kt) {
+        // (the leader's loaders also wait for the stage's A/B tiles, so that
+        // a complete scale slot implies a complete stage for the MMA issuer)
         if (!mbar_wait(&sf_full[stage], phase, kErrTimeoutProducer) ||
+            (rank == 0 && !mbar_wait(&full[stage], phase, kErrTimeoutProducer)) ||
             !mbar_wait(&sf_free[slot], slot_phase ^ 1u, kErrTimeoutProducer)) {
           ok = false;
           break;

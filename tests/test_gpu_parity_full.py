@@ -129,7 +129,8 @@ def layer(request):
     r = ops.dispatch(top, gate, e, amax)
     aq, asf = ops.quantize_gather(xd, r, r.act_global)
     hamax = torch.zeros(e, dtype=torch.int32, device=DEV)
-    hidden = ops.grouped_gemm(aq, ops.replicate_scales(asf, 128), kw.gate_up_q, kw.gate_up_sf, r,
+    a_sf = ops.replicate_scales(asf, 128) if kw.gate_up_sf_layout == capi.SF_REPLICATED else asf
+    hidden = ops.grouped_gemm(aq, a_sf, kw.gate_up_q, kw.gate_up_sf, r,
                               epilogue=capi.EPI_SWIGLU, act_global=r.act_global, w_global=bank.gate_up_global,
                               amax_out=hamax, sf_layout=kw.gate_up_sf_layout)
     hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)

@@ -338,18 +338,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Named (hardware) barriers between warps of one CTA: `named_sync` blocks the
+// warp until `threads` threads (whole warps) have arrived at barrier `id`
+// (1..15; 0 is __syncthreads); `named_arrive` counts the warp without
+// waiting. Unlike an mbarrier wait, a named-barrier wait does not stall the
+// MMA issue of the thread that runs it. They have no time limit: every user
+// here runs the same number of arrivals and syncs on every path, errors
+// included (all other waits of the kernels are bounded).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // Wait for the phase with the given parity to complete. Bounded: gives up
-// after `limit_ns` of wall time (or when another thread already raised an
-// error), records `code` and returns false.
+// after `limit_ns` of wall time (or, with `stop_on_error`, as soon as another
+// thread raised an error), records `code` and returns false. Waits that keep
+// a lock-step protocol going after an error (a phase that is completed on
+// every path) pass stop_on_error = false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code,
-                                          uint64_t limit_ns = 2000000000ull) {
+                                          uint64_t limit_ns = 2000000000ull, bool stop_on_error = true) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t start = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0u) {
-      if (error_raised()) return false;
+      if (stop_on_error && error_raised()) return false;
       if (globaltimer_ns() - start > limit_ns) {
         record_error(code);
         return false;

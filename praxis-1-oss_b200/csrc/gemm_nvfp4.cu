@@ -332,6 +332,11 @@ __global__ void __launch_bounds__(192, 1) gemm_nvfp4_kernel(const __grid_constan
 //               config 2). The rescale epilogue (256 columns) keeps the
 //               staged TMA stores, which write full lines.
 // ---------------------------------------------------------------------------
+// Named barriers of the scale slots (ids 1, 2): the leader's MMA warp and
+// its four scale-loader warps.
+constexpr uint32_t kSfBarrier0 = 1;
+constexpr uint32_t kSfBarrierThreads = 32 * 5;
+
 template <bool REP, bool DIRECT>
 struct PairShape {
   static constexpr int BN = 256;
@@ -401,7 +406,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
   uint64_t* sf_full = bars + 2 * S::STAGES;  // each CTA: its scale loads of a stage
   uint64_t* acc_full = bars + 3 * S::STAGES;
   uint64_t* acc_empty = acc_full + 1;       // leader: 16 epilogue warps of the pair
-  uint64_t* sf_ready = acc_empty + 1;       // leader: a scale slot written by the 8 loader warps
+  uint64_t* sf_ready = acc_empty + 1;       // leader: the peer's 4 loader warps wrote a scale slot
   uint64_t* sf_free = sf_ready + S::SF_SLOTS;  // each CTA: the MMAs reading a scale slot are done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + S::SF_SLOTS);
 
@@ -418,7 +423,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * S::EPI_WARPS);
     for (int s = 0; s < S::SF_SLOTS; ++s) {
-      mbar_init(&sf_ready[s], 2 * S::SF_WARPS);
+      mbar_init(&sf_ready[s], S::SF_WARPS);
       mbar_init(&sf_free[s], 1);
     }
     fence_barrier_init();
@@ -493,46 +498,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer (leader) ----------------
-      // One wait per k-tile: the leader's loader warps signal a scale slot
-      // only once the stage's A/B tiles of both CTAs have landed too. An
-      // mbarrier wait in this thread stalls the MMA issue while it is
-      // outstanding (the tensor pipe's queue holds few instructions), so it
-      // waits as seldom as it can, and never on a tcgen05 operation of
-      // another thread (which would queue behind the MMAs already issued).
+    if (rank == 0) {
+      // ---------------- MMA issuer (leader; the whole warp, lane 0 issues) ----------------
+      // Per k-tile the warp meets the leader's four loader warps at the named
+      // barrier of the scale slot: they arrive once both CTAs' scales are in
+      // tensor memory and the stage's A/B tiles of both CTAs have landed. An
+      // mbarrier wait here stalls the MMA issue for hundreds of cycles (the
+      // tensor pipe ran at half rate with one per k-tile); a named barrier
+      // does not. The warp never waits on a tcgen05 operation of another
+      // thread either (it would queue behind the MMAs already issued). After
+      // an error the loop keeps meeting the loaders at every k-tile and keeps
+      // committing (with no MMAs), so every barrier keeps its phases and no
+      // warp waits for a signal that never comes.
       constexpr uint32_t idesc = idesc_nvf4(256, S::BN);
-      uint32_t stage = 0, it = 0, slot = 0, slot_phase = 0;
+      uint32_t stage = 0, it = 0, slot = 0;
       bool ok = true;
-      for (int u = cluster; u < total && ok; u += nclusters, ++it) {
-        if (!mbar_wait(acc_empty, (it & 1u) ^ 1u, kErrTimeoutMma)) break;
+      for (int u = cluster; u < total; u += nclusters, ++it) {
+        ok = ok && mbar_wait(acc_empty, (it & 1u) ^ 1u, kErrTimeoutMma);
         tc_fence_after();
         const uint32_t d_tmem = tmem + ((it & 1u) ? S::ACC_ALT_COL : 0u);
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&sf_ready[slot], slot_phase, kErrTimeoutMma)) {
-            ok = false;
-            break;
-          }
+          named_sync(kSfBarrier0 + slot, kSfBarrierThreads);
           tc_fence_after();
-          const int kb_n = min(4, kb_total - kt * 4);  // 2 or 4 (K % 128 == 0)
-          const uint32_t a_base = smem_u32(sA + stage * S::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
-          const uint32_t sfa_t = tmem + S::SF_COL + S::SF_SLOT_COLS * slot, sfb_t = sfa_t + 16;
-          for (int kb = 0; kb < kb_n; ++kb) {
-            const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
-            const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
-            tc_mma_nvf4_pair(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * 8, (kt | kb) != 0 ? 1u : 0u);
+          if (lane == 0) {
+            if (ok) {
+              const int kb_n = min(4, kb_total - kt * 4);  // 2 or 4 (K % 128 == 0)
+              const uint32_t a_base = smem_u32(sA + stage * S::A_BYTES);
+              const uint32_t b_base = smem_u32(sB + stage * S::B_BYTES);
+              const uint32_t sfa_t = tmem + S::SF_COL + S::SF_SLOT_COLS * slot, sfb_t = sfa_t + 16;
+              for (int kb = 0; kb < kb_n; ++kb) {
+                const uint64_t ad = smem_desc(a_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+                const uint64_t bd = smem_desc(b_base + kb * 32, 16, 1024, kLayoutSwizzle128B);
+                tc_mma_nvf4_pair(d_tmem, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * 8, (kt | kb) != 0 ? 1u : 0u);
+              }
+            }
+            tc_commit_pair(&sf_free[slot], 0x3);
+            tc_commit_pair(&empty[stage], 0x3);
           }
-          tc_commit_pair(&sf_free[slot], 0x3);
-          tc_commit_pair(&empty[stage], 0x3);
-          if (++slot == S::SF_SLOTS) {
-            slot = 0;
-            slot_phase ^= 1u;
-          }
+          __syncwarp();
+          if (++slot == S::SF_SLOTS) slot = 0;
           if (++stage == S::STAGES) stage = 0;
         }
-        if (!ok) break;
-        tc_commit_pair(acc_full, 0x3);
+        if (lane == 0) tc_commit_pair(acc_full, 0x3);
+        __syncwarp();
       }
     }
   } else if (warp >= S::SF_WARP0) {
@@ -548,45 +556,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
     const uint32_t sf_ready_leader = mapa_shared(smem_u32(sf_ready), 0);
     uint32_t stage = 0, phase = 0, slot = 0, slot_phase = 0;
     bool ok = true;
-    for (int u = cluster; u < total && ok; u += nclusters) {
+    for (int u = cluster; u < total; u += nclusters) {
       for (int kt = 0; kt < k_tiles; ++kt) {
-        // (the leader's loaders also wait for the stage's A/B tiles, so that
-        // a complete scale slot implies a complete stage for the MMA issuer)
-        if (!mbar_wait(&sf_full[stage], phase, kErrTimeoutProducer) ||
-            (rank == 0 && !mbar_wait(&full[stage], phase, kErrTimeoutProducer)) ||
-            !mbar_wait(&sf_free[slot], slot_phase ^ 1u, kErrTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint8_t* sa = sSFA + stage * S::SFA_BYTES + lane * 16;
-        const uint8_t* sb = sSFB + stage * S::SFB_BYTES + lane * 16;
-        uint32_t ra[16], rb[32];
+        // The leader's loaders also wait for the stage's A/B tiles, so the
+        // MMA warp needs no other signal. The sf_free wait runs on every path:
+        // the MMA warp commits every slot, errors included, and the wait keeps
+        // the loaders from running more than two k-tiles ahead of the named
+        // barriers.
+        ok = ok && mbar_wait(&sf_full[stage], phase, kErrTimeoutProducer) &&
+             (rank != 0 || mbar_wait(&full[stage], phase, kErrTimeoutProducer));
+        ok = mbar_wait(&sf_free[slot], slot_phase ^ 1u, kErrTimeoutProducer, 2000000000ull, false) && ok;
+        if (ok) {
+          tc_fence_after();
+          const uint8_t* sa = sSFA + stage * S::SFA_BYTES + lane * 16;
+          const uint8_t* sb = sSFB + stage * S::SFB_BYTES + lane * 16;
+          uint32_t ra[16], rb[32];
 #pragma unroll
-        for (int kb = 0; kb < 4; ++kb) {
-          const uint4 v = *reinterpret_cast<const uint4*>(sa + kb * 512 * S::SF_COPIES);
-          ra[4 * kb] = v.x;
-          ra[4 * kb + 1] = v.y;
-          ra[4 * kb + 2] = v.z;
-          ra[4 * kb + 3] = v.w;
+          for (int kb = 0; kb < 4; ++kb) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sa + kb * 512 * S::SF_COPIES);
+            ra[4 * kb] = v.x;
+            ra[4 * kb + 1] = v.y;
+            ra[4 * kb + 2] = v.z;
+            ra[4 * kb + 3] = v.w;
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const uint4 w = *reinterpret_cast<const uint4*>(sb + (REP ? kb * 4096 + t * 2048 : t * 2048 + kb * 512));
-            rb[8 * kb + 4 * t] = w.x;
-            rb[8 * kb + 4 * t + 1] = w.y;
-            rb[8 * kb + 4 * t + 2] = w.z;
-            rb[8 * kb + 4 * t + 3] = w.w;
+            for (int t = 0; t < 2; ++t) {
+              const uint4 w = *reinterpret_cast<const uint4*>(sb + (REP ? kb * 4096 + t * 2048 : t * 2048 + kb * 512));
+              rb[8 * kb + 4 * t] = w.x;
+              rb[8 * kb + 4 * t + 1] = w.y;
+              rb[8 * kb + 4 * t + 2] = w.z;
+              rb[8 * kb + 4 * t + 3] = w.w;
+            }
           }
+          const uint32_t sfa_t = tmem + lane_base + S::SF_COL + S::SF_SLOT_COLS * slot;
+          tc_st_32x32b_x16(sfa_t, ra);
+          tc_st_32x32b_x32(sfa_t + 16, rb);
+          tc_wait_st();
         }
-        const uint32_t sfa_t = tmem + lane_base + S::SF_COL + S::SF_SLOT_COLS * slot;
-        tc_st_32x32b_x16(sfa_t, ra);
-        tc_st_32x32b_x32(sfa_t + 16, rb);
-        tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          if (rank == 0) mbar_arrive(&sf_ready[slot]);
-          else mbar_arrive_cluster(sf_ready_leader + slot * 8);
+        if (rank == 0) {
+          // the peer's loaders are done with the slot too, then the MMA warp may go
+          ok = mbar_wait(&sf_ready[slot], slot_phase, kErrTimeoutProducer, 2000000000ull, false) && ok;
+          named_arrive(kSfBarrier0 + slot, kSfBarrierThreads);
+        } else if (lane == 0) {
+          mbar_arrive_cluster(sf_ready_leader + slot * 8);
         }
         if (++slot == S::SF_SLOTS) {
           slot = 0;

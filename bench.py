@@ -107,6 +107,9 @@ def parse():
                     help="expert-parallel row exchange (N > 1): copy engines into IPC-mapped peer buffers, or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the extra config keys of the default line")
+    ap.add_argument("--flashinfer", action="store_true",
+                    help="also time FlashInfer's block-scaled grouped GEMM (the kernel the reference calls) on the "
+                         "same operands (N = 1)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override the config's token count (small profiling cases)")
     return ap.parse_args()
@@ -500,6 +503,8 @@ def run_b200(args, cfg):
     extra = {}
     if args.config == "2" and not args.no_extra:
         extra = extra_configs(pkg, L, args, dev)
+    if args.flashinfer:
+        extra["flashinfer_gemm"] = flashinfer_gemm(pkg, L, x, cfg, stages)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
@@ -531,6 +536,75 @@ def run_b200(args, cfg):
                         parity.get("gate_max_bf16_ulp_vs_oracle", 0) <= 1 and
                         parity.get("out_rel_l2_vs_port", 0.0) <= 1e-2)
     print(json.dumps(line), flush=True)
+
+
+def flashinfer_gemm(pkg, L, x, cfg, stages):
+    """FlashInfer's block-scaled contiguous grouped GEMM, the kernel the
+    reference's grouped_nvfp4_mm calls on SM100 (praxis/kernels/nvfp4.py:
+    355-419), timed on this layer's own FP4 operands with the reference's
+    call: 128-row tiles, cluster 1x1, the tile table of the padded CSR, unit
+    alpha, and the identity row mapping with unit scales (the reference pins
+    flashinfer 0.6.18, whose use_fused_finalize=False returns the plain GEMM;
+    the installed version always finalizes, here with atomic adds into a
+    zeroed output). Against this library's gate/up (SwiGLU fused) and down
+    (rescale fused) GEMMs; the reference runs its SwiGLU and rescale as
+    separate passes."""
+    import torch
+
+    try:
+        import flashinfer
+        from flashinfer.fused_moe.cute_dsl.blockscaled_contiguous_grouped_gemm_finalize_fusion import (
+            blockscaled_contiguous_grouped_gemm_finalize_fusion_nvfp4 as fi,
+        )
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"flashinfer not importable: {type(exc).__name__}: {exc}"[:200]}
+    ops, capi = pkg.ops, pkg.capi
+    bank, kw = L["bank"], L["kw"]
+    e, k, c, f = cfg["experts"], cfg["top_k"], cfg["dim"], cfg["hidden"]
+    t = x.shape[0]
+    dev = x.device
+    logits, amax = ops.router_logits(x, L["terms"])
+    top, gate = ops.route(logits, L["mod"].expert_bias, k)
+    r = ops.dispatch(top, gate, e, amax, full=False)
+    aq, asf = ops.quantize_gather(x, r, r.act_global)
+    hamax = torch.zeros(e, dtype=torch.int32, device=dev)
+    hidden = ops.grouped_gemm(aq, asf, kw.gate_up_q, kw.gate_up_sf, r, epilogue=capi.EPI_SWIGLU,
+                              act_global=r.act_global, w_global=bank.gate_up_global, amax_out=hamax,
+                              sf_layout=kw.gate_up_sf_layout)
+    hq, hsf = ops.quantize_rows(hidden, r, amax_bits=hamax)
+    rp = aq.shape[0]
+    tiles = rp // 128
+    pc = r.pcsr.long()
+    expert = torch.bucketize(torch.arange(tiles, device=dev) * 128, pc[1:], right=True).clamp_max(e - 1)
+    limit = pc[1:][expert].to(torch.int32)
+    expert = expert.to(torch.int32)
+    # the reference's operand shapes exactly (its 128-row tile table must match the padded layout)
+    assert int(limit.max()) <= rp and tuple(asf.shape) == (rp, c // 16) and tuple(hsf.shape) == (rp, f // 16)
+    ntiles = torch.tensor([tiles], dtype=torch.int32, device=dev)
+    ident = torch.arange(rp, dtype=torch.int32, device=dev)
+    ones = torch.ones(rp, 1, dtype=torch.float32, device=dev)
+    alpha = torch.ones(e, dtype=torch.float32, device=dev)
+    res = {"version": getattr(flashinfer, "__version__", "?"), "tile": [128, 128], "cluster": [1, 1]}
+    flops = {"gate_up": 2.0 * t * k * c * 2 * f, "down": 2.0 * t * k * f * c}
+    for name, a_, as_, b_, bs_, n_ in (("gate_up", aq, asf, bank.gate_up_q, bank.gate_up_sf, 2 * f),
+                                       ("down", hq, hsf, bank.down_q, bank.down_sf, c)):
+        out = torch.zeros(rp, n_, dtype=torch.bfloat16, device=dev)
+
+        def call():
+            fi(a_, b_, as_, bs_, alpha, expert, ntiles, limit, ident, ones, out, mma_tiler_mn=(128, 128),
+               cluster_shape_mn=(1, 1), enable_pdl=False)
+
+        try:
+            for _ in range(3):
+                call()
+            ms = time_steps(call, dev, 20, 0)
+        except Exception as exc:  # noqa: BLE001
+            res[name] = {"failed": f"{type(exc).__name__}: {exc}"[:200]}
+            continue
+        ours = stages["gemm1_swiglu" if name == "gate_up" else "gemm2_rescale"]
+        res[name] = {"flashinfer_ms": ms, "flashinfer_tflops": flops[name] / (ms / 1e3) / 1e12, "b200_ms": ours,
+                     "speedup": ms / ours}
+    return res
 
 
 def cpu_leg_with_parity(L, cfg, gpu_res):

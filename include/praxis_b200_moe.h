@@ -199,6 +199,47 @@ int praxis_b200_combine(const void* rows, int32_t cols, const int64_t* inverse, 
                         const void* shared, void* out, int64_t tokens, int32_t top_k, int32_t experts, int device,
                         void* stream);
 
+/* The MoE tail fused into what follows it (praxis.layers.MOE_TAIL_NORM):
+ * the combine of praxis_b200_combine (its arithmetic, shared add included)
+ * gives y, never stored; then, per token,
+ *   x  = bf16(f32(residual) + f32(y))                  (the residual add)
+ *   with mod: x = bf16(fma(f32(x), bf16(f32(scl) + 1), f32(shf)))
+ *             (mod_fma == 0: the product rounded before the add)
+ *   residual_out = x
+ *   with norm_weight: normed_out = bf16(bf16(norm_weight * (r * f32(x))) * norm_scale),
+ *             r = rsqrt(sum(f32(x)^2) / C + eps)
+ * the sum in the order of torch's vectorized RMSNorm kernel (128 threads per
+ * row, float4 vectors, shuffle-down tree, (w0 + w2) + (w1 + w3)), the IEEE
+ * division and the hardware reciprocal square root. norm_weight is fp32 [C]
+ * and already 1 + weight (RMSNorm's zero-centred scale), norm_scale the
+ * block's scalar. mod rows are [R, 2C] bf16, shift then scale; the row of
+ * token t follows praxis/kernels/norm_triton.py:417-431 with
+ * mod_geom = {RF, RC, NREG, PW, WD, PH} ({1, 1, 0, 1, 1, 1}: row t) applied
+ * to t + mod_row0 (the global row of a chunk's first token).
+ * The three forms replace praxis/kernels/moe_tail_triton.py:329-352
+ * (tail_add_norm_scale: norm_weight set, mod NULL), :355-385
+ * (tail_add_mod_norm_scale: both set) and :431-445 (tail_residual_add:
+ * norm_weight NULL, mod NULL), NVFP4 one-chunk mode. */
+typedef struct praxis_b200_tail {
+  const void* residual;      /* [T, C] bf16 */
+  void* residual_out;        /* [T, C] bf16 */
+  const float* norm_weight;  /* [C] fp32, 1 + weight; NULL: residual add only */
+  void* normed_out;          /* [T, C] bf16 (with norm_weight) */
+  float eps;
+  float norm_scale;
+  const void* mod;           /* [R, 2C] bf16 or NULL (needs norm_weight) */
+  int32_t mod_fma;
+  int64_t mod_geom[6];
+  int64_t mod_row0;
+} praxis_b200_tail;
+
+/* C % 4 == 0; bf16 buffers 8-byte aligned, norm_weight 16-byte aligned. */
+int praxis_b200_combine_tail(const void* rows, int32_t cols, const int64_t* inverse, const int64_t* top_idx,
+                             const void* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
+                             const uint32_t* h_amax, const float* w_global, int32_t rows_rescaled, float scaling,
+                             const void* shared, const praxis_b200_tail* tail, int64_t tokens, int32_t top_k,
+                             int32_t experts, int device, void* stream);
+
 /* Packs expert-first bf16 weights w [E, K, N] (RoutedExperts layout: input
  * features first) as W^T per expert: q [E, N, K/2], sf [E, N, K/16]
  * (swizzled), global [E]. scratch: E uint32.
@@ -247,6 +288,9 @@ typedef struct praxis_b200_moe_args {
   size_t workspace_size;
   int device;
   void* stream;
+  /* Optional MoE tail fused into what follows it (praxis_b200_combine_tail):
+   * when set, its outputs replace `out`, which may be NULL. */
+  const praxis_b200_tail* tail;
 } praxis_b200_moe_args;
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,

@@ -563,6 +563,84 @@ def rescale_combine(raw, inverse, top_idx, gate, csr, pcsr, hg, wg, scaling, sha
     return y
 
 
+def rms_sum_of_squares(xo: torch.Tensor) -> torch.Tensor:
+    """Per row, sum of f32(xo)^2 in the order of torch's vectorized RMSNorm
+    kernel that the reference's fused norms reproduce
+    (praxis/kernels/norm_triton.py:11-22, praxis/kernels/moe_tail_triton.py:
+    160-190): 128 threads t = 32 w + l, thread t adds the squares of the four
+    elements of float4 vectors t, t + 128, ... in order; a shuffle-down tree
+    (16, 8, 4, 2, 1) per warp; then (w0 + w2) + (w1 + w3). Missing elements
+    (rows not a multiple of 512 wide) add +0.0."""
+    t, n = xo.shape
+    ni = (n + 511) // 512
+    v = torch.zeros(t, ni * 512, dtype=_F32)
+    v[:, :n] = xo.to(_F32)
+    v = v.reshape(t, ni, 4, 32, 4)
+    acc = torch.zeros(t, 4, 32, dtype=_F32)
+    for i in range(ni):
+        for e in range(4):
+            q = v[:, i, :, :, e]
+            acc = acc + q * q
+    for off in (16, 8, 4, 2, 1):
+        acc = acc[..., :off] + acc[..., off:2 * off]
+    w = acc[..., 0]
+    return (w[:, 0] + w[:, 2]) + (w[:, 1] + w[:, 3])
+
+
+def mod_row_map(rows: int, geom=None) -> torch.Tensor:
+    """The modulation row of token rows 0..rows-1
+    (praxis/kernels/norm_triton.py:417-431): geom = (RF, RC, NREG, PW, WD,
+    PH) of a compact modulation, None for one row per token."""
+    r = torch.arange(rows, dtype=torch.int64)
+    if geom is None:
+        return r
+    rf, rc, nreg, pw, wd, ph = (int(v) for v in geom)
+    b = r // rf
+    t = r - b * rf
+    q = (t - nreg).clamp(min=0) // pw
+    return b * rc + torch.where(t < nreg, t, nreg + ((q // wd) // ph) * wd + q % wd)
+
+
+def tail_residual_add(y: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """``x + y`` in bf16 (praxis/kernels/moe_tail_triton.py:401-428)."""
+    return (x.to(_F32) + y.to(_F32)).to(_BF16)
+
+
+def tail_modulate(xo: torch.Tensor, mod: torch.Tensor, mrow: torch.Tensor) -> torch.Tensor:
+    """The modulation of praxis/kernels/moe_tail_triton.py:257-266 on the
+    new residual: bf16(xo * bf16(scale + 1) + shift), mod rows [R, 2C] =
+    (shift | scale). With bf16 operands the product is exact in fp32, so the
+    fused and the unfused forms round alike."""
+    n = xo.shape[1]
+    m = mod[mrow].to(_F32)
+    sh, sc = m[:, :n], m[:, n:]
+    sc1 = (sc + f32(1.0)).to(_BF16).to(_F32)
+    return (xo.to(_F32) * sc1 + sh).to(_BF16)
+
+
+def tail_add_norm_scale(y: torch.Tensor, x: torch.Tensor, w1: torch.Tensor, eps: float, s: float,
+                        mod: torch.Tensor | None = None, geom=None, row0: int = 0):
+    """The MoE tail fused into the next block's residual add + RMSNorm
+    (praxis/kernels/moe_tail_triton.py:108-190, the ``add_norm_scale``
+    contract of praxis/kernels/norm_triton.py:1-32): xo = bf16(x + y);
+    with ``mod`` the modulation of :func:`tail_modulate` (rows mapped by
+    :func:`mod_row_map` from token row + ``row0``, moe_tail_triton.py:
+    196-307); r = rsqrt(ss / N + eps) (IEEE division; here the correctly
+    rounded reciprocal square root, where the GPU's hardware estimate may
+    differ by an ulp); h = bf16(bf16(w1 * (r * xo)) * s), w1 = 1 + weight in
+    fp32."""
+    n = x.shape[1]
+    xo = tail_residual_add(y, x)
+    if mod is not None:
+        xo = tail_modulate(xo, mod, mod_row_map(row0 + x.shape[0], geom)[row0:])
+    ss = rms_sum_of_squares(xo)
+    v = ss / f32(float(n)) + f32(float(eps))
+    r = v.to(torch.float64).rsqrt().to(_F32).unsqueeze(1)
+    o = (w1.to(_F32).unsqueeze(0) * (r * xo.to(_F32))).to(_BF16)
+    h = (o.to(_F32) * f32(float(s))).to(_BF16)
+    return xo, h
+
+
 # ---------------------------------------------------------------------------
 # The routed bank forward
 # ---------------------------------------------------------------------------

@@ -20,10 +20,10 @@ from __future__ import annotations
 import sys
 
 from . import build, capi, expert_parallel, ops, pipeline, torch_ops  # noqa: F401
-from .bank import B200NVFP4RoutedExperts, pack_routed_experts  # noqa: F401
+from .bank import B200NVFP4RoutedExperts, pack_routed_experts, routed_forward_tail  # noqa: F401
 from .moe import B200MoEFeedForward  # noqa: F401
 
 sys.modules.setdefault("praxis_b200", sys.modules[__name__])
 
-__all__ = ["B200NVFP4RoutedExperts", "B200MoEFeedForward", "pack_routed_experts", "build", "capi", "ops",
-           "expert_parallel", "pipeline", "torch_ops"]
+__all__ = ["B200NVFP4RoutedExperts", "B200MoEFeedForward", "pack_routed_experts", "routed_forward_tail",
+           "build", "capi", "ops", "expert_parallel", "pipeline", "torch_ops"]

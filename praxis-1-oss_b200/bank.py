@@ -246,6 +246,35 @@ class B200NVFP4RoutedExperts(nn.Module):
         return out
 
 
+def routed_forward_tail(bank: B200NVFP4RoutedExperts, x: Tensor, top_idx: Tensor, gate: Tensor, *,
+                        scaling: float, chunk_size: int, tail: ops.Tail, shared: Tensor | None = None
+                        ) -> tuple[Tensor, Tensor | None]:
+    """``routed_forward_with_shared`` whose output goes straight into what
+    follows the layer (the reference's MOE_TAIL_NORM, praxis/layers.py:429-441,
+    praxis/kernels/moe_tail_triton.py:329-445): the residual add of
+    ``tail.residual``, then, when ``tail.norm_weight`` is set, the next block's
+    RMSNorm (with its modulation when ``tail.mod`` is set). Returns ``(new
+    residual, normed rows or None)`` with the eager bits; the routed output
+    itself is never stored. Each dispatch chunk fuses its own rows."""
+    bank._check(x, top_idx, gate, scaling, chunk_size)
+    r = tail.residual
+    if r.shape != x.shape or r.dtype != torch.bfloat16 or not r.is_contiguous() or r.device != x.device:
+        raise ValueError("Expected a contiguous BF16 residual shaped like the routed activations")
+    if shared is not None and (shared.shape != x.shape or shared.dtype != x.dtype or not shared.is_contiguous()):
+        raise ValueError("Expected a contiguous BF16 shared-expert output shaped like the activations")
+    kw = bank.kernel_weights()
+    residual_out = torch.empty_like(x)
+    normed = None if tail.norm_weight is None else torch.empty_like(x)
+    for start in range(0, x.shape[0], chunk_size):
+        end = min(start + chunk_size, x.shape[0])
+        ops.moe_forward(
+            x[start:end], top_idx[start:end], gate[start:end], kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global,
+            bank.down_q, kw.down_sf, bank.down_global, float(scaling), None if shared is None else shared[start:end],
+            gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout, tail=tail.chunk(start, end),
+            tail_out=(residual_out[start:end], None if normed is None else normed[start:end]))
+    return residual_out, normed
+
+
 def pack_routed_experts(gate_up_weight: Tensor, down_weight: Tensor, *, keep_on_device: bool = False
                         ) -> B200NVFP4RoutedExperts:
     """Packs expert-first bf16 banks [E,C,2H] / [E,H,C] on the GPU with the

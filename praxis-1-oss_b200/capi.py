@@ -59,6 +59,24 @@ class MoeArgs(C.Structure):
         ("workspace_size", SZ),
         ("device", C.c_int),
         ("stream", P),
+        ("tail", P),
+    ]
+
+
+class TailArgs(C.Structure):
+    """``praxis_b200_tail``."""
+
+    _fields_ = [
+        ("residual", P),
+        ("residual_out", P),
+        ("norm_weight", P),
+        ("normed_out", P),
+        ("eps", F32),
+        ("norm_scale", F32),
+        ("mod", P),
+        ("mod_fma", I32),
+        ("mod_geom", I64 * 6),
+        ("mod_row0", I64),
     ]
 
 
@@ -122,6 +140,10 @@ SIGNATURES: dict[str, tuple] = {
     "praxis_b200_combine": (
         C.c_int,
         [P, I32, P, P, P, P, P, P, P, P, I32, F32, P, P, I64, I32, I32, C.c_int, P],
+    ),
+    "praxis_b200_combine_tail": (
+        C.c_int,
+        [P, I32, P, P, P, P, P, P, P, P, I32, F32, P, C.POINTER(TailArgs), I64, I32, I32, C.c_int, P],
     ),
     "praxis_b200_pack_weights": (C.c_int, [P, I32, I32, I32, P, P, P, P, C.c_int, P]),
     "praxis_b200_interleave_gate_up": (C.c_int, [P, P, I32, I32, I32, P, P, C.c_int, P]),

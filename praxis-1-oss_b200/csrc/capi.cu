@@ -44,6 +44,27 @@ int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const in
                 const int32_t* csr, const int32_t* pcsr, const float* h_global, const uint32_t* h_amax,
                 const float* w_global, int rows_rescaled, float scaling, const uint16_t* shared, uint16_t* out,
                 int64_t tokens, int top_k, int experts, cudaStream_t stream);
+int run_combine_tail(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx,
+                     const uint16_t* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
+                     const uint32_t* h_amax, const float* w_global, int rows_rescaled, float scaling,
+                     const uint16_t* shared, const TailArgs& tail, int64_t tokens, int top_k, int experts,
+                     cudaStream_t stream);
+
+// The ABI's tail descriptor as the kernel's arguments.
+static TailArgs tail_args(const praxis_b200_tail& t) {
+  TailArgs a;
+  a.x = static_cast<const uint16_t*>(t.residual);
+  a.x_out = static_cast<uint16_t*>(t.residual_out);
+  a.w1 = t.norm_weight;
+  a.h_out = static_cast<uint16_t*>(t.normed_out);
+  a.eps = t.eps;
+  a.norm_scale = t.norm_scale;
+  a.mod = static_cast<const uint16_t*>(t.mod);
+  a.mod_fma = t.mod_fma;
+  for (int i = 0; i < 6; ++i) a.mod_geom[i] = t.mod_geom[i];
+  a.mod_row0 = t.mod_row0;
+  return a;
+}
 
 static thread_local char g_message[1024] = "";
 
@@ -356,6 +377,22 @@ int praxis_b200_combine(const void* rows, int32_t cols, const int64_t* inverse, 
                      PRAXIS_STREAM(stream));
 }
 
+int praxis_b200_combine_tail(const void* rows, int32_t cols, const int64_t* inverse, const int64_t* top_idx,
+                             const void* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
+                             const uint32_t* h_amax, const float* w_global, int32_t rows_rescaled, float scaling,
+                             const void* shared, const praxis_b200_tail* tail, int64_t tokens, int32_t top_k,
+                             int32_t experts, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (tail == nullptr) return set_error(PRAXIS_B200_EINVAL, "combine_tail: null tail descriptor");
+  if (tokens == 0) return PRAXIS_B200_OK;
+  if (!rows || !inverse || !top_idx || !gate || !csr || !pcsr)
+    return set_error(PRAXIS_B200_EINVAL, "combine_tail: null pointer");
+  return run_combine_tail(static_cast<const uint16_t*>(rows), cols, inverse, top_idx,
+                          static_cast<const uint16_t*>(gate), csr, pcsr, h_global, h_amax, w_global, rows_rescaled,
+                          scaling, static_cast<const uint16_t*>(shared), tail_args(*tail), tokens, top_k, experts,
+                          PRAXIS_STREAM(stream));
+}
+
 int praxis_b200_pack_weights(const void* w, int32_t experts, int32_t k, int32_t n, void* q, void* sf,
                              float* global_out, uint32_t* scratch, int device, void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
@@ -443,7 +480,7 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   if (!a) return set_error(PRAXIS_B200_EINVAL, "moe_forward: null args");
   PRAXIS_DEVICE_OR_RETURN(a->device);
   const bool with_router = a->router_weight != nullptr;
-  if (!a->x || !a->top_idx || !a->gate || !a->out || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
+  if (!a->x || !a->top_idx || !a->gate || (!a->out && !a->tail) || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
       !a->down_q || !a->down_sf || !a->down_global || !a->workspace)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: null pointer");
   const int gl = a->gate_up_sf_layout, dl = a->down_sf_layout;
@@ -526,6 +563,10 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
                         a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, dl, s);
   if (rc) return rc;
+  if (a->tail != nullptr)
+    return run_combine_tail(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
+                            a->scaling, static_cast<const uint16_t*>(a->shared), tail_args(*a->tail), a->tokens,
+                            a->top_k, a->experts, s);
   return run_combine(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
                      a->scaling, static_cast<const uint16_t*>(a->shared), static_cast<uint16_t*>(a->out), a->tokens,
                      a->top_k, a->experts, s);

@@ -123,6 +123,24 @@ inline EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Inputs and outputs of the fused MoE tail (combine_tail_kernel): the
+// residual x and its new value x_out; w1 (1 + norm weight, fp32) and h_out
+// when the RMSNorm follows; mod rows [R, 2C] (shift | scale) with the
+// modulation row map {RF, RC, NREG, PW, WD, PH} of global token rows
+// (token t of this launch is row t + mod_row0).
+struct TailArgs {
+  const uint16_t* x;
+  uint16_t* x_out;
+  const float* w1;
+  uint16_t* h_out;
+  float eps;
+  float norm_scale;
+  const uint16_t* mod;
+  int mod_fma;
+  int64_t mod_geom[6];
+  int64_t mod_row0;
+};
+
 int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, const TileEntry* tiles,
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,

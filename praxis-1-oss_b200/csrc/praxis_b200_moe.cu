@@ -8,5 +8,6 @@
 #include "quantize.cu"
 #include "gemm_nvfp4.cu"
 #include "combine.cu"
+#include "tail.cu"
 #include "swiglu.cu"
 #include "capi.cu"

@@ -18,7 +18,8 @@ import torch.nn.functional as F
 from torch import Tensor, nn
 
 from . import ops
-from .bank import B200NVFP4RoutedExperts, pack_routed_experts
+from .bank import B200NVFP4RoutedExperts, pack_routed_experts, routed_forward_tail
+from .ops import Tail
 
 _NVTX = os.environ.get("PRAXIS_NVTX", "0") not in ("", "0")
 
@@ -174,6 +175,44 @@ class B200MoEFeedForward(nn.Module):
             raise ValueError(f"router_rows {router_rows}: need 0 <= r0 <= r1 <= total")
         if x.dim() < 2 or x.shape[-2] != r1 - r0:
             raise ValueError(f"router_rows {router_rows}: x must hold r1 - r0 = {r1 - r0} rows per sequence")
+
+    @torch.no_grad()
+    def forward_tail(self, x: Tensor, residual: Tensor, norm: nn.Module | None = None, scale=None, *,
+                     mod: Tensor | None = None, modfma: bool = True, geom=None
+                     ) -> tuple[Tensor, Tensor | None]:
+        """``forward(x)`` fused into what follows it in the reference's
+        MOE_TAIL_NORM path (praxis/layers.py:429-441): the residual add
+        ``residual + y`` and, with ``norm`` (the reference's zero-centred
+        RMSNorm: ``weight``, ``eps``) and ``scale``, the next block's
+        ``norm(residual + y) * scale`` — with ``mod`` ([R, 2C] shift | scale
+        rows, ``geom`` the (RF, RC, NREG, PW, WD, PH) of ``CompactMod`` or
+        None) its modulation in between — as ``tail_residual_add``,
+        ``tail_add_norm_scale`` and ``tail_add_mod_norm_scale`` of
+        praxis/kernels/moe_tail_triton.py:329-445 compute them. Returns
+        ``(new residual, normed rows or None)`` with the eager bits; the
+        routed combine, the shared add, the residual add, the modulation and
+        the norm run as the last kernel of the routed forward."""
+        if self.routed is None:
+            raise RuntimeError("routed experts are not set (set_routed_weights / from_reference)")
+        if (norm is None) != (scale is None):
+            raise ValueError("norm and scale go together")
+        shape = x.shape
+        c = x.size(-1)
+        x_flat = x.reshape(-1, c).contiguous()
+        top_idx, gate = self.route(x_flat)
+        y_shared = self.shared(x_flat).contiguous() if self.shared is not None else None
+        tail = Tail(residual=residual.reshape(-1, c).contiguous())
+        if norm is not None:
+            tail = tail._replace(norm_weight=(1 + norm.weight.detach().to(torch.float32)).contiguous(),
+                                 eps=float(norm.eps), norm_scale=float(torch.as_tensor(scale).float()))
+        if mod is not None:
+            tail = tail._replace(mod=mod.reshape(-1, 2 * c).contiguous(), mod_fma=bool(modfma),
+                                 mod_geom=None if geom is None else tuple(int(v) for v in geom))
+        chunk = self.dispatch_chunk_size or max(1, x_flat.shape[0])
+        with _Range("routed"):
+            xo, h = routed_forward_tail(self.routed, x_flat, top_idx, gate, scaling=self.routed_scaling_factor,
+                                        chunk_size=chunk, tail=tail, shared=y_shared)
+        return xo.reshape(shape), None if h is None else h.reshape(shape)
 
     @torch.no_grad()
     def forward(self, x: Tensor, *, router_rows: tuple[int, int, int] | None = None) -> Tensor:

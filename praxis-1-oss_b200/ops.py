@@ -337,6 +337,111 @@ def combine(rows: Tensor, routing: Routing, scaling: float, *, h_global: Tensor 
     return out
 
 
+class Tail(NamedTuple):
+    """What follows the MoE output in the reference's MOE_TAIL_NORM path
+    (praxis/layers.py:429-441, praxis/kernels/moe_tail_triton.py:329-445):
+    the residual add of ``residual``; with ``norm_weight`` (fp32 ``1 +
+    weight`` of the next block's zero-centred RMSNorm, its ``eps``) the norm
+    of the new residual times ``norm_scale``; with ``mod`` ([R, 2C] bf16,
+    shift then scale, row map ``mod_geom`` = (RF, RC, NREG, PW, WD, PH) of
+    ``CompactMod`` or None for one row per token, applied to the token's row
+    + ``mod_row0``) the modulation between the two, fused (``mod_fma``) or
+    rounded product first."""
+
+    residual: Tensor
+    norm_weight: Tensor | None = None
+    eps: float = 1e-6
+    norm_scale: float = 1.0
+    mod: Tensor | None = None
+    mod_fma: bool = True
+    mod_geom: tuple | None = None
+    mod_row0: int = 0
+
+    def chunk(self, start: int, end: int) -> "Tail":
+        """The tail of token rows start..end-1 (the modulation rows keep
+        their global row map)."""
+        return self._replace(residual=self.residual[start:end], mod_row0=self.mod_row0 + start)
+
+
+def _tail_struct(tail: Tail, t: int, c: int, device, outs: tuple | None = None
+                 ) -> tuple[capi.TailArgs, Tensor, Tensor | None]:
+    """Validates ``tail`` for [t, c] outputs on ``device`` and allocates them
+    (or checks ``outs`` = (new residual, normed rows or None))."""
+    _need(tail.residual, "residual", BF16, 2, device)
+    if tuple(tail.residual.shape) != (t, c):
+        raise ValueError("the residual does not match the MoE output shape")
+    if tail.norm_weight is not None:
+        _need(tail.norm_weight, "norm weight", torch.float32, 1, device)
+        if tail.norm_weight.numel() != c:
+            raise ValueError("the norm weight does not match the hidden size")
+    if tail.mod is not None:
+        if tail.norm_weight is None:
+            raise ValueError("the modulation needs the norm")
+        _need(tail.mod, "mod", BF16, 2, device)
+        if tail.mod.shape[1] != 2 * c:
+            raise ValueError("modulation rows must be [R, 2C] (shift | scale)")
+        geom = (1, 1, 0, 1, 1, 1) if tail.mod_geom is None else tuple(int(v) for v in tail.mod_geom)
+        need_rows = _mod_rows_needed(t + int(tail.mod_row0), geom)
+        if tail.mod.shape[0] < need_rows:
+            raise ValueError(f"modulation has {tail.mod.shape[0]} rows, the token rows map to {need_rows}")
+    else:
+        geom = (1, 1, 0, 1, 1, 1)
+    if outs is None:
+        residual_out = torch.empty_like(tail.residual)
+        normed = None if tail.norm_weight is None else torch.empty_like(tail.residual)
+    else:
+        residual_out, normed = outs
+        for ten, name in ((residual_out, "residual_out"), (normed, "normed_out")):
+            if ten is None and (name == "residual_out" or tail.norm_weight is not None):
+                raise ValueError(f"{name} is missing")
+            if ten is not None:
+                _need(ten, name, BF16, 2, device)
+                if tuple(ten.shape) != (t, c) or not ten.is_contiguous():
+                    raise ValueError(f"{name} must be a contiguous [{t}, {c}] tensor")
+    st = capi.TailArgs(
+        residual=tail.residual.data_ptr(), residual_out=residual_out.data_ptr(),
+        norm_weight=_p(tail.norm_weight), normed_out=_p(normed), eps=float(tail.eps),
+        norm_scale=float(tail.norm_scale), mod=_p(tail.mod), mod_fma=int(bool(tail.mod_fma)),
+        mod_geom=(capi.I64 * 6)(*geom), mod_row0=int(tail.mod_row0))
+    return st, residual_out, normed
+
+
+def _mod_rows_needed(t: int, geom: tuple) -> int:
+    """1 + the largest modulation row the token rows 0..t-1 map to
+    (praxis/kernels/norm_triton.py:417-431)."""
+    rf, rc, nreg, pw, wd, ph = geom
+    if min(rf, rc, pw, wd, ph) <= 0 or nreg < 0:
+        raise ValueError(f"bad modulation geometry {geom}")
+    if t == 0:
+        return 0
+    row = torch.arange(t, dtype=torch.int64)
+    b = row // rf
+    tt = row - b * rf
+    q = (tt - nreg).clamp(min=0) // pw
+    col = torch.where(tt < nreg, tt, nreg + (q // wd) // ph * wd + q % wd)
+    return int((b * rc + col).max()) + 1
+
+
+def combine_tail(rows: Tensor, routing: Routing, scaling: float, tail: Tail, *, shared: Tensor | None = None,
+                 h_global: Tensor | None = None, h_amax: Tensor | None = None, w_global: Tensor | None = None,
+                 rows_rescaled: bool = False) -> tuple[Tensor, Tensor | None]:
+    """The combine of :func:`combine` (with ``shared``) fused into ``tail``
+    (MOE_TAIL_NORM: ``tail_add_norm_scale``, ``tail_add_mod_norm_scale`` or
+    ``tail_residual_add`` of praxis/kernels/moe_tail_triton.py:329-445):
+    returns ``(new residual, normed rows or None)`` with the eager bits."""
+    t, k = routing.top_idx.shape
+    c = rows.shape[1]
+    e = routing.csr.numel() - 1
+    if shared is not None:
+        _need(shared, "shared", BF16, 2, rows.device)
+    st, residual_out, normed = _tail_struct(tail, t, c, rows.device)
+    capi.check(capi.load().praxis_b200_combine_tail(
+        _p(rows), c, _p(routing.inverse), _p(routing.top_idx), _p(routing.gate), _p(routing.csr), _p(routing.pcsr),
+        _p(h_global), _p(h_amax), _p(w_global), int(rows_rescaled), float(scaling), _p(shared), C.byref(st), t, k,
+        e, _dev(rows), _stream(rows)))
+    return residual_out, normed
+
+
 def pack_weights(w: Tensor) -> tuple[Tensor, Tensor, Tensor]:
     """Expert-first bf16 bank [E, K, N] -> (q [E,N,K/2], sf [E,N,K/16],
     global [E]) on the GPU, the bytes of praxis/quantization/nvfp4.py:67-146."""
@@ -417,11 +522,14 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
                 shared: Tensor | None = None, *, router_terms: Tensor | None = None,
                 router_bias: Tensor | None = None, top_k: int | None = None, activation: str = "sigmoid",
                 out: Tensor | None = None, gate_up_sf_layout: int | None = None,
-                down_sf_layout: int | None = None):
+                down_sf_layout: int | None = None, tail: Tail | None = None, tail_out: tuple | None = None):
     """One dispatch chunk through ``praxis_b200_moe_forward``. With
     ``router_terms`` the router runs too and (out, top_idx, gate) is returned.
     ``gate_up_q/sf`` are in the interleaved kernel layout; the weight scales
-    are compact or replicated (``*_sf_layout``, else told by their size)."""
+    are compact or replicated (``*_sf_layout``, else told by their size).
+    With ``tail`` the combine is fused into what follows the layer
+    (:func:`combine_tail`) and ``(new residual, normed rows or None)`` takes
+    the place of ``out`` (written into ``tail_out`` when given)."""
     _need(x, "x", BF16, 2)
     t, c = x.shape
     e, c_half_f, _ = down_q.shape
@@ -433,7 +541,11 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         gate = torch.empty(t, k, dtype=BF16, device=dev)
     else:
         k = top_idx.shape[1]
-    if out is None:
+    st = None
+    if tail is not None:
+        st, residual_out, normed = _tail_struct(tail, t, c, dev, tail_out)
+        out = None
+    elif out is None:
         out = torch.empty_like(x)
     if gate_up_sf_layout is None:
         gate_up_sf_layout = _layout_of(gate_up_sf, gate_up_q, "gate_up_sf")
@@ -448,14 +560,16 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         activation={"sigmoid": capi.SIGMOID, "softmax": capi.SOFTMAX}[activation],
         router_bias=None if router_bias is None else router_bias.data_ptr(),
         top_idx=top_idx.data_ptr(), gate=gate.data_ptr(),
-        shared=None if shared is None else shared.data_ptr(), out=out.data_ptr(),
+        shared=None if shared is None else shared.data_ptr(), out=_p(out),
         gate_up_q=gate_up_q.data_ptr(), gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(),
         down_q=down_q.data_ptr(), down_sf=down_sf.data_ptr(), down_global=down_global.data_ptr(),
         gate_up_sf_layout=int(gate_up_sf_layout), down_sf_layout=int(down_sf_layout), tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
         workspace=ws.data_ptr(), workspace_size=ws_size, device=_dev(x),
         stream=torch.cuda.current_stream(dev).cuda_stream,
+        tail=None if st is None else C.addressof(st),
     )
     capi.check(lib.praxis_b200_moe_forward(C.byref(args)))
+    res = (out,) if tail is None else (residual_out, normed)
     if router_terms is not None:
-        return out, top_idx, gate
-    return out
+        res = res + (top_idx, gate)
+    return res if len(res) > 1 else out

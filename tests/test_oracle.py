@@ -179,3 +179,56 @@ def test_softmax_rows_sum_order_and_accuracy():
         f32 = torch.softmax(logits, -1).double()
         err, err_torch = ((got.double() - ref).abs() / ref).max().item(), ((f32 - ref).abs() / ref).max().item()
         assert err < 4e-6 and err < 4 * err_torch + 1e-6, (e, err, err_torch)
+
+
+def test_tail_norm_restatement_close_to_float64():
+    """The oracle's tail (eager reduction order) against float64 arithmetic:
+    the residual add is exact up to its bf16 rounding and the normalised rows
+    agree within one bf16 ulp."""
+    g = torch.Generator().manual_seed(5)
+    for n in (512, 3072, 1020):
+        x = torch.randn(40, n, generator=g).to(torch.bfloat16)
+        y = torch.randn(40, n, generator=g).to(torch.bfloat16)
+        w1 = 1 + torch.randn(n, generator=g) * 0.1
+        xo, h = O.tail_add_norm_scale(y, x, w1, 1e-6, 0.5)
+        assert torch.equal(xo, (x.float() + y.float()).to(torch.bfloat16))
+        ss = O.rms_sum_of_squares(xo).double()
+        ref = (xo.double() ** 2).sum(-1)
+        assert ((ss - ref).abs() / ref).max().item() < 1e-5
+        r = (ref / n + 1e-6).rsqrt().unsqueeze(1)
+        want = ((w1.double() * (r * xo.double())).to(torch.bfloat16).double() * 0.5).to(torch.bfloat16)
+        d = (h.view(torch.int16).int() - want.view(torch.int16).int()).abs()
+        assert d.max().item() <= 1
+
+
+def test_modulation_row_map():
+    """The compact modulation row map (praxis/kernels/norm_triton.py:417-431)
+    against its definition written out row by row."""
+    rf, rc, nreg, pw, wd, ph = geom = (26, 8, 2, 2, 3, 2)
+    got = O.mod_row_map(60, geom).tolist()
+    want = []
+    for row in range(60):
+        b, t = divmod(row, rf)
+        if t < nreg:
+            want.append(b * rc + t)
+            continue
+        u = t - nreg
+        j, u = u % pw, u // pw   # innermost index j < PW
+        x, u = u % wd, u // wd   # then x < WD
+        i, fy = u % ph, u // ph  # then i < PH; the rest is (f, y)
+        want.append(b * rc + nreg + fy * wd + x)
+    assert got == want
+    assert O.mod_row_map(5).tolist() == [0, 1, 2, 3, 4]
+
+
+def test_modulation_fused_and_unfused_agree():
+    """bf16 operands make the modulation product exact in fp32, so the fused
+    (FMA) and unfused forms give the same bits (the oracle has one form)."""
+    g = torch.Generator().manual_seed(8)
+    xo = torch.randn(64, 256, generator=g).to(torch.bfloat16)
+    mod = (torch.randn(64, 512, generator=g) * 0.3).to(torch.bfloat16)
+    sc1 = (mod[:, 256:].float() + 1).to(torch.bfloat16).float()
+    prod = xo.float() * sc1
+    assert torch.equal(prod.double(), xo.double() * sc1.double())
+    out = O.tail_modulate(xo, mod, torch.arange(64))
+    assert torch.equal(out, (prod + mod[:, :256].float()).to(torch.bfloat16))

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define PRAXIS_B200_ABI_VERSION 1
+#define PRAXIS_B200_ABI_VERSION 2
 
 enum {
   PRAXIS_B200_OK = 0,
@@ -122,6 +122,26 @@ int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* r
                          int64_t* inverse, int64_t* tokens_out, int32_t* tokens32, void* sorted_gate,
                          int32_t* offsets, int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles,
                          int32_t* num_tiles, float* act_global, uint32_t* act_amax, int device, void* stream);
+
+/* praxis_b200_dispatch of `passes` (1 or 2) lockstep inputs, tokens back to
+ * back (a classifier-free-guidance pair: pass 1 from token pass0_tokens).
+ * With passes == 2 the routed rows of expert e and pass s form group
+ * g = 2 e + s, and the per-expert outputs become per group: order / inverse
+ * sort by (g, position), csr [2E + 1] is the reference's seg_csr, offsets
+ * [2E] the group end offsets (the reference's per-expert offsets are
+ * offsets[1::2]), pcsr / tiles / act_global / act_amax per group, each group
+ * padded to 128 rows on its own. The same values as the reference's P = 2
+ * route_dispatch / dispatch_ref (praxis/kernels/router_fused.py:738-804,
+ * :820-852), the per-(expert, pass) segments of
+ * praxis/kernels/nvfp4_pair.py:1-20. max_tiles =
+ * praxis_b200_padded_rows(T*k, E*passes) / 128. */
+size_t praxis_b200_dispatch_passes_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t passes);
+int praxis_b200_dispatch_passes(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
+                                int32_t top_k, int32_t experts, int32_t passes, int64_t pass0_tokens, void* workspace,
+                                size_t workspace_size, int64_t* order, int64_t* inverse, int64_t* tokens_out,
+                                int32_t* tokens32, void* sorted_gate, int32_t* offsets, int32_t* csr, int32_t* pcsr,
+                                int32_t* tiles, int32_t max_tiles, int32_t* num_tiles, float* act_global,
+                                uint32_t* act_amax, int device, void* stream);
 
 /* NVFP4 quantization of the routed rows (gathered from x [T, C] bf16 through
  * inverse/top_idx) into the padded expert-grouped layout: q [Rp, C/2] (two
@@ -291,10 +311,18 @@ typedef struct praxis_b200_moe_args {
   /* Optional MoE tail fused into what follows it (praxis_b200_combine_tail):
    * when set, its outputs replace `out`, which may be NULL. */
   const praxis_b200_tail* tail;
+  /* Lockstep passes (0 or 1: one input; 2: a classifier-free-guidance pair
+   * whose second input starts at token pass0_tokens): the routed rows of
+   * both inputs go through one pass of the expert GEMMs, grouped per
+   * (expert, input) as praxis_b200_dispatch_passes groups them, and every
+   * output row has the bits of its input run alone
+   * (MoEFeedForward.forward_pair, praxis/layers.py:1779-1853). */
+  int32_t passes;
+  int64_t pass0_tokens;
 } praxis_b200_moe_args;
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,
-                                      int32_t with_router);
+                                      int32_t with_router, int32_t passes);
 int praxis_b200_moe_forward(const praxis_b200_moe_args* args);
 
 /* Expert-rank half of an expert-parallel layer (no reference counterpart:

@@ -415,6 +415,28 @@ def dispatch(top_idx: torch.Tensor, gate: torch.Tensor, num_experts: int):
     return order, inverse, tokens, gate.reshape(-1)[order], offsets, csr
 
 
+def dispatch_passes(top_idx: torch.Tensor, gate: torch.Tensor, num_experts: int, rows):
+    """The dispatch metadata of lockstep inputs ``rows = (T0, T1)`` (or one
+    input, ``(T,)``): ``dispatch_ref`` of praxis/kernels/router_fused.py:
+    820-852. Key of slot (t, s) = top_idx[t, s] * P + pass(t); a stable sort
+    of the keys gives order and inverse; seg_csr [P*E + 1] counts per key;
+    offsets = seg_csr[P::P] (per-expert end offsets); tokens = order // k.
+    Returns order, inverse, tokens, sorted_gate, seg_csr, offsets."""
+    rows = tuple(int(r) for r in rows)
+    npass = len(rows)
+    t, k = top_idx.shape
+    pas = torch.zeros(t, dtype=torch.int64)
+    if npass == 2:
+        pas[rows[0]:] = 1
+    keys = (top_idx * npass + pas[:, None]).reshape(-1)
+    _, order = keys.sort(stable=True)
+    inverse = torch.empty_like(order)
+    inverse[order] = torch.arange(order.numel())
+    counts = torch.bincount(keys, minlength=npass * num_experts)
+    seg_csr = torch.nn.functional.pad(counts.cumsum(0).to(torch.int32), (1, 0))
+    return order, inverse, order // k, gate.reshape(-1)[order], seg_csr, seg_csr[npass::npass].contiguous()
+
+
 def pad_csr(csr: torch.Tensor, align: int = ALIGN) -> torch.Tensor:
     """praxis/kernels/nvfp4.py:37-41: ((csr[i] + (align-1)*i) // align) * align."""
     i = torch.arange(csr.numel(), dtype=torch.int64)

@@ -7,6 +7,7 @@ calls (praxis/layers.py:2230-2270):
 
     routed_forward(x, top_idx, gate, *, scaling, chunk_size, dispatch=None)
     routed_forward_with_shared(x, top_idx, gate, *, scaling, chunk_size, shared, dispatch=None)
+    routed_forward_pair(xs, top_idxs, gates, *, scaling, ...)   (praxis/layers.py:1803-1806)
 
 so ``layer.routed = B200NVFP4RoutedExperts.from_packed(layer.routed.state_dict())``
 swaps the reference's FlashInfer/Triton kernels for this library's sm_100a
@@ -94,10 +95,9 @@ class B200NVFP4RoutedExperts(nn.Module):
 
     Device moves are supported; dtype casts, training and gradients are not
     (praxis/quantization/nvfp4.py:229-290). The fused SwiGLU GEMM reads the
-    gate/up weight in 64-row gate/up blocks and both GEMMs read replicated
-    block scales: those copies are built on the device by ``prepare()``
-    (called by the first forward; call it before capturing a CUDA graph) and
-    are not part of the state dict.
+    gate/up weight in 64-row gate/up blocks: that copy is built on the device
+    by ``prepare()`` (called by the first forward; call it before capturing a
+    CUDA graph) and is not part of the state dict.
     """
 
     format = "nvfp4"
@@ -188,6 +188,55 @@ class B200NVFP4RoutedExperts(nn.Module):
             return self.routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size) + shared
         return self._routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size, shared=shared)
 
+    def routed_forward_pair(self, xs, top_idxs, gates, *, scaling: float, shared=None, tail: ops.Tail | None = None,
+                            dispatch=None) -> list:
+        """``[self.routed_forward(x, i, g, scaling=scaling, chunk_size=len(x)) for ...]``
+        of two inputs (the guided and unguided passes of a CFG pair) in one
+        paired dispatch, each input one dispatch chunk
+        (praxis/quantization/nvfp4.py:467-488, the paired dispatch of
+        praxis/kernels/nvfp4_pair.py:1-20): the rows of expert e are grouped
+        per input, each group with its own activation and hidden global
+        scales, so every output has the bits of its input run alone, while
+        the expert GEMMs run once over both inputs' rows. ``shared``: the two
+        shared-expert outputs, added after rounding as by
+        ``routed_forward_with_shared``. ``tail``: the fused tail over both
+        inputs' rows back to back (:func:`routed_forward_tail`); the result
+        is then ``[(new residual, normed or None)]`` per input. ``dispatch``
+        is accepted for the reference's signature and not needed (the
+        dispatch runs inside the fused call). Inputs that sit back to back
+        in one buffer are used in place; others are copied together."""
+        del dispatch
+        xs, top_idxs, gates = list(xs), list(top_idxs), list(gates)
+        if not (len(xs) == len(top_idxs) == len(gates) == 2):
+            raise ValueError("routed_forward_pair takes two inputs")
+        t0, t1 = xs[0].shape[0], xs[1].shape[0]
+        for x, i, g in zip(xs, top_idxs, gates, strict=True):
+            self._check(x, i, g, scaling, max(1, x.shape[0]))
+        if top_idxs[0].shape[1] != top_idxs[1].shape[1] or xs[0].device != xs[1].device:
+            raise ValueError("the two inputs must share top-k and device")
+        x = _adjacent(xs)
+        top_idx = _adjacent(top_idxs)
+        gate = _adjacent(gates)
+        self._check(x, top_idx, gate, scaling, max(1, t0 + t1))
+        sh = None
+        if shared is not None:
+            shared = list(shared)
+            if len(shared) != 2 or any(s.shape != xi.shape or s.dtype != xi.dtype or s.device != xi.device
+                                       for s, xi in zip(shared, xs, strict=True)):
+                raise ValueError("Expected two BF16 shared-expert outputs shaped like the inputs")
+            sh = _adjacent(shared)
+        kw = self.kernel_weights()
+        common = dict(gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout, rows=(t0, t1))
+        if tail is not None:
+            xo, h = ops.moe_forward(
+                x, top_idx, gate, kw.gate_up_q, kw.gate_up_sf, self.gate_up_global, self.down_q, kw.down_sf,
+                self.down_global, float(scaling), sh, tail=tail, **common)
+            return [(xo[:t0], None if h is None else h[:t0]), (xo[t0:], None if h is None else h[t0:])]
+        out = ops.moe_forward(
+            x, top_idx, gate, kw.gate_up_q, kw.gate_up_sf, self.gate_up_global, self.down_q, kw.down_sf,
+            self.down_global, float(scaling), sh, **common)
+        return [out[:t0], out[t0:]]
+
     def forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, *, scaling: float, chunk_size: int) -> Tensor:
         return self.routed_forward(x, top_idx, gate, scaling=scaling, chunk_size=chunk_size)
 
@@ -244,6 +293,20 @@ class B200NVFP4RoutedExperts(nn.Module):
                 gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout,
             )
         return out
+
+
+def _adjacent(parts: list) -> Tensor:
+    """The rows of ``parts`` (contiguous 2-D tensors of one width) back to
+    back: a view when they already sit so in one buffer (the reference's
+    PAIR_BUFFER writes the paired inputs into adjacent slices), else a copy."""
+    a, b = parts
+    if (
+        a.is_contiguous() and b.is_contiguous() and a.dtype == b.dtype and a.shape[1:] == b.shape[1:]
+        and a.untyped_storage().data_ptr() == b.untyped_storage().data_ptr()
+        and b.data_ptr() == a.data_ptr() + a.numel() * a.element_size()
+    ):
+        return torch.as_strided(a, (a.shape[0] + b.shape[0],) + tuple(a.shape[1:]), a.stride())
+    return torch.cat([a, b])
 
 
 def routed_forward_tail(bank: B200NVFP4RoutedExperts, x: Tensor, top_idx: Tensor, gate: Tensor, *,

@@ -22,6 +22,8 @@ I64 = C.c_int64
 F32 = C.c_float
 SZ = C.c_size_t
 
+ABI_VERSION = 2  # PRAXIS_B200_ABI_VERSION of include/praxis_b200_moe.h
+
 OK, EINVAL, ECUDA, EUNSUPPORTED = 0, 1, 2, 3
 SIGMOID, SOFTMAX = 0, 1
 EPI_PLAIN, EPI_SWIGLU, EPI_RESCALE = 0, 1, 2
@@ -60,6 +62,8 @@ class MoeArgs(C.Structure):
         ("device", C.c_int),
         ("stream", P),
         ("tail", P),
+        ("passes", I32),
+        ("pass0_tokens", I64),
     ]
 
 
@@ -122,6 +126,11 @@ SIGNATURES: dict[str, tuple] = {
     "praxis_b200_route": (C.c_int, [P, P, I64, I32, I32, I32, P, P, C.c_int, P]),
     "praxis_b200_row_amax": (C.c_int, [P, I64, I32, P, C.c_int, P]),
     "praxis_b200_dispatch_workspace_size": (SZ, [I64, I32, I32]),
+    "praxis_b200_dispatch_passes_workspace_size": (SZ, [I64, I32, I32, I32]),
+    "praxis_b200_dispatch_passes": (
+        C.c_int,
+        [P, P, P, I64, I32, I32, I32, I64, P, SZ, P, P, P, P, P, P, P, P, P, I32, P, P, P, C.c_int, P],
+    ),
     "praxis_b200_dispatch": (
         C.c_int,
         [P, P, P, I64, I32, I32, P, SZ, P, P, P, P, P, P, P, P, P, I32, P, P, P, C.c_int, P],
@@ -147,7 +156,7 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "praxis_b200_pack_weights": (C.c_int, [P, I32, I32, I32, P, P, P, P, C.c_int, P]),
     "praxis_b200_interleave_gate_up": (C.c_int, [P, P, I32, I32, I32, P, P, C.c_int, P]),
-    "praxis_b200_moe_workspace_size": (SZ, [I64, I32, I32, I32, I32, I32]),
+    "praxis_b200_moe_workspace_size": (SZ, [I64, I32, I32, I32, I32, I32, I32]),
     "praxis_b200_moe_forward": (C.c_int, [C.POINTER(MoeArgs)]),
     "praxis_b200_expert_workspace_size": (SZ, [I64, I32, I32, I32]),
     "praxis_b200_expert_forward": (C.c_int, [C.POINTER(ExpertArgs)]),
@@ -194,7 +203,7 @@ def load(build_if_missing: bool = False) -> C.CDLL:
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.praxis_b200_abi_version() != 1:
+        if lib.praxis_b200_abi_version() != ABI_VERSION:
             raise PraxisB200Error("ABI version mismatch")
         _LIB = lib
         return lib

@@ -12,9 +12,9 @@
 namespace praxis {
 
 // Internal entry points of the other .cu files.
-size_t dispatch_workspace_bytes(int64_t tokens, int top_k, int experts);
+size_t dispatch_workspace_bytes(int64_t tokens, int top_k, int groups);
 int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* row_amax, int64_t tokens, int top_k,
-                 int experts, void* workspace, size_t workspace_bytes, int64_t* order, int64_t* inverse,
+                 int experts, Passes passes, void* workspace, size_t workspace_bytes, int64_t* order, int64_t* inverse,
                  int64_t* tokens_out, int32_t* tokens32, uint16_t* sorted_gate, int32_t* offsets, int32_t* csr,
                  int32_t* pcsr, TileEntry* tiles, int max_tiles, int32_t* num_tiles, float* act_global,
                  uint32_t* act_amax_bits, cudaStream_t stream);
@@ -22,7 +22,7 @@ int run_row_amax(const uint16_t* x, int64_t rows, int cols, uint16_t* out, cudaS
 int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int64_t* top_idx, const int64_t* inverse,
                         const int32_t* csr, const int32_t* pcsr, const float* globals, const uint32_t* amax_bits,
                         int top_k, int experts, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
-                        uint8_t* q, uint8_t* sf, int sf_layout, cudaStream_t stream);
+                        uint8_t* q, uint8_t* sf, int sf_layout, cudaStream_t stream, Passes passes = Passes{1, 0});
 int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
                       const float* globals, const uint32_t* amax_bits, uint8_t* q, uint8_t* sf, int sf_layout,
                       cudaStream_t stream);
@@ -43,12 +43,12 @@ int run_rescale_swiglu(const uint16_t* raw, int64_t rows, int hidden, const int3
 int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx, const uint16_t* gate,
                 const int32_t* csr, const int32_t* pcsr, const float* h_global, const uint32_t* h_amax,
                 const float* w_global, int rows_rescaled, float scaling, const uint16_t* shared, uint16_t* out,
-                int64_t tokens, int top_k, int experts, cudaStream_t stream);
+                int64_t tokens, int top_k, int experts, cudaStream_t stream, Passes passes = Passes{1, 0});
 int run_combine_tail(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx,
                      const uint16_t* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
                      const uint32_t* h_amax, const float* w_global, int rows_rescaled, float scaling,
                      const uint16_t* shared, const TailArgs& tail, int64_t tokens, int top_k, int experts,
-                     cudaStream_t stream);
+                     cudaStream_t stream, Passes passes = Passes{1, 0});
 
 // The ABI's tail descriptor as the kernel's arguments.
 static TailArgs tail_args(const praxis_b200_tail& t) {
@@ -144,8 +144,11 @@ struct MoeLayout {
   int max_tiles;
 };
 
-static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int hidden, bool with_router) {
+// `passes` lockstep passes: per-group buffers for experts * passes groups.
+static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int passes, int dim, int hidden,
+                            bool with_router) {
   MoeLayout L;
+  const int groups = experts * passes;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -153,20 +156,20 @@ static MoeLayout moe_layout(int64_t tokens, int top_k, int experts, int dim, int
     return o;
   };
   const int64_t r = tokens * top_k;
-  L.rp = padded_rows(r, experts);
+  L.rp = padded_rows(r, groups);
   L.max_tiles = (int)(L.rp / 128);
-  L.dispatch = take(dispatch_workspace_bytes(tokens, top_k, experts));
+  L.dispatch = take(dispatch_workspace_bytes(tokens, top_k, groups));
   L.row_amax = take((size_t)tokens * 2);
   L.logits = take(with_router ? (size_t)tokens * experts * 4 : 0);
   L.inverse = take((size_t)r * 8);
-  L.csr = take((size_t)(experts + 1) * 4);
-  L.pcsr = take((size_t)(experts + 1) * 4);
-  L.offsets = take((size_t)experts * 4);
+  L.csr = take((size_t)(groups + 1) * 4);
+  L.pcsr = take((size_t)(groups + 1) * 4);
+  L.offsets = take((size_t)groups * 4);
   L.tiles = take((size_t)(2 * L.max_tiles + 1) * sizeof(TileEntry));
   L.num_tiles = take(8);
-  L.act_amax = take((size_t)experts * 4);
-  L.act_global = take((size_t)experts * 4);
-  L.h_amax = take((size_t)experts * 4);
+  L.act_amax = take((size_t)groups * 4);
+  L.act_global = take((size_t)groups * 4);
+  L.h_amax = take((size_t)groups * 4);
   L.aq = take((size_t)L.rp * dim / 2);
   L.asf = take((size_t)L.rp * dim / 16 * 4);  // room for the replicated layout
   L.asf_compact = take((size_t)L.rp * dim / 16);
@@ -266,23 +269,39 @@ size_t praxis_b200_dispatch_workspace_size(int64_t tokens, int32_t top_k, int32_
   return dispatch_workspace_bytes(tokens, top_k, experts);
 }
 
+size_t praxis_b200_dispatch_passes_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t passes) {
+  return dispatch_workspace_bytes(tokens, top_k, experts * (passes == 2 ? 2 : 1));
+}
+
+int praxis_b200_dispatch_passes(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
+                                int32_t top_k, int32_t experts, int32_t passes, int64_t pass0_tokens, void* workspace,
+                                size_t workspace_size, int64_t* order, int64_t* inverse, int64_t* tokens_out,
+                                int32_t* tokens32, void* sorted_gate, int32_t* offsets, int32_t* csr, int32_t* pcsr,
+                                int32_t* tiles, int32_t max_tiles, int32_t* num_tiles, float* act_global,
+                                uint32_t* act_amax, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if ((tokens > 0 && !top_idx) || !csr || !pcsr || !tiles || !num_tiles || !workspace)
+    return set_error(PRAXIS_B200_EINVAL, "dispatch: null pointer");
+  if (tokens > 0 && sorted_gate && !gate) return set_error(PRAXIS_B200_EINVAL, "dispatch: sorted_gate needs gate");
+  if (passes != 1 && passes != 2) return set_error(PRAXIS_B200_EINVAL, "dispatch: passes must be 1 or 2");
+  if (max_tiles < padded_rows(tokens * top_k, (int64_t)experts * passes) / 128)
+    return set_error(PRAXIS_B200_EINVAL, "dispatch: max_tiles below padded_rows/128");
+  int32_t* off = offsets;
+  return run_dispatch(top_idx, static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(row_amax), tokens,
+                      top_k, experts, Passes{passes, passes == 2 ? pass0_tokens : 0}, workspace, workspace_size, order,
+                      inverse, tokens_out, tokens32, static_cast<uint16_t*>(sorted_gate), off ? off : csr + 1, csr,
+                      pcsr, reinterpret_cast<TileEntry*>(tiles), max_tiles, num_tiles, act_global, act_amax,
+                      PRAXIS_STREAM(stream));
+}
+
 int praxis_b200_dispatch(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
                          int32_t top_k, int32_t experts, void* workspace, size_t workspace_size, int64_t* order,
                          int64_t* inverse, int64_t* tokens_out, int32_t* tokens32, void* sorted_gate,
                          int32_t* offsets, int32_t* csr, int32_t* pcsr, int32_t* tiles, int32_t max_tiles,
                          int32_t* num_tiles, float* act_global, uint32_t* act_amax, int device, void* stream) {
-  PRAXIS_DEVICE_OR_RETURN(device);
-  if ((tokens > 0 && !top_idx) || !csr || !pcsr || !tiles || !num_tiles || !workspace)
-    return set_error(PRAXIS_B200_EINVAL, "dispatch: null pointer");
-  if (tokens > 0 && sorted_gate && !gate) return set_error(PRAXIS_B200_EINVAL, "dispatch: sorted_gate needs gate");
-  if (max_tiles < padded_rows(tokens * top_k, experts) / 128)
-    return set_error(PRAXIS_B200_EINVAL, "dispatch: max_tiles below padded_rows/128");
-  int32_t* off = offsets;
-  return run_dispatch(top_idx, static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(row_amax), tokens,
-                      top_k, experts, workspace, workspace_size, order, inverse, tokens_out, tokens32,
-                      static_cast<uint16_t*>(sorted_gate), off ? off : csr + 1, csr, pcsr,
-                      reinterpret_cast<TileEntry*>(tiles), max_tiles, num_tiles, act_global, act_amax,
-                      PRAXIS_STREAM(stream));
+  return praxis_b200_dispatch_passes(top_idx, gate, row_amax, tokens, top_k, experts, 1, 0, workspace,
+                                     workspace_size, order, inverse, tokens_out, tokens32, sorted_gate, offsets, csr,
+                                     pcsr, tiles, max_tiles, num_tiles, act_global, act_amax, device, stream);
 }
 
 int praxis_b200_dispatch_noalloc(const int64_t* top_idx, const void* gate, const void* row_amax, int64_t tokens,
@@ -472,8 +491,8 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
 }
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,
-                                      int32_t with_router) {
-  return moe_layout(tokens, top_k, experts, dim, hidden, with_router != 0).total;
+                                      int32_t with_router, int32_t passes) {
+  return moe_layout(tokens, top_k, experts, passes == 2 ? 2 : 1, dim, hidden, with_router != 0).total;
 }
 
 int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
@@ -493,10 +512,16 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
       a->top_k > a->experts)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: bad sizes");
   if (a->dim % 128 || a->hidden % 128) return set_error(PRAXIS_B200_EINVAL, "moe_forward: C and F must be multiples of 128");
+  if (a->passes != 0 && a->passes != 1 && a->passes != 2)
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: passes must be 1 or 2");
+  const Passes passes{a->passes == 2 ? 2 : 1, a->passes == 2 ? a->pass0_tokens : 0};
+  if (passes.n == 2 && (passes.t0 < 0 || passes.t0 > a->tokens))
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: pass 0 tokens outside 0..tokens");
+  const int groups = a->experts * passes.n;
   const int64_t r = a->tokens * a->top_k;
-  if ((r + 127 * (int64_t)a->experts) * (int64_t)(a->dim > 2 * a->hidden ? a->dim : 2 * a->hidden) >= ((int64_t)1 << 31) * 8)
+  if ((r + 127 * (int64_t)groups) * (int64_t)(a->dim > 2 * a->hidden ? a->dim : 2 * a->hidden) >= ((int64_t)1 << 31) * 8)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: chunk exceeds the kernels' indexing range");
-  const MoeLayout L = moe_layout(a->tokens, a->top_k, a->experts, a->dim, a->hidden, with_router);
+  const MoeLayout L = moe_layout(a->tokens, a->top_k, a->experts, passes.n, a->dim, a->hidden, with_router);
   if (a->workspace_size < L.total)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: workspace %zu < %zu bytes", a->workspace_size, L.total);
   if (a->tokens == 0) return PRAXIS_B200_OK;
@@ -531,7 +556,7 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
     rc = run_row_amax(x, a->tokens, a->dim, row_amax, s);
   }
   if (rc) return rc;
-  rc = run_dispatch(a->top_idx, gate, row_amax, a->tokens, a->top_k, a->experts, ws + L.dispatch,
+  rc = run_dispatch(a->top_idx, gate, row_amax, a->tokens, a->top_k, a->experts, passes, ws + L.dispatch,
                     L.row_amax - L.dispatch, nullptr, inverse, nullptr, nullptr, nullptr, offsets, csr, pcsr, tiles,
                     L.max_tiles, num_tiles, act_global, act_amax, s);
   if (rc) return rc;
@@ -541,17 +566,17 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   const bool rep = gl == PRAXIS_B200_SF_REPLICATED, down_rep = dl == PRAXIS_B200_SF_REPLICATED;
   rc = run_quantize_gather(x, a->tokens, a->dim, a->top_idx, inverse, csr, pcsr, act_global, nullptr, a->top_k,
                            a->experts, tiles, num_tiles, L.max_tiles, aq, rep ? ws + L.asf_compact : asf,
-                           PRAXIS_B200_SF_COMPACT, s);
+                           PRAXIS_B200_SF_COMPACT, s, passes);
   if (rc) return rc;
   if (rep) {
     rc = run_replicate_scales(ws + L.asf_compact, L.rp, a->dim, 128, asf, s);
     if (rc) return rc;
   }
-  cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * a->experts, s);
+  cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * groups, s);
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
                         a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
-                        h_amax, gl, s);
+                        h_amax, gl, s, 0, passes.n);
   if (rc) return rc;
   rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
                          down_rep ? ws + L.hsf_compact : hsf, PRAXIS_B200_SF_COMPACT, s);
@@ -561,15 +586,16 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
     if (rc) return rc;
   }
   rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
-                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, dl, s);
+                        a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, dl, s, 0,
+                        passes.n);
   if (rc) return rc;
   if (a->tail != nullptr)
     return run_combine_tail(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
                             a->scaling, static_cast<const uint16_t*>(a->shared), tail_args(*a->tail), a->tokens,
-                            a->top_k, a->experts, s);
+                            a->top_k, a->experts, s, passes);
   return run_combine(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,
                      a->scaling, static_cast<const uint16_t*>(a->shared), static_cast<uint16_t*>(a->out), a->tokens,
-                     a->top_k, a->experts, s);
+                     a->top_k, a->experts, s, passes);
 }
 
 // ---------------------------------------------------------------------------

@@ -22,7 +22,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate, const int32_t* __restrict__ csr,
     const int32_t* __restrict__ pcsr, const float* __restrict__ h_global, const uint32_t* __restrict__ h_amax,
     const float* __restrict__ w_global, int rows_rescaled, float scaling, const uint16_t* __restrict__ shared,
-    uint16_t* __restrict__ out, int64_t tokens, int top_k, int experts) {
+    uint16_t* __restrict__ out, int64_t tokens, int top_k, int experts, Passes passes) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
   __shared__ int64_t s_src[8][8];
@@ -32,17 +32,12 @@ __global__ void __launch_bounds__(256) combine_kernel(
   if (t >= tokens) return;
   if (lane < top_k) {
     const int64_t p = t * top_k + lane;
-    int64_t e64 = top_idx[p];
-    int e = (int)e64;
-    if (e64 < 0 || e64 >= experts) {
-      record_error(kErrIndexRange);
-      e = e64 < 0 ? 0 : experts - 1;
-    }
-    s_src[warp][lane] = (int64_t)pcsr[e] + inverse[p] - csr[e];
+    const int e = checked_expert(top_idx[p], experts), g = route_group(e, t, passes);
+    s_src[warp][lane] = (int64_t)pcsr[g] + inverse[p] - csr[g];
     s_scale[warp][lane] = mul_rn(bf16_to_f32(gate[p]), scaling);
     float mult = 1.0f;
     if (!rows_rescaled) {
-      const float gh = h_global != nullptr ? h_global[e] : global_from_amax_bits(h_amax[e]);
+      const float gh = h_global != nullptr ? h_global[g] : global_from_amax_bits(h_amax[g]);
       mult = bf16_round(mul_rn(gh, w_global[e]));
     }
     s_mult[warp][lane] = mult;
@@ -106,7 +101,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
 int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const int64_t* top_idx, const uint16_t* gate,
                 const int32_t* csr, const int32_t* pcsr, const float* h_global, const uint32_t* h_amax,
                 const float* w_global, int rows_rescaled, float scaling, const uint16_t* shared, uint16_t* out,
-                int64_t tokens, int top_k, int experts, cudaStream_t stream) {
+                int64_t tokens, int top_k, int experts, cudaStream_t stream, Passes passes) {
   if (cols % 8 != 0) return set_error(PRAXIS_B200_EINVAL, "combine needs C %% 8 == 0");
   if (top_k < 1 || top_k > 8) return set_error(PRAXIS_B200_EINVAL, "top_k must be 1..8");
   if (!rows_rescaled && (w_global == nullptr || (h_global == nullptr && h_amax == nullptr)))
@@ -116,7 +111,8 @@ int run_combine(const uint16_t* rows, int cols, const int64_t* inverse, const in
   // eight 16-byte loads in flight per lane for every top_k
 #define PRAXIS_COMBINE(KMAX, U)                                                                                    \
   launch_pdl(combine_kernel<KMAX, U>, dim3((unsigned)blocks), dim3(256), 0, stream, rows, cols, inverse, top_idx, gate, \
-             csr, pcsr, h_global, h_amax, w_global, rows_rescaled, scaling, shared, out, tokens, top_k, experts)
+             csr, pcsr, h_global, h_amax, w_global, rows_rescaled, scaling, shared, out, tokens, top_k, experts,  \
+             passes)
   if (top_k == 1) PRAXIS_COMBINE(1, 8);
   else if (top_k == 2) PRAXIS_COMBINE(2, 4);
   else if (top_k <= 4) PRAXIS_COMBINE(4, 2);

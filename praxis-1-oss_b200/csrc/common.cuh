@@ -668,4 +668,29 @@ struct TileEntry {
 
 constexpr int kTileRows = 128;
 
+// Lockstep passes (the two inputs of a classifier-free-guidance pair, tokens
+// back to back, pass 1 from token t0): the routed rows of token t sent to
+// expert e form group e * n + pass, each group with its own activation and
+// hidden global scales and its own padded rows, so every row keeps the bits
+// of its pass run alone (praxis/kernels/nvfp4_pair.py:1-20; segment order of
+// praxis/kernels/router_fused.py:820-839). n = 1: group e.
+struct Passes {
+  int32_t n;
+  int64_t t0;
+};
+
+__device__ __forceinline__ int route_group(int e, int64_t token, Passes ps) {
+  return ps.n == 2 ? 2 * e + (token >= ps.t0 ? 1 : 0) : e;
+}
+
+// The expert index of a routed slot, clamped (with an index-range error
+// recorded) when out of range.
+__device__ __forceinline__ int checked_expert(int64_t e, int experts) {
+  if (e < 0 || e >= experts) {
+    record_error(kErrIndexRange);
+    return e < 0 ? 0 : experts - 1;
+  }
+  return (int)e;
+}
+
 }  // namespace praxis

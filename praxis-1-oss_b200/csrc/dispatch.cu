@@ -26,14 +26,6 @@ constexpr int kDispatchWarps = 8;
 constexpr int kDispatchUnroll = 8;  // 32-position passes whose loads are issued together
 constexpr int kMaxExperts = 1024;
 
-__device__ __forceinline__ int clamp_expert(int64_t e, int experts) {
-  if (e < 0 || e >= experts) {
-    record_error(kErrIndexRange);
-    return e < 0 ? 0 : experts - 1;
-  }
-  return (int)e;
-}
-
 // ---------------------------------------------------------------------------
 // Row max |x| (bf16), praxis/kernels/nvfp4_moe.py:15-21
 // ---------------------------------------------------------------------------
@@ -63,16 +55,19 @@ __global__ void row_amax_kernel(const uint16_t* __restrict__ x, int64_t rows, in
 // ---------------------------------------------------------------------------
 // 1. count
 // ---------------------------------------------------------------------------
+// `experts` counts the routed experts, `groups` = experts * passes.n the
+// histogram bins (route_group).
 __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ row_amax,
-                                      int64_t positions, int top_k, int experts, int seg_len, int segments,
-                                      int32_t* __restrict__ seg_count, uint32_t* __restrict__ seg_max) {
+                                      int64_t positions, int top_k, int experts, Passes passes, int groups,
+                                      int seg_len, int segments, int32_t* __restrict__ seg_count,
+                                      uint32_t* __restrict__ seg_max) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
   extern __shared__ uint32_t s_dc[];
-  uint32_t* hist = s_dc;                                  // [warps][experts]
-  uint32_t* hmax = s_dc + kDispatchWarps * experts;       // [warps][experts]
+  uint32_t* hist = s_dc;                                 // [warps][groups]
+  uint32_t* hmax = s_dc + kDispatchWarps * groups;       // [warps][groups]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kDispatchWarps * experts; i += blockDim.x) {
+  for (int i = threadIdx.x; i < kDispatchWarps * groups; i += blockDim.x) {
     hist[i] = 0;
     hmax[i] = 0;
   }
@@ -81,8 +76,8 @@ __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const
   if (seg < segments) {
     const int64_t begin = (int64_t)seg * seg_len;
     const int64_t end = min(positions, begin + seg_len);
-    uint32_t* h = hist + warp * experts;
-    uint32_t* hm = hmax + warp * experts;
+    uint32_t* h = hist + warp * groups;
+    uint32_t* hm = hmax + warp * groups;
     // the loads of 8 passes of 32 positions go out before the histogram work
     for (int64_t base = begin; base < end; base += 32 * kDispatchUnroll) {
       int ev[kDispatchUnroll];
@@ -91,7 +86,7 @@ __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const
       for (int u = 0; u < kDispatchUnroll; ++u) {
         const int64_t p = base + 32 * u + lane;
         const bool live = p < end;
-        ev[u] = live ? clamp_expert(top_idx[p], experts) : -1;
+        ev[u] = live ? route_group(checked_expert(top_idx[p], experts), p / top_k, passes) : -1;
         mv[u] = (live && row_amax != nullptr) ? __float_as_uint(bf16_to_f32(row_amax[p / top_k])) : 0u;
       }
 #pragma unroll
@@ -108,9 +103,9 @@ __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const
   }
   __syncwarp();
   if (seg < segments) {
-    for (int e = lane; e < experts; e += 32) {
-      seg_count[(int64_t)seg * experts + e] = (int32_t)hist[warp * experts + e];
-      seg_max[(int64_t)seg * experts + e] = hmax[warp * experts + e];
+    for (int e = lane; e < groups; e += 32) {
+      seg_count[(int64_t)seg * groups + e] = (int32_t)hist[warp * groups + e];
+      seg_max[(int64_t)seg * groups + e] = hmax[warp * groups + e];
     }
   }
 }
@@ -317,19 +312,20 @@ int run_segment_tiles(const int32_t* counts, const int32_t* starts, int segments
 // 3. scatter
 // ---------------------------------------------------------------------------
 __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate,
-                                        int64_t positions, int top_k, int experts, int seg_len, int segments,
+                                        int64_t positions, int top_k, int experts, Passes passes, int groups,
+                                        int seg_len, int segments,
                                         const int32_t* __restrict__ seg_start, const int32_t* __restrict__ csr,
                                         int64_t* __restrict__ order, int64_t* __restrict__ inverse,
                                         int64_t* __restrict__ tokens, int32_t* __restrict__ tokens32,
                                         uint16_t* __restrict__ sorted_gate) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
-  extern __shared__ int32_t s_cursor[];  // [warps][experts]
+  extern __shared__ int32_t s_cursor[];  // [warps][groups]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seg = blockIdx.x * kDispatchWarps + warp;
   if (seg >= segments) return;
-  int32_t* cur = s_cursor + warp * experts;
-  for (int e = lane; e < experts; e += 32) cur[e] = csr[e] + seg_start[(int64_t)seg * experts + e];
+  int32_t* cur = s_cursor + warp * groups;
+  for (int e = lane; e < groups; e += 32) cur[e] = csr[e] + seg_start[(int64_t)seg * groups + e];
   __syncwarp();
   const int64_t begin = (int64_t)seg * seg_len;
   const int64_t end = min(positions, begin + seg_len);
@@ -341,7 +337,7 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
     for (int u = 0; u < kDispatchUnroll; ++u) {
       const int64_t p = base + 32 * u + lane;
       const bool live = p < end;
-      ev[u] = live ? clamp_expert(top_idx[p], experts) : -1;
+      ev[u] = live ? route_group(checked_expert(top_idx[p], experts), p / top_k, passes) : -1;
       gv[u] = (live && sorted_gate) ? gate[p] : (uint16_t)0;
     }
 #pragma unroll
@@ -380,30 +376,38 @@ static void dispatch_geometry(int64_t positions, int* seg_len, int* segments) {
   if (*segments == 0) *segments = 1;
 }
 
-size_t dispatch_workspace_bytes(int64_t tokens, int top_k, int experts) {
+// `groups`: routed experts x passes.
+size_t dispatch_workspace_bytes(int64_t tokens, int top_k, int groups) {
   int seg_len, segments;
   dispatch_geometry(tokens * top_k, &seg_len, &segments);
-  return (size_t)segments * experts * 8 + 256;
+  return (size_t)segments * groups * 8 + 256;
 }
 
+// With passes.n == 2 every per-expert output (offsets, csr, pcsr, the tile
+// tables, the global scales) is per group (route_group), 2 * experts of them.
 int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* row_amax, int64_t tokens, int top_k,
-                 int experts, void* workspace, size_t workspace_bytes, int64_t* order, int64_t* inverse,
+                 int experts, Passes passes, void* workspace, size_t workspace_bytes, int64_t* order, int64_t* inverse,
                  int64_t* tokens_out, int32_t* tokens32, uint16_t* sorted_gate, int32_t* offsets, int32_t* csr,
                  int32_t* pcsr, TileEntry* tiles, int max_tiles, int32_t* num_tiles, float* act_global,
                  uint32_t* act_amax_bits, cudaStream_t stream) {
-  if (experts <= 0 || experts > kMaxExperts) return set_error(PRAXIS_B200_EINVAL, "experts must be 1..%d", kMaxExperts);
+  if (passes.n != 1 && passes.n != 2) return set_error(PRAXIS_B200_EINVAL, "passes must be 1 or 2");
+  if (passes.n == 2 && (passes.t0 < 0 || passes.t0 > tokens))
+    return set_error(PRAXIS_B200_EINVAL, "pass 0 tokens %lld outside 0..%lld", (long long)passes.t0, (long long)tokens);
+  const int groups = experts * passes.n;
+  if (experts <= 0 || groups > kMaxExperts)
+    return set_error(PRAXIS_B200_EINVAL, "experts x passes must be 1..%d", kMaxExperts);
   if (top_k <= 0 || tokens < 0) return set_error(PRAXIS_B200_EINVAL, "bad tokens/top_k");
   if (tokens * top_k >= (int64_t)1 << 31) return set_error(PRAXIS_B200_EINVAL, "too many routed rows");
-  if (workspace_bytes < dispatch_workspace_bytes(tokens, top_k, experts))
+  if (workspace_bytes < dispatch_workspace_bytes(tokens, top_k, groups))
     return set_error(PRAXIS_B200_EINVAL, "dispatch workspace too small");
   const int64_t positions = tokens * top_k;
   int seg_len, segments;
   dispatch_geometry(positions, &seg_len, &segments);
   int32_t* seg_count = static_cast<int32_t*>(workspace);
-  uint32_t* seg_max = reinterpret_cast<uint32_t*>(seg_count + (size_t)segments * experts);
+  uint32_t* seg_max = reinterpret_cast<uint32_t*>(seg_count + (size_t)segments * groups);
   const int blocks = (segments + kDispatchWarps - 1) / kDispatchWarps;
-  const size_t smem_count = (size_t)2 * kDispatchWarps * experts * 4;
-  const size_t smem_scatter = (size_t)kDispatchWarps * experts * 4;
+  const size_t smem_count = (size_t)2 * kDispatchWarps * groups * 4;
+  const size_t smem_scatter = (size_t)kDispatchWarps * groups * 4;
   static DeviceOnce attr;
   int rc = device_once(attr, [](int dev) {
     cudaError_t e = cudaFuncSetAttribute(dispatch_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -417,17 +421,17 @@ int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* r
   });
   if (rc) return rc;
   launch_pdl(dispatch_count_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_count, stream, top_idx, row_amax,
-             positions, top_k, experts, seg_len, segments, seg_count, seg_max);
+             positions, top_k, experts, passes, groups, seg_len, segments, seg_count, seg_max);
   rc = check_launch("dispatch_count");
   if (rc) return rc;
-  launch_pdl(dispatch_scan_kernel, dim3(1), dim3(1024), 0, stream, seg_count, seg_max, segments, experts, positions,
+  launch_pdl(dispatch_scan_kernel, dim3(1), dim3(1024), 0, stream, seg_count, seg_max, segments, groups, positions,
              (int)kTileRows, offsets, csr, pcsr, tiles, max_tiles, num_tiles, row_amax ? act_global : nullptr,
              row_amax ? act_amax_bits : nullptr);
   rc = check_launch("dispatch_scan");
   if (rc) return rc;
   if (positions > 0) {
     launch_pdl(dispatch_scatter_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_scatter, stream, top_idx, gate,
-               positions, top_k, experts, seg_len, segments, seg_count, csr, order, inverse, tokens_out, tokens32,
+               positions, top_k, experts, passes, groups, seg_len, segments, seg_count, csr, order, inverse, tokens_out, tokens32,
                sorted_gate);
     rc = check_launch("dispatch_scatter");
   }

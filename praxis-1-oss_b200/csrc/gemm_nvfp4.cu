@@ -51,11 +51,14 @@ __device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&
     d[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
 }
 
-// Tile expert e reads weights e % weight_experts: one expert per tile on a
-// single GPU; with expert parallelism a tile's "expert" is a segment
-// (source rank, local expert) whose activation scales are its own.
+// Tile expert e reads weights (e / groups_per_weight) % weight_experts: one
+// expert per tile on a single GPU; with lockstep passes a tile's "expert" is
+// a group (expert, pass) = expert * passes + pass; with expert parallelism a
+// segment (source rank, local expert) = rank * local experts + expert. Either
+// way the group has activation scales of its own.
 __device__ __forceinline__ int weight_expert(const GemmParams& p, int e) {
-  return e < p.weight_experts ? e : e % p.weight_experts;
+  const int w = p.groups_per_weight > 1 ? e / p.groups_per_weight : e;
+  return w < p.weight_experts ? w : w % p.weight_experts;
 }
 
 __device__ __forceinline__ float expert_multiplier(const GemmParams& p, int e) {
@@ -868,7 +871,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
                      const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
-                     cudaStream_t stream, int sm_limit) {
+                     cudaStream_t stream, int sm_limit, int groups_per_weight) {
   if (n % 128 != 0 || k % 128 != 0 || n <= 0 || k <= 0)
     return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs N and K multiples of 128 (N=%d K=%d)", n, k);
   if (experts < 1) return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs at least one expert");
@@ -912,6 +915,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.amax_out = amax_out;
   p.max_tiles = max_tiles;
   p.weight_experts = experts;
+  p.groups_per_weight = groups_per_weight;
   p.sm_limit = sm_limit;
   const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
   if (n % 256 == 0 && (rep || gemm_variant() == 0)) {

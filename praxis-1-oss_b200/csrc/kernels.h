@@ -39,7 +39,8 @@ struct GemmParams {
   const uint32_t* act_amax;
   const float* w_global;
   uint32_t* amax_out;
-  int32_t weight_experts;  // tile expert e uses weights e % weight_experts
+  int32_t weight_experts;  // tile expert e uses weights (e / groups_per_weight) % weight_experts
+  int32_t groups_per_weight;
   int32_t sm_limit;        // launch on at most this many SMs (0: all); host side only
 };
 
@@ -145,6 +146,6 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
                      const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
-                     cudaStream_t stream, int sm_limit = 0);
+                     cudaStream_t stream, int sm_limit = 0, int groups_per_weight = 1);
 
 }  // namespace praxis

@@ -135,7 +135,7 @@ __device__ __forceinline__ float expert_global(const float* g, const uint32_t* a
 __global__ void __launch_bounds__(256) quantize_gather_kernel(
     const uint16_t* __restrict__ x, int64_t tokens, int k_dim, const int64_t* __restrict__ top_idx,
     const int64_t* __restrict__ inverse, const int32_t* __restrict__ csr, const int32_t* __restrict__ pcsr,
-    const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int top_k, int experts,
+    const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int top_k, int experts, Passes passes,
     const TileEntry* __restrict__ tiles, const int32_t* __restrict__ num_tiles, int token_blocks,
     uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
   pdl_wait();  // the previous kernel of the stream has completed
@@ -168,12 +168,7 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
   const int64_t t = (int64_t)blockIdx.x * 8 + warp;
   if (t >= tokens) return;
   if (lane < top_k) {
-    int64_t e64 = top_idx[t * top_k + lane];
-    int e = (int)e64;
-    if (e64 < 0 || e64 >= experts) {
-      record_error(kErrIndexRange);
-      e = e64 < 0 ? 0 : experts - 1;
-    }
+    const int e = route_group(checked_expert(top_idx[t * top_k + lane], experts), t, passes);
     const float g = expert_global(globals, amax_bits, e);
     s_dest[warp][lane] = (int64_t)pcsr[e] + inverse[t * top_k + lane] - csr[e];
     s_g[warp][lane] = g;
@@ -330,7 +325,7 @@ __global__ void replicate_scales_kernel(const uint4* __restrict__ sf, int64_t ch
 int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int64_t* top_idx, const int64_t* inverse,
                         const int32_t* csr, const int32_t* pcsr, const float* globals, const uint32_t* amax_bits,
                         int top_k, int experts, const TileEntry* tiles, const int32_t* num_tiles, int max_tiles,
-                        uint8_t* q, uint8_t* sf, int sf_layout, cudaStream_t stream) {
+                        uint8_t* q, uint8_t* sf, int sf_layout, cudaStream_t stream, Passes passes) {
   if (k_dim % 64 != 0) return set_error(PRAXIS_B200_EINVAL, "quantize needs K % 64 == 0");
   if (top_k < 1 || top_k > 8) return set_error(PRAXIS_B200_EINVAL, "top_k must be 1..8");
   if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
@@ -340,7 +335,7 @@ int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int6
   const int grid = token_blocks + max_tiles;
   if (grid == 0) return PRAXIS_B200_OK;
   launch_pdl(quantize_gather_kernel, dim3(grid), dim3(256), 0, stream, x, tokens, k_dim, top_idx, inverse, csr, pcsr,
-             globals, amax_bits, top_k, experts, tiles, num_tiles, token_blocks, q, sf,
+             globals, amax_bits, top_k, experts, passes, tiles, num_tiles, token_blocks, q, sf,
              sf_layout == PRAXIS_B200_SF_REPLICATED);
   return check_launch("quantize_gather");
 }

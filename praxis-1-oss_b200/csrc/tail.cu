@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(256) combine_tail_kernel(
     const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate, const int32_t* __restrict__ csr,
     const int32_t* __restrict__ pcsr, const float* __restrict__ h_global, const uint32_t* __restrict__ h_amax,
     const float* __restrict__ w_global, int rows_rescaled, float scaling, const uint16_t* __restrict__ shared,
-    TailArgs tail, int64_t tokens, int top_k, int experts) {
+    TailArgs tail, int64_t tokens, int top_k, int experts, Passes passes) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
   __shared__ int64_t s_src[8][8];
@@ -69,17 +69,12 @@ __global__ void __launch_bounds__(256) combine_tail_kernel(
   if (t >= tokens) return;
   if (lane < top_k) {
     const int64_t p = t * top_k + lane;
-    int64_t e64 = top_idx[p];
-    int e = (int)e64;
-    if (e64 < 0 || e64 >= experts) {
-      record_error(kErrIndexRange);
-      e = e64 < 0 ? 0 : experts - 1;
-    }
-    s_src[warp][lane] = (int64_t)pcsr[e] + inverse[p] - csr[e];
+    const int e = checked_expert(top_idx[p], experts), g = route_group(e, t, passes);
+    s_src[warp][lane] = (int64_t)pcsr[g] + inverse[p] - csr[g];
     s_scale[warp][lane] = mul_rn(bf16_to_f32(gate[p]), scaling);
     float mult = 1.0f;
     if (!rows_rescaled) {
-      const float gh = h_global != nullptr ? h_global[e] : global_from_amax_bits(h_amax[e]);
+      const float gh = h_global != nullptr ? h_global[g] : global_from_amax_bits(h_amax[g]);
       mult = bf16_round(mul_rn(gh, w_global[e]));
     }
     s_mult[warp][lane] = mult;
@@ -200,7 +195,7 @@ int run_combine_tail(const uint16_t* rows, int cols, const int64_t* inverse, con
                      const uint16_t* gate, const int32_t* csr, const int32_t* pcsr, const float* h_global,
                      const uint32_t* h_amax, const float* w_global, int rows_rescaled, float scaling,
                      const uint16_t* shared, const TailArgs& tail, int64_t tokens, int top_k, int experts,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, Passes passes) {
   if (cols % 4 != 0 || cols <= 0) return set_error(PRAXIS_B200_EINVAL, "combine_tail needs C %% 4 == 0");
   if (top_k < 1 || top_k > 8) return set_error(PRAXIS_B200_EINVAL, "top_k must be 1..8");
   if (!rows_rescaled && (w_global == nullptr || (h_global == nullptr && h_amax == nullptr)))
@@ -224,7 +219,7 @@ int run_combine_tail(const uint16_t* rows, int cols, const int64_t* inverse, con
 #define PRAXIS_TAIL(KMAX, NORM, MOD)                                                                               \
   launch_pdl(combine_tail_kernel<KMAX, NORM, MOD>, dim3((unsigned)blocks), dim3(256), 0, stream, rows, cols,       \
              inverse, top_idx, gate, csr, pcsr, h_global, h_amax, w_global, rows_rescaled, scaling, shared, tail,  \
-             tokens, top_k, experts)
+             tokens, top_k, experts, passes)
 #define PRAXIS_TAIL_K(NORM, MOD)          \
   if (top_k <= 2) PRAXIS_TAIL(2, NORM, MOD);      \
   else if (top_k <= 4) PRAXIS_TAIL(4, NORM, MOD); \

@@ -47,8 +47,11 @@ class SharedExpert(nn.Module):
         self.gate_up = nn.Parameter(torch.empty(dim, 2 * hidden))
         self.down = nn.Parameter(torch.empty(hidden, dim))
 
-    def forward(self, x: Tensor) -> Tensor:
+    def forward(self, x: Tensor, out: Tensor | None = None) -> Tensor:
+        """``out``: a [rows, C] destination for 2-D ``x`` (the same GEMM)."""
         gate, up = (x @ self.gate_up).chunk(2, dim=-1)
+        if out is not None:
+            return torch.mm(F.silu(gate) * up, self.down, out=out)
         return (F.silu(gate) * up) @ self.down
 
 
@@ -213,6 +216,48 @@ class B200MoEFeedForward(nn.Module):
             xo, h = routed_forward_tail(self.routed, x_flat, top_idx, gate, scaling=self.routed_scaling_factor,
                                         chunk_size=chunk, tail=tail, shared=y_shared)
         return xo.reshape(shape), None if h is None else h.reshape(shape)
+
+    @torch.no_grad()
+    def forward_pair(self, xs) -> list[Tensor]:
+        """``[self(x) for x in xs]`` with one routed-expert pass for both
+        inputs of a classifier-free-guidance pair (``MoEFeedForward.forward_pair``,
+        praxis/layers.py:1779-1853): the router and the gates run on both
+        inputs' rows at once (row-wise kernels, so each row's bits are those
+        of its own call), the shared expert per input, and the routed bank's
+        ``routed_forward_pair`` sends both inputs' routed rows through the
+        expert GEMMs once, grouped per (expert, input) so that every output
+        has the bits of ``forward``. Falls back to one forward per input where
+        the pair does not apply (the reference's conditions: two inputs, each
+        one dispatch chunk, no routing hook)."""
+        xs = list(xs)
+        if self.routed is None:
+            raise RuntimeError("routed experts are not set (set_routed_weights / from_reference)")
+        flats = [x.reshape(-1, x.size(-1)) for x in xs]
+        chunk = self.dispatch_chunk_size
+        if (
+            len(xs) != 2
+            or self.routing_hook is not None
+            or any(not f.is_cuda or f.dtype != torch.bfloat16 or f.device != flats[0].device for f in flats)
+            or any(not 0 < f.shape[0] <= (chunk or f.shape[0]) for f in flats)
+        ):
+            return [self(x) for x in xs]
+        from .bank import _adjacent
+
+        flats = [f.contiguous() for f in flats]
+        t0 = flats[0].shape[0]
+        x = _adjacent(flats)
+        top_idx, gate = self.route(x)
+        shared = None
+        if self.shared is not None:
+            y_sh = torch.empty_like(x)
+            self.shared(flats[0], out=y_sh[:t0])
+            self.shared(flats[1], out=y_sh[t0:])
+            shared = [y_sh[:t0], y_sh[t0:]]
+        with _Range("routed"):
+            ys = self.routed.routed_forward_pair(
+                [x[:t0], x[t0:]], [top_idx[:t0], top_idx[t0:]], [gate[:t0], gate[t0:]],
+                scaling=self.routed_scaling_factor, shared=shared)
+        return [y.reshape(xi.shape) for y, xi in zip(ys, xs, strict=True)]
 
     @torch.no_grad()
     def forward(self, x: Tensor, *, router_rows: tuple[int, int, int] | None = None) -> Tensor:

@@ -121,21 +121,39 @@ def row_amax(x: Tensor) -> Tensor:
     return out
 
 
+def _passes(rows, t: int) -> tuple[int, int]:
+    """(passes, tokens of pass 0) of the reference's ``rows`` tuple: one input
+    (``(T,)`` or None) or a lockstep pair ``(T0, T1)``."""
+    if rows is None:
+        return 1, 0
+    rows = tuple(int(r) for r in rows)
+    if len(rows) not in (1, 2) or sum(rows) != t or min(rows) < 0:
+        raise ValueError(f"rows {rows}: one or two inputs whose tokens add up to {t}")
+    return (2, rows[0]) if len(rows) == 2 else (1, 0)
+
+
 def dispatch(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | None = None,
-             full: bool = True) -> Routing:
+             full: bool = True, rows: tuple | None = None) -> Routing:
     """``_dispatch_rows`` + inverse + padded CSR + tile table (+ activation
-    global scales from ``amax``) on the device."""
+    global scales from ``amax``) on the device. ``rows = (T0, T1)``: the
+    tokens are a lockstep pair (praxis/kernels/router_fused.py:820-852, P =
+    2); csr / pcsr / tiles / globals are then per (expert, input) group
+    2 e + s, ``seg_csr`` is the reference's and ``offsets`` its per-expert
+    end offsets."""
     _need(top_idx, "top_idx", torch.int64, 2)
     _need(gate, "gate", BF16, 2, top_idx.device)
     if gate.shape != top_idx.shape:
         raise ValueError("gate / top_idx shape mismatch")
     t, k = top_idx.shape
+    npass, t0 = _passes(rows, t)
     dev = top_idx.device
     r = t * k
     e = num_experts
-    max_tiles = padded_rows(r, e) // 128
+    g = e * npass
+    max_tiles = padded_rows(r, g) // 128
     lib = capi.load()
-    ws = torch.empty(int(lib.praxis_b200_dispatch_workspace_size(t, k, e)), dtype=torch.uint8, device=dev)
+    ws = torch.empty(int(lib.praxis_b200_dispatch_passes_workspace_size(t, k, e, npass)), dtype=torch.uint8,
+                     device=dev)
     i64 = dict(dtype=torch.int64, device=dev)
     i32 = dict(dtype=torch.int32, device=dev)
     order = torch.empty(r, **i64) if full else None
@@ -143,22 +161,24 @@ def dispatch(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | Non
     tokens = torch.empty(r, **i64) if full else None
     tokens32 = torch.empty(r, **i32) if full else None
     sorted_gate = torch.empty(r, dtype=BF16, device=dev) if full else None
-    offsets = torch.empty(e, **i32)
-    csr = torch.empty(e + 1, **i32)
-    pcsr = torch.empty(e + 1, **i32)
+    offsets = torch.empty(g, **i32)
+    csr = torch.empty(g + 1, **i32)
+    pcsr = torch.empty(g + 1, **i32)
     tiles = torch.empty(2 * max(max_tiles, 1), 4, **i32)  # 128-row tiles, then 256-row pairs
     num_tiles = torch.empty(2, **i32)
     act_global = act_amax = None
     if amax is not None:
         _need(amax, "row amax", BF16, 1, dev)
-        act_global = torch.empty(e, dtype=torch.float32, device=dev)
-        act_amax = torch.empty(e, dtype=torch.int32, device=dev)
-    capi.check(lib.praxis_b200_dispatch(
-        _p(top_idx), _p(gate), _p(amax), t, k, e, _p(ws), ws.numel(), _p(order), _p(inverse), _p(tokens),
-        _p(tokens32), _p(sorted_gate), _p(offsets), _p(csr), _p(pcsr), _p(tiles), max_tiles, _p(num_tiles),
-        _p(act_global), _p(act_amax), _dev(top_idx), _stream(top_idx)))
-    return Routing(top_idx, gate, order, inverse, sorted_gate, tokens, tokens32, csr, offsets, (t,), csr, pcsr,
-                   tiles, num_tiles, act_global, act_amax)
+        act_global = torch.empty(g, dtype=torch.float32, device=dev)
+        act_amax = torch.empty(g, dtype=torch.int32, device=dev)
+    capi.check(lib.praxis_b200_dispatch_passes(
+        _p(top_idx), _p(gate), _p(amax), t, k, e, npass, t0, _p(ws), ws.numel(), _p(order), _p(inverse),
+        _p(tokens), _p(tokens32), _p(sorted_gate), _p(offsets), _p(csr), _p(pcsr), _p(tiles), max_tiles,
+        _p(num_tiles), _p(act_global), _p(act_amax), _dev(top_idx), _stream(top_idx)))
+    rows_t = (t,) if npass == 1 else (t0, t - t0)
+    return Routing(top_idx, gate, order, inverse, sorted_gate, tokens, tokens32, csr,
+                   offsets if npass == 1 else offsets[1::2], rows_t, csr, pcsr, tiles, num_tiles, act_global,
+                   act_amax)
 
 
 def dispatch_noalloc(top_idx: Tensor, gate: Tensor, num_experts: int, amax: Tensor | None = None, *,
@@ -221,11 +241,11 @@ def _check_dispatch_outputs(t: int, k: int, e: int, device, amax: Tensor | None,
 def route_dispatch(logits: Tensor, bias: Tensor, rows: tuple, top_k: int = 8,
                    activation: str = "sigmoid") -> Routing:
     """``router_fused.route_dispatch`` (praxis/kernels/router_fused.py:738)
-    for one input (P = 1), any E <= 256 and k <= 8."""
-    if len(rows) != 1 or rows[0] != logits.shape[0]:
-        raise ValueError("route_dispatch here takes one input (rows == (T,))")
+    for one input (``rows = (T,)``) or a lockstep pair (``rows = (T0, T1)``,
+    the reference's P = 2), any E <= 256 and k <= 8."""
+    _passes(rows, logits.shape[0])
     top_idx, gate = route(logits, bias, top_k, activation)
-    return dispatch(top_idx, gate, logits.shape[1])
+    return dispatch(top_idx, gate, logits.shape[1], rows=rows)
 
 
 def _sf_buffer(rows: int, kdim: int, sf_layout: int, device) -> Tensor:
@@ -522,14 +542,18 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
                 shared: Tensor | None = None, *, router_terms: Tensor | None = None,
                 router_bias: Tensor | None = None, top_k: int | None = None, activation: str = "sigmoid",
                 out: Tensor | None = None, gate_up_sf_layout: int | None = None,
-                down_sf_layout: int | None = None, tail: Tail | None = None, tail_out: tuple | None = None):
+                down_sf_layout: int | None = None, tail: Tail | None = None, tail_out: tuple | None = None,
+                rows: tuple | None = None):
     """One dispatch chunk through ``praxis_b200_moe_forward``. With
     ``router_terms`` the router runs too and (out, top_idx, gate) is returned.
     ``gate_up_q/sf`` are in the interleaved kernel layout; the weight scales
     are compact or replicated (``*_sf_layout``, else told by their size).
     With ``tail`` the combine is fused into what follows the layer
     (:func:`combine_tail`) and ``(new residual, normed rows or None)`` takes
-    the place of ``out`` (written into ``tail_out`` when given)."""
+    the place of ``out`` (written into ``tail_out`` when given).
+    ``rows = (T0, T1)``: x holds a lockstep pair of inputs back to back (the
+    reference's forward_pair); one pass of the expert GEMMs serves both and
+    every output row has the bits of its input run alone."""
     _need(x, "x", BF16, 2)
     t, c = x.shape
     e, c_half_f, _ = down_q.shape
@@ -551,8 +575,9 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         gate_up_sf_layout = _layout_of(gate_up_sf, gate_up_q, "gate_up_sf")
     if down_sf_layout is None:
         down_sf_layout = _layout_of(down_sf, down_q, "down_sf")
+    npass, t0 = _passes(rows, t)
     lib = capi.load()
-    ws_size = int(lib.praxis_b200_moe_workspace_size(t, k, e, c, f, int(router_terms is not None)))
+    ws_size = int(lib.praxis_b200_moe_workspace_size(t, k, e, c, f, int(router_terms is not None), npass))
     ws = torch.empty(ws_size, dtype=torch.uint8, device=dev)
     args = capi.MoeArgs(
         x=x.data_ptr(), router_weight=None if router_terms is None else router_terms.data_ptr(),
@@ -566,7 +591,7 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         gate_up_sf_layout=int(gate_up_sf_layout), down_sf_layout=int(down_sf_layout), tokens=t, dim=c, hidden=f, experts=e, top_k=k, scaling=float(scaling),
         workspace=ws.data_ptr(), workspace_size=ws_size, device=_dev(x),
         stream=torch.cuda.current_stream(dev).cuda_stream,
-        tail=None if st is None else C.addressof(st),
+        tail=None if st is None else C.addressof(st), passes=npass, pass0_tokens=t0,
     )
     capi.check(lib.praxis_b200_moe_forward(C.byref(args)))
     res = (out,) if tail is None else (residual_out, normed)

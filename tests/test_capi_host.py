@@ -43,11 +43,16 @@ def test_library_is_built_for_sm100a_only():
 
 
 def test_host_helpers(lib):
-    assert lib.praxis_b200_abi_version() == 1
+    assert lib.praxis_b200_abi_version() == pkg().capi.ABI_VERSION == 2
     assert lib.praxis_b200_padded_rows(65536, 64) == (65536 + 127 * 64) // 128 * 128
     assert pkg().ops.padded_rows(512, 8) == lib.praxis_b200_padded_rows(512, 8)
-    ws = lib.praxis_b200_moe_workspace_size(16384, 4, 64, 3072, 1536, 1)
+    ws = lib.praxis_b200_moe_workspace_size(16384, 4, 64, 3072, 1536, 1, 1)
     assert ws > 16384 * 4 * 3072 * 2  # holds the routed output rows
+    # a lockstep pair pads every (expert, input) group on its own
+    ws2 = lib.praxis_b200_moe_workspace_size(16384, 4, 64, 3072, 1536, 1, 2)
+    assert ws2 > ws
+    assert lib.praxis_b200_dispatch_passes_workspace_size(16384, 4, 64, 2) == \
+        lib.praxis_b200_dispatch_workspace_size(16384, 4, 128)
 
 
 def test_argument_errors_before_launch(lib):

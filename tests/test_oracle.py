@@ -232,3 +232,22 @@ def test_modulation_fused_and_unfused_agree():
     assert torch.equal(prod.double(), xo.double() * sc1.double())
     out = O.tail_modulate(xo, mod, torch.arange(64))
     assert torch.equal(out, (prod + mod[:, :256].float()).to(torch.bfloat16))
+
+
+def test_dispatch_passes_one_input_is_the_dispatch():
+    """dispatch_passes with one input is the single-input dispatch, and for a
+    pair its order is that of the concatenated input (a stable sort by
+    expert puts pass 0's rows first inside every expert), only the segment
+    offsets split per pass."""
+    g = torch.Generator().manual_seed(4)
+    top = torch.randint(0, 16, (300, 4), generator=g)
+    gate = torch.rand(300, 4, generator=g).to(torch.bfloat16)
+    o1, i1, t1, sg1, off1, csr1 = O.dispatch(top, gate, 16)
+    o, i, t, sg, seg, off = O.dispatch_passes(top, gate, 16, (300,))
+    assert torch.equal(o, o1) and torch.equal(i, i1) and torch.equal(t, t1) and torch.equal(sg, sg1)
+    assert torch.equal(seg, csr1) and torch.equal(off, off1)
+    o2, i2, t2, sg2, seg2, off2 = O.dispatch_passes(top, gate, 16, (120, 180))
+    assert torch.equal(o2, o1) and torch.equal(i2, i1) and torch.equal(off2, off1)
+    assert seg2.numel() == 33 and torch.equal(seg2[::2], csr1)
+    pass0 = torch.bincount(top[:120].reshape(-1), minlength=16)
+    assert torch.equal((seg2[1::2] - seg2[:-1:2]).long(), pass0)

@@ -110,6 +110,9 @@ def parse():
     ap.add_argument("--flashinfer", action="store_true",
                     help="also time FlashInfer's block-scaled grouped GEMM (the kernel the reference calls) on the "
                          "same operands (N = 1)")
+    ap.add_argument("--router-fused", action="store_true",
+                    help="also time the reference's own router_fused.route_dispatch (CuTe DSL, E=128/top-8) from the "
+                         "offline reference install under baseline/_ref against this library's routing (N = 1)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override the config's token count (small profiling cases)")
     return ap.parse_args()
@@ -505,6 +508,8 @@ def run_b200(args, cfg):
         extra = extra_configs(pkg, L, args, dev)
     if args.flashinfer:
         extra["flashinfer_gemm"] = flashinfer_gemm(pkg, L, x, cfg, stages)
+    if args.router_fused:
+        extra["router_fused_reference"] = router_fused_head_to_head(pkg, dev)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
@@ -607,6 +612,62 @@ def flashinfer_gemm(pkg, L, x, cfg, stages):
     return res
 
 
+def router_fused_head_to_head(pkg, dev, tokens=16384, dim=3072, experts=128, top_k=8):
+    """The reference's sm_100 routing path at its own shape (E=128, top-8):
+    the stock fp32 router GEMM (``F.linear(x.float(), W.float())``,
+    praxis/layers.py:1104-1122) and ``router_fused.route_dispatch``
+    (praxis/kernels/router_fused.py:738-804, CuTe DSL) from the offline
+    reference install, against this library's logits kernel and its route +
+    dispatch kernels; P = 1 and the CFG pair P = 2. Also the bitwise
+    agreement of the two routings on the reference's logits."""
+    import sys
+
+    import torch
+    import torch.nn.functional as F
+
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "praxis" / "kernels" / "router_fused.py").is_file():
+        return {"unavailable": "the reference install (baseline/_ref) is absent"}
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    try:
+        import cutlass.cute  # noqa: F401
+        from praxis.kernels import router_fused as rf
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"router_fused not importable: {type(exc).__name__}: {exc}"[:200]}
+    try:  # the kernel imports more of the DSL when it is first compiled
+        rf.route_dispatch(torch.zeros(64, experts, device=dev), torch.zeros(experts, device=dev), (64,))
+    except ImportError as exc:
+        return {"unavailable": f"router_fused does not build with this image's CUTLASS DSL: {exc}"[:200]}
+    ops = pkg.ops
+    g = torch.Generator(device=dev).manual_seed(77)
+    x = torch.randn(tokens, dim, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(experts, dim, generator=g, device=dev) * 0.02)
+    bias = (torch.randn(experts, generator=g, device=dev) * 0.05).float()
+    terms = ops.split_router_weight(w)
+    res = {"workload": f"T={tokens}, C={dim}, E={experts}, top-{top_k}", "reps": 20}
+    try:
+        for name, rows in (("single", (tokens,)), ("pair", (tokens // 2, tokens - tokens // 2))):
+            logits = F.linear(x.float(), w.float())
+            ref_ms = time_steps(lambda: rf.route_dispatch(logits, bias, rows), dev, 20, 3)
+            ours_ms = time_steps(lambda: ops.route_dispatch(logits, bias, rows, top_k=top_k), dev, 20, 3)
+            a, b = rf.route_dispatch(logits, bias, rows), ops.route_dispatch(logits, bias, rows, top_k=top_k)
+            same = all(torch.equal(getattr(a, n), getattr(b, n)) for n in
+                       ("top_idx", "gate", "order", "inverse", "sorted_gate", "tokens", "tokens32", "seg_csr"))
+            same = same and torch.equal(a.offsets, b.offsets.contiguous())
+            res[name] = {"route_dispatch_reference_ms": ref_ms, "route_dispatch_b200_ms": ours_ms,
+                         "speedup": ref_ms / ours_ms, "bit_exact": bool(same)}
+        sgemm_ms = time_steps(lambda: F.linear(x.float(), w.float()), dev, 20, 3)
+        logits_ms = time_steps(lambda: ops.router_logits(x, terms), dev, 20, 3)
+        res["router_logits"] = {"reference_fp32_gemm_ms": sgemm_ms, "b200_ms": logits_ms,
+                                "speedup": sgemm_ms / logits_ms}
+        res["total_speedup"] = (sgemm_ms + res["single"]["route_dispatch_reference_ms"]) / (
+            logits_ms + res["single"]["route_dispatch_b200_ms"])
+    except Exception as exc:  # noqa: BLE001
+        res["failed"] = f"{type(exc).__name__}: {exc}"[:300]
+    return res
+
+
 def cpu_leg_with_parity(L, cfg, gpu_res):
     """The CPU baseline on the GPU arm's own packed weights and inputs, and
     the parity of the GPU results with it: routing on the GPU's logits
@@ -676,7 +737,83 @@ def extra_configs(pkg, L, args, dev):
     y5 = torch.empty_like(x5)
     lat = graph_latency(lambda: L5["layer"](x5, y5), dev, calls=max(20, args.steps * 2))
     out["config5_graph_latency"] = dict(lat, workload="BASELINE config 5: T=512, C=1024, E=32, k=2, F=2048")
+    del L5, x5, y5
+    out["tail_fusion"] = tail_fusion(pkg, L, dev, steps)
+    out["checkpoint_pair"] = checkpoint_pair(pkg, dev, steps)
     return out
+
+
+def tail_fusion(pkg, L, dev, steps):
+    """Config 2 with the MoE tail fused into the next block's residual add +
+    RMSNorm (praxis.layers.MOE_TAIL_NORM, praxis/kernels/moe_tail_triton.py:
+    329-352) against the layer followed by the reference's eager residual add
+    and norm (praxis/layers.py:214-224); the two must give the same bits."""
+    import torch
+    import torch.nn.functional as F
+
+    x = L["x_cpu"].to(dev)
+    t, c = x.shape
+    g = torch.Generator(device=dev).manual_seed(5)
+    resid = torch.randn(t, c, generator=g, device=dev).to(torch.bfloat16)
+    w1 = (1 + torch.randn(c, generator=g, device=dev) * 0.1).float()
+    s_bf16 = torch.tensor(0.75, dtype=torch.bfloat16, device=dev)
+    y = torch.empty_like(x)
+    tail = pkg.ops.Tail(resid, w1, 1e-6, 0.75)
+    bank, kw, mod = L["bank"], L["kw"], L["mod"]
+
+    def fused():
+        return pkg.ops.moe_forward(x, None, None, kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q,
+                                   kw.down_sf, bank.down_global, 2.5, router_terms=L["terms"],
+                                   router_bias=mod.expert_bias, top_k=mod.top_k, tail=tail,
+                                   gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout)
+
+    def unfused():
+        L["layer"](x, y)
+        xo = resid + y
+        return xo, F.rms_norm(xo.float(), (c,), weight=w1, eps=1e-6).to(torch.bfloat16) * s_bf16
+
+    xo_f, h_f, _, _ = fused()
+    xo_u, h_u = unfused()
+    same = bool(torch.equal(xo_f, xo_u) and torch.equal(h_f, h_u))
+    ms_f = time_steps(fused, dev, steps, 3)
+    ms_u = time_steps(unfused, dev, steps, 3)
+    return {"workload": "config 2 + the next block's residual add and RMSNorm (C=3072)",
+            "fused_ms": ms_f, "unfused_eager_ms": ms_u, "saved_ms": ms_u - ms_f, "bit_exact": same,
+            "steps": steps}
+
+
+def checkpoint_pair(pkg, dev, steps):
+    """The released checkpoint's MoE shape (E=128, top-8, C=3072, F=1280) as
+    a classifier-free-guidance pair of two 8,192-token inputs: one routed
+    pass for both (forward_pair, praxis/layers.py:1779-1853) against one
+    forward per input (what the reference runs on B200: its NVFP4 pair path
+    is SM 11.0 only); the pair must give each input's bits."""
+    import torch
+
+    ck = CONFIGS["ckpt"]
+    Lc = build_layer(pkg, ck, 1006, dev)
+    x = Lc["x_cpu"].to(dev)
+    t = x.shape[0]
+    t0 = t // 2
+    bank, kw, mod = Lc["bank"], Lc["kw"], Lc["mod"]
+    args = (kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global, bank.down_q, kw.down_sf, bank.down_global, 2.5)
+    kwargs = dict(router_terms=Lc["terms"], router_bias=mod.expert_bias, top_k=ck["top_k"],
+                  gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout)
+
+    def pair():
+        return pkg.ops.moe_forward(x, None, None, *args, rows=(t0, t - t0), **kwargs)
+
+    def separate():
+        return [pkg.ops.moe_forward(x[a:b], None, None, *args, **kwargs) for a, b in ((0, t0), (t0, t))]
+
+    yp = pair()[0]
+    ys = separate()
+    same = bool(torch.equal(yp[:t0], ys[0][0]) and torch.equal(yp[t0:], ys[1][0]))
+    ms_p = time_steps(pair, dev, steps, 3)
+    ms_s = time_steps(separate, dev, steps, 3)
+    return {"workload": f"checkpoint shape E=128, top-8, C=3072, F=1280; CFG pair of 2 x {t0} tokens",
+            "pair_ms": ms_p, "separate_ms": ms_s, "speedup": ms_s / ms_p, "bit_exact_vs_separate": same,
+            "value": t / (ms_p / 1e3), "unit": "tokens/s", "steps": steps}
 
 
 def run_expert_parallel(args, cfg):

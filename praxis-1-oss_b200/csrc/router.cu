@@ -81,12 +81,12 @@ __global__ void __launch_bounds__(192, 1) router_logits_kernel(
         if (!mbar_wait(&empty[stage], phase ^ 1u, kErrTimeoutProducer)) break;
         uint8_t* st = smem + (size_t)stage * stage_bytes;
         mbar_arrive_expect_tx(&full[stage], (uint32_t)stage_bytes);
-        // CTAs start at different slabs, so they do not all read the same
-        // weight lines at the same time (the sum order is any order anyway)
-        const int slab = (kt + (int)blockIdx.x) % ktiles;
-        tma_load_2d(st, &tmap_x, &full[stage], slab * kRouterBK, (int32_t)row0);
+        // every CTA walks the columns in the same order, so a token's logits
+        // do not depend on where its row sits in the call (a lockstep pair,
+        // a router_rows slice and a lone call give the same bits)
+        tma_load_2d(st, &tmap_x, &full[stage], kt * kRouterBK, (int32_t)row0);
         for (int s = 0; s < splits; ++s)
-          tma_load_2d(st + kRouterABytes + s * e_pad * 128, &tmap_w, &full[stage], slab * kRouterBK, s * experts);
+          tma_load_2d(st + kRouterABytes + s * e_pad * 128, &tmap_w, &full[stage], kt * kRouterBK, s * experts);
         if (++stage == (uint32_t)stages) {
           stage = 0;
           phase ^= 1u;

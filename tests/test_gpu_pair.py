@@ -141,10 +141,23 @@ def test_routed_forward_pair_with_tail(P):
         assert_bytes_equal(out[i][1], want[1])
 
 
-def test_moe_forward_pair_with_router(P):
+def test_router_logits_do_not_depend_on_row_position(P):
+    """A token's logits are the same wherever its row sits in the call: what
+    lets a pair, a router_rows slice and a lone call route alike."""
+    g = torch.Generator().manual_seed(41)
+    x = torch.randn(1000, 3072, generator=g).to(torch.bfloat16).to(DEV)
+    terms = P.ops.split_router_weight((torch.randn(128, 3072, generator=g) * 0.02).to(DEV))
+    full, amax = P.ops.router_logits(x, terms)
+    for a, b in ((0, 1000), (5, 600), (128, 1000), (777, 778), (300, 428)):
+        part, pamax = P.ops.router_logits(x[a:b], terms)
+        assert_bytes_equal(part, full[a:b])
+        assert_bytes_equal(pamax, amax[a:b])
+
+
+@pytest.mark.parametrize("t0,t1,c,e,k,f", [(384, 128, 512, 32, 4, 256), (2048, 2048, 1024, 128, 8, 512)])
+def test_moe_forward_pair_with_router(P, t0, t1, c, e, k, f):
     """The whole chunk with the router inside (one C call for both inputs)
     against the same call per input."""
-    t0, t1, c, e, k, f = 384, 128, 512, 32, 4, 256
     bank, _, _ = _bank(P, e, c, f, seed=21)
     kw = bank.kernel_weights()
     g = torch.Generator().manual_seed(22)

@@ -74,11 +74,13 @@ def zipf_selection_bias(experts: int, beta: float = ZIPF_BETA, seed: int = 0):
     return beta * (logp - torch.logsumexp(logp, 0))
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate/up GEMM
-# launch, from one single-pass ncu capture of the full-size bench workload:
-#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
-#       --clock-control none -k regex:gemm_nvfp4_pair -s 5 -c 5 python bench.py --steps 2 --warmup 3
-# (read 616,229,120 + write 194,864,384 at config 2, 16384 tokens).
-GEMM1_TRAFFIC = {("2", 16384): 616229120 + 194864384}
+# launch at the full config-2 workload, from a capture of those two metrics
+# alone (one pass, as ncu reported for the same metrics on a 2,048-token case):
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
+#       -k regex:gemm_nvfp4_pair_kernel -c 1
+#       python bench.py --steps 1 --warmup 1 --no-e2e --no-cpu-baseline --no-extra
+# (read 462,110,976 + write 193,003,520 at config 2, 16384 tokens; compact scales).
+GEMM1_TRAFFIC = {("2", 16384): 462110976 + 193003520}
 
 
 def gemm1_bytes(t, k, c, f, e):

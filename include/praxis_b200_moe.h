@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define PRAXIS_B200_ABI_VERSION 2
+#define PRAXIS_B200_ABI_VERSION 3
 
 enum {
   PRAXIS_B200_OK = 0,
@@ -190,6 +190,23 @@ int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q,
                              void* out, const float* act_global, const uint32_t* act_amax, const float* w_global,
                              uint32_t* amax_out, int32_t sf_layout, int device, void* stream);
 
+/* The gate/up GEMM with SwiGLU and NVFP4 output at a calibrated hidden
+ * global scale (SetFusedSwiglu / FC1 FP4 output): the hidden values of
+ * EPI_SWIGLU (the same bits) are quantized in the epilogue with the frozen
+ * global `hidden_global` by the reference's recipe (E2M1 codes, UE4M3 scale
+ * per 16, compact 128x4 scale atoms) into q_out [Rp, N/4] and sf_out
+ * [Rp, N/32]; the bf16 hidden rows, their per-expert maxima and the hidden
+ * quantize pass are not needed. Replaces praxis/kernels/nvfp4_swiglu.py:40-74
+ * (gate_up_fp4, a FlashInfer act-fusion kernel whose bits are not
+ * available here: this entry computes the hidden quantize recipe of
+ * praxis/kernels/nvfp4.py:197-254 at the frozen global on the EPI_SWIGLU
+ * hidden values). N % 256 == 0, compact scales; outputs 16-byte aligned. */
+int praxis_b200_gemm_swiglu_fp4(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf,
+                                const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles,
+                                int64_t rows_padded, int32_t n, int32_t k, int32_t experts, const float* act_global,
+                                const uint32_t* act_amax, const float* w_global, float hidden_global, void* q_out,
+                                void* sf_out, int device, void* stream);
+
 /* Copies compact scales sf [rows, k/16] (the reference's swizzled layout)
  * into the replicated GEMM layout out [4 * rows * k/16]: group_rows = 128 for
  * activations, 256 for weights (rows = E * N, N % 256 == 0). rows % group_rows
@@ -319,6 +336,11 @@ typedef struct praxis_b200_moe_args {
    * (MoEFeedForward.forward_pair, praxis/layers.py:1779-1853). */
   int32_t passes;
   int64_t pass0_tokens;
+  /* > 0: the calibrated FC1 output scale (praxis_b200_gemm_swiglu_fp4): the
+   * gate/up GEMM writes FP4 hidden rows at this frozen global, which is also
+   * the down GEMM's activation global (NVFP4RoutedExperts.set_fused_swiglu_scale,
+   * praxis/quantization/nvfp4.py:235-260, :327-339). 0: dynamic globals. */
+  float fc1_output_scale;
 } praxis_b200_moe_args;
 
 size_t praxis_b200_moe_workspace_size(int64_t tokens, int32_t top_k, int32_t experts, int32_t dim, int32_t hidden,

@@ -666,9 +666,13 @@ def tail_add_norm_scale(y: torch.Tensor, x: torch.Tensor, w1: torch.Tensor, eps:
 # ---------------------------------------------------------------------------
 # The routed bank forward
 # ---------------------------------------------------------------------------
-def expert_outputs(x, tokens, offsets, bank, trace=None):
+def expert_outputs(x, tokens, offsets, bank, trace=None, hidden_global=None):
     """``_expert_outputs(raw_output=True)`` on SM100
-    (praxis/quantization/nvfp4.py:291-388): returns raw, csr, pcsr, g_h."""
+    (praxis/quantization/nvfp4.py:291-388): returns raw, csr, pcsr, g_h.
+    ``hidden_global``: a calibrated FC1 output scale (the
+    ``set_fused_swiglu_scale`` path, :327-339): the hidden rows are
+    quantized at this frozen global for every expert, which the combine's
+    rescale then uses."""
     e = bank["gate_up_q"].shape[0]
     c = x.shape[1]
     f = bank["down_q"].shape[2] * 2
@@ -680,7 +684,10 @@ def expert_outputs(x, tokens, offsets, bank, trace=None):
     aq, asf = quantize_activations(x, csr, pcsr, prows, ag, row_indices=tokens)
     gu = grouped_gemm(aq, asf, bank["gate_up_q"], bank["gate_up_sf"], pcsr, c, 2 * f)
     hidden, rowmax = rescale_swiglu_maximum(gu, pcsr, ag, bank["gate_up_global"])
-    hg = segment_global_scales(rowmax, pcsr)
+    if hidden_global is None:
+        hg = segment_global_scales(rowmax, pcsr)
+    else:
+        hg = torch.full((e,), float(hidden_global), dtype=_F32)
     hq, hsf = quantize_activations(hidden, pcsr, pcsr, prows, hg)
     raw = grouped_gemm(hq, hsf, bank["down_q"], bank["down_sf"], pcsr, f, c)
     if trace is not None:
@@ -689,16 +696,17 @@ def expert_outputs(x, tokens, offsets, bank, trace=None):
     return raw, csr, pcsr, hg
 
 
-def routed_forward(x, top_idx, gate, bank, scaling, chunk_size, shared=None, trace=None):
+def routed_forward(x, top_idx, gate, bank, scaling, chunk_size, shared=None, trace=None, hidden_global=None):
     """``NVFP4RoutedExperts._routed_forward`` on SM100
     (praxis/quantization/nvfp4.py:616-747): per dispatch chunk, dispatch,
-    expert outputs and the fused rescale + combine (+ shared)."""
+    expert outputs and the fused rescale + combine (+ shared);
+    ``hidden_global`` as in :func:`expert_outputs`."""
     e = bank["gate_up_q"].shape[0]
     out = torch.empty_like(x)
     for start in range(0, x.shape[0], chunk_size):
         end = min(start + chunk_size, x.shape[0])
         order, inverse, tokens, _sg, offsets, _csr = dispatch(top_idx[start:end], gate[start:end], e)
-        raw, csr, pcsr, hg = expert_outputs(x[start:end], tokens, offsets, bank, trace)
+        raw, csr, pcsr, hg = expert_outputs(x[start:end], tokens, offsets, bank, trace, hidden_global)
         out[start:end] = rescale_combine(
             raw, inverse, top_idx[start:end], gate[start:end], csr, pcsr, hg,
             bank["down_global"], scaling, None if shared is None else shared[start:end],

@@ -115,6 +115,7 @@ class B200NVFP4RoutedExperts(nn.Module):
         for name in sorted(_BUFFER_NAMES):
             self.register_buffer(name, state[name].detach())
         self._kernel: KernelWeights | None = None
+        self._fc1_fp4_scale: float | None = None
         super().train(False)
 
     @classmethod
@@ -147,7 +148,25 @@ class B200NVFP4RoutedExperts(nn.Module):
 
     def _load_from_state_dict(self, *args, **kwargs):
         self._kernel = None
+        self._fc1_fp4_scale = None
         super()._load_from_state_dict(*args, **kwargs)
+
+    def set_fused_swiglu_scale(self, scale: float | None) -> None:
+        """Set a calibrated FC1 output scale, or go back to dynamic hidden
+        scales with None (praxis/quantization/nvfp4.py:235-260, the same
+        checks): the gate/up GEMM then writes FP4 hidden rows at this frozen
+        global, which is also the down GEMM's activation global. This changes
+        output bits (by design: the reference's calibrated path does too).
+        The scale is runtime state, not a checkpoint buffer; loading a state
+        dict clears it."""
+        if scale is not None and (
+            isinstance(scale, bool)
+            or not isinstance(scale, float | int)
+            or not math.isfinite(scale)
+            or scale <= 0
+        ):
+            raise ValueError("FC1 output scale must be finite and positive")
+        self._fc1_fp4_scale = None if scale is None else float(scale)
 
     def prepare(self) -> None:
         """Build the kernel-layout gate/up weights on the buffers' device:
@@ -226,7 +245,8 @@ class B200NVFP4RoutedExperts(nn.Module):
                 raise ValueError("Expected two BF16 shared-expert outputs shaped like the inputs")
             sh = _adjacent(shared)
         kw = self.kernel_weights()
-        common = dict(gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout, rows=(t0, t1))
+        common = dict(gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout, rows=(t0, t1),
+                      fc1_output_scale=self._fc1_fp4_scale)
         if tail is not None:
             xo, h = ops.moe_forward(
                 x, top_idx, gate, kw.gate_up_q, kw.gate_up_sf, self.gate_up_global, self.down_q, kw.down_sf,
@@ -291,6 +311,7 @@ class B200NVFP4RoutedExperts(nn.Module):
                 self.down_q, kw.down_sf, self.down_global, float(scaling),
                 None if shared is None else shared[start:end], out=out[start:end],
                 gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout,
+                fc1_output_scale=self._fc1_fp4_scale,
             )
         return out
 
@@ -334,7 +355,8 @@ def routed_forward_tail(bank: B200NVFP4RoutedExperts, x: Tensor, top_idx: Tensor
             x[start:end], top_idx[start:end], gate[start:end], kw.gate_up_q, kw.gate_up_sf, bank.gate_up_global,
             bank.down_q, kw.down_sf, bank.down_global, float(scaling), None if shared is None else shared[start:end],
             gate_up_sf_layout=kw.gate_up_sf_layout, down_sf_layout=kw.down_sf_layout, tail=tail.chunk(start, end),
-            tail_out=(residual_out[start:end], None if normed is None else normed[start:end]))
+            tail_out=(residual_out[start:end], None if normed is None else normed[start:end]),
+            fc1_output_scale=bank._fc1_fp4_scale)
     return residual_out, normed
 
 

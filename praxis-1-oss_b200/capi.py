@@ -22,7 +22,7 @@ I64 = C.c_int64
 F32 = C.c_float
 SZ = C.c_size_t
 
-ABI_VERSION = 2  # PRAXIS_B200_ABI_VERSION of include/praxis_b200_moe.h
+ABI_VERSION = 3  # PRAXIS_B200_ABI_VERSION of include/praxis_b200_moe.h
 
 OK, EINVAL, ECUDA, EUNSUPPORTED = 0, 1, 2, 3
 SIGMOID, SOFTMAX = 0, 1
@@ -64,6 +64,7 @@ class MoeArgs(C.Structure):
         ("tail", P),
         ("passes", I32),
         ("pass0_tokens", I64),
+        ("fc1_output_scale", F32),
     ]
 
 
@@ -145,6 +146,10 @@ SIGNATURES: dict[str, tuple] = {
         [P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, P, P, P, P, P, I32, C.c_int, P],
     ),
     "praxis_b200_replicate_scales": (C.c_int, [P, I64, I32, I32, P, C.c_int, P]),
+    "praxis_b200_gemm_swiglu_fp4": (
+        C.c_int,
+        [P, P, P, P, P, P, I32, I64, I32, I32, I32, P, P, P, F32, P, P, C.c_int, P],
+    ),
     "praxis_b200_rescale_swiglu": (C.c_int, [P, I64, I32, P, I32, P, P, P, P, I32, C.c_int, P]),
     "praxis_b200_combine": (
         C.c_int,

@@ -363,6 +363,20 @@ int praxis_b200_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q,
                           act_amax, w_global, amax_out, sf_layout, PRAXIS_STREAM(stream));
 }
 
+int praxis_b200_gemm_swiglu_fp4(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf,
+                                const int32_t* tiles, const int32_t* num_tiles, int32_t max_tiles,
+                                int64_t rows_padded, int32_t n, int32_t k, int32_t experts, const float* act_global,
+                                const uint32_t* act_amax, const float* w_global, float hidden_global, void* q_out,
+                                void* sf_out, int device, void* stream) {
+  PRAXIS_DEVICE_OR_RETURN(device);
+  if (!a_q || !a_sf || !b_q || !b_sf || !tiles || !num_tiles || !q_out || !sf_out)
+    return set_error(PRAXIS_B200_EINVAL, "gemm_swiglu_fp4: null pointer");
+  return run_grouped_gemm(a_q, a_sf, b_q, b_sf, reinterpret_cast<const TileEntry*>(tiles), num_tiles, max_tiles,
+                          rows_padded, n, k, experts, EPI_SWIGLU_FP4, nullptr, n / 2, act_global, act_amax, w_global,
+                          nullptr, PRAXIS_B200_SF_COMPACT, PRAXIS_STREAM(stream), 0, 1, static_cast<uint8_t*>(q_out),
+                          static_cast<uint8_t*>(sf_out), hidden_global, 0.0f);
+}
+
 int praxis_b200_replicate_scales(const void* sf, int64_t rows, int32_t k, int32_t group_rows, void* out, int device,
                                  void* stream) {
   PRAXIS_DEVICE_OR_RETURN(device);
@@ -518,6 +532,10 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   if (passes.n == 2 && (passes.t0 < 0 || passes.t0 > a->tokens))
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: pass 0 tokens outside 0..tokens");
   const int groups = a->experts * passes.n;
+  const float fc1 = a->fc1_output_scale;
+  if (fc1 < 0.0f || !(fc1 < 3.4e38f)) return set_error(PRAXIS_B200_EINVAL, "moe_forward: bad FC1 output scale");
+  if (fc1 > 0.0f && (gl != PRAXIS_B200_SF_COMPACT || (2 * a->hidden) % 256 != 0))
+    return set_error(PRAXIS_B200_EINVAL, "moe_forward: the FC1 FP4 output needs compact scales and F %% 128 == 0");
   const int64_t r = a->tokens * a->top_k;
   if ((r + 127 * (int64_t)groups) * (int64_t)(a->dim > 2 * a->hidden ? a->dim : 2 * a->hidden) >= ((int64_t)1 << 31) * 8)
     return set_error(PRAXIS_B200_EINVAL, "moe_forward: chunk exceeds the kernels' indexing range");
@@ -572,14 +590,23 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
     rc = run_replicate_scales(ws + L.asf_compact, L.rp, a->dim, 128, asf, s);
     if (rc) return rc;
   }
-  cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * groups, s);
-  if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
-  rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
-                        a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
-                        h_amax, gl, s, 0, passes.n);
-  if (rc) return rc;
-  rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
-                         down_rep ? ws + L.hsf_compact : hsf, PRAXIS_B200_SF_COMPACT, s);
+  if (fc1 > 0.0f) {
+    // calibrated FC1 output: FP4 hidden rows straight from the gate/up
+    // epilogue at the frozen global, which the down GEMM's rescale uses too
+    rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
+                          a->dim, a->experts, EPI_SWIGLU_FP4, nullptr, a->hidden, act_global, nullptr,
+                          a->gate_up_global, nullptr, gl, s, 0, passes.n, hq, down_rep ? ws + L.hsf_compact : hsf,
+                          fc1, 0.0f);
+  } else {
+    cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * groups, s);
+    if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
+    rc = run_grouped_gemm(aq, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, L.rp, 2 * a->hidden,
+                          a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, act_global, nullptr, a->gate_up_global,
+                          h_amax, gl, s, 0, passes.n);
+    if (rc) return rc;
+    rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
+                           down_rep ? ws + L.hsf_compact : hsf, PRAXIS_B200_SF_COMPACT, s);
+  }
   if (rc) return rc;
   if (down_rep) {
     rc = run_replicate_scales(ws + L.hsf_compact, L.rp, a->hidden, 128, hsf, s);
@@ -587,7 +614,7 @@ int praxis_b200_moe_forward(const praxis_b200_moe_args* a) {
   }
   rc = run_grouped_gemm(hq, hsf, a->down_q, a->down_sf, tiles, num_tiles, L.max_tiles, L.rp, a->dim, a->hidden,
                         a->experts, EPI_RESCALE, rows, a->dim, nullptr, h_amax, a->down_global, nullptr, dl, s, 0,
-                        passes.n);
+                        passes.n, nullptr, nullptr, 0.0f, fc1);
   if (rc) return rc;
   if (a->tail != nullptr)
     return run_combine_tail(rows, a->dim, inverse, a->top_idx, gate, csr, pcsr, nullptr, h_amax, a->down_global, 1,

@@ -22,6 +22,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "nvfp4_quant.cuh"
 
 namespace praxis {
 
@@ -64,7 +65,9 @@ __device__ __forceinline__ int weight_expert(const GemmParams& p, int e) {
 __device__ __forceinline__ float expert_multiplier(const GemmParams& p, int e) {
   // bf16(g_a * g_w) in float32 (praxis/kernels/nvfp4_moe.py:117-121, :237-241)
   float ga;
-  if (p.act_global != nullptr) {
+  if (p.act_global_scalar > 0.0f) {
+    ga = p.act_global_scalar;
+  } else if (p.act_global != nullptr) {
     ga = p.act_global[e];
   } else {
     ga = global_from_amax_bits(p.act_amax[e]);
@@ -390,11 +393,12 @@ __device__ __forceinline__ void st_global_v8(uint16_t* ptr, uint4 a, uint4 b) {
 }
 
 template <int EPI, bool REP>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI == EPI_SWIGLU>::THREADS, 1)
-    gemm_nvfp4_pair_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __cluster_dims__(2, 1, 1)
+    __launch_bounds__(PairShape<REP, EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_FP4>::THREADS, 1)
+        gemm_nvfp4_pair_kernel(const __grid_constant__ GemmParams p) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
-  constexpr bool DIRECT = EPI == EPI_SWIGLU;
+  constexpr bool DIRECT = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_FP4;
   using S = PairShape<REP, DIRECT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -416,6 +420,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+  // EPI_SWIGLU_FP4: div_rn(1/g, 1 + m/8) of the frozen hidden global g
+  __shared__ float s_r8[8];
+  if constexpr (EPI == EPI_SWIGLU_FP4) {
+    if (threadIdx.x < 8) s_r8[threadIdx.x] = recip8_entry(div_rn(1.0f, p.fixed_global), (int)threadIdx.x);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -648,6 +657,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
       const bool store_row = live && grow < p.out_rows;
       const uint32_t tbase = tmem + ((quad * 32u) << 16) + (odd ? S::ACC_ALT_COL : 0u);
       const float mult = (EPI == EPI_PLAIN) ? 1.0f : expert_multiplier(p, t.expert);
+      const float fp4_inv_g = (EPI == EPI_SWIGLU_FP4) ? div_rn(1.0f, p.fixed_global) : 0.0f;
       __nv_bfloat162 hmax = __floats2bfloat162_rn(0.0f, 0.0f);  // max |h| per column parity
       if constexpr (!DIRECT) {
         // the staging boxes are free once this warp's previous stores read them
@@ -690,6 +700,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairShape<REP, EPI =
             } else {
               prev = make_uint4(w[0], w[1], w[2], w[3]);
             }
+          }
+        } else if constexpr (EPI == EPI_SWIGLU_FP4) {
+          // the same 32 hidden values (columns 64*half + 32*bl .. + 31 of the
+          // tile: two 16-blocks), quantized with the frozen global as the
+          // hidden quantize would (codes 16 bytes, two scale bytes)
+          uint32_t codes[4];
+          uint32_t sf2 = 0;
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            uint32_t w[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int e0 = b * 16 + 2 * j;
+              const uint32_t h = swiglu_pair(__uint_as_float(r0[e0]), __uint_as_float(r0[e0 + 1]),
+                                             __uint_as_float(r1[e0]), __uint_as_float(r1[e0 + 1]), mult);
+              w[j] = valid ? h : 0u;
+            }
+            float v[16];
+            float amax;
+            bool has_nan;
+            unpack16_bf16(w, v, amax, has_nan);
+            uint32_t sfb;
+            quantize16_fast(v, amax, p.fixed_global, fp4_inv_g, s_r8, has_nan, codes[2 * b], codes[2 * b + 1], sfb);
+            sf2 |= sfb << (8 * b);
+          }
+          if (store_row) {
+            const int hcol = n * (S::BN / 2) + 64 * half + 32 * bl;  // first hidden column
+            const int j16 = hcol >> 4;
+            *reinterpret_cast<uint4*>(p.q_out + grow * (p.out_cols / 2) + (hcol >> 1)) =
+                make_uint4(codes[0], codes[1], codes[2], codes[3]);
+            *reinterpret_cast<uint16_t*>(p.sf_out + sf_row_base(grow, p.out_cols / 16) + (j16 >> 2) * 512 +
+                                         (j16 & 3)) = (uint16_t)sf2;
           }
         } else {
           // one 32 x 64 box per block: reuse the staging box once the
@@ -819,7 +861,7 @@ static int gemm_variant() {
 
 template <int EPI, bool REP>
 static int launch_gemm_pair(const GemmParams& p, int max_tiles, cudaStream_t stream) {
-  using S = PairShape<REP, EPI == EPI_SWIGLU>;
+  using S = PairShape<REP, EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_FP4>;
   auto kernel = gemm_nvfp4_pair_kernel<EPI, REP>;
   static DeviceOnce attr;
   static int max_clusters[kMaxDevices] = {0};
@@ -860,6 +902,8 @@ static int launch_pair_epi(const GemmParams& p, int epilogue, int max_tiles, cud
   switch (epilogue) {
     case EPI_SWIGLU:
       return launch_gemm_pair<EPI_SWIGLU, REP>(p, max_tiles, stream);
+    case EPI_SWIGLU_FP4:
+      return launch_gemm_pair<EPI_SWIGLU_FP4, REP>(p, max_tiles, stream);
     case EPI_RESCALE:
       return launch_gemm_pair<EPI_RESCALE, REP>(p, max_tiles, stream);
     default:
@@ -871,7 +915,8 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
                      const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
-                     cudaStream_t stream, int sm_limit, int groups_per_weight) {
+                     cudaStream_t stream, int sm_limit, int groups_per_weight, uint8_t* q_out, uint8_t* sf_out,
+                     float fixed_global, float act_global_scalar) {
   if (n % 128 != 0 || k % 128 != 0 || n <= 0 || k <= 0)
     return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs N and K multiples of 128 (N=%d K=%d)", n, k);
   if (experts < 1) return set_error(PRAXIS_B200_EINVAL, "grouped GEMM needs at least one expert");
@@ -881,10 +926,24 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
     return set_error(PRAXIS_B200_EINVAL, "SwiGLU epilogue needs out_cols = N/2, amax_out and w_global");
   if (epilogue == EPI_PLAIN && out_cols != n)
     return set_error(PRAXIS_B200_EINVAL, "plain epilogue needs out_cols = N");
-  if (epilogue == EPI_RESCALE && (out_cols != n || w_global == nullptr || (act_global == nullptr && act_amax == nullptr)))
+  const bool have_act_global = act_global != nullptr || act_amax != nullptr || act_global_scalar > 0.0f;
+  if (epilogue == EPI_RESCALE && (out_cols != n || w_global == nullptr || !have_act_global))
     return set_error(PRAXIS_B200_EINVAL, "rescale epilogue needs global scales");
-  if (epilogue != EPI_PLAIN && epilogue != EPI_SWIGLU && epilogue != EPI_RESCALE)
+  if (epilogue != EPI_PLAIN && epilogue != EPI_SWIGLU && epilogue != EPI_RESCALE && epilogue != EPI_SWIGLU_FP4)
     return set_error(PRAXIS_B200_EINVAL, "unknown epilogue %d", epilogue);
+  if (epilogue == EPI_SWIGLU_FP4) {
+    if (out_cols * 2 != n || w_global == nullptr || !have_act_global || q_out == nullptr || sf_out == nullptr ||
+        !(fixed_global > 0.0f && fixed_global < 3.4e38f))
+      return set_error(PRAXIS_B200_EINVAL,
+                       "FP4 SwiGLU epilogue needs out_cols = N/2, w_global, FP4 outputs and a positive global");
+    if (n % 256 != 0 || out_cols % 64 != 0 || sf_layout != PRAXIS_B200_SF_COMPACT || gemm_variant() != 0)
+      return set_error(PRAXIS_B200_EINVAL, "FP4 SwiGLU epilogue needs the CTA-pair kernel (N %% 256 == 0) "
+                                           "with compact scales");
+    if (((uintptr_t)q_out & 15) || ((uintptr_t)sf_out & 15))
+      return set_error(PRAXIS_B200_EINVAL, "FP4 outputs must be 16-byte aligned");
+  }
+  if (act_global_scalar < 0.0f || !(act_global_scalar < 3.4e38f))
+    return set_error(PRAXIS_B200_EINVAL, "bad activation global scale");
   if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
     return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
   if (sf_layout == PRAXIS_B200_SF_REPLICATED && n % 256 != 0)
@@ -916,6 +975,10 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
   p.max_tiles = max_tiles;
   p.weight_experts = experts;
   p.groups_per_weight = groups_per_weight;
+  p.q_out = q_out;
+  p.sf_out = sf_out;
+  p.fixed_global = fixed_global;
+  p.act_global_scalar = act_global_scalar;
   p.sm_limit = sm_limit;
   const bool rep = sf_layout == PRAXIS_B200_SF_REPLICATED;
   if (n % 256 == 0 && (rep || gemm_variant() == 0)) {
@@ -924,8 +987,10 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
     if (rc) return rc;
     rc = make_bytes_map(&p.tmap_sfb, b_sf, (size_t)experts * n * (k / 16) * copies, rep ? 64 : 8);
     if (rc) return rc;
-    rc = make_out_map(&p.tmap_out, out, rows_padded, out_cols);
-    if (rc) return rc;
+    if (epilogue != EPI_SWIGLU_FP4) {  // the FP4 epilogue writes codes and scales with plain stores
+      rc = make_out_map(&p.tmap_out, out, rows_padded, out_cols);
+      if (rc) return rc;
+    }
     return rep ? launch_pair_epi<true>(p, epilogue, max_tiles, stream)
                : launch_pair_epi<false>(p, epilogue, max_tiles, stream);
   }

@@ -17,7 +17,7 @@ namespace praxis {
 
 constexpr int kMaxDevices = 64;
 
-enum Epilogue : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESCALE = 2 };
+enum Epilogue : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESCALE = 2, EPI_SWIGLU_FP4 = 3 };
 
 struct GemmParams {
   CUtensorMap tmap_a;    // packed FP4 activation rows (padded, expert-grouped)
@@ -41,6 +41,10 @@ struct GemmParams {
   uint32_t* amax_out;
   int32_t weight_experts;  // tile expert e uses weights (e / groups_per_weight) % weight_experts
   int32_t groups_per_weight;
+  uint8_t* q_out;            // EPI_SWIGLU_FP4: E2M1 hidden rows [rows, out_cols / 2]
+  uint8_t* sf_out;           // EPI_SWIGLU_FP4: their UE4M3 scales, compact layout
+  float fixed_global;        // EPI_SWIGLU_FP4: the frozen hidden global scale
+  float act_global_scalar;   // > 0: the activation global of every tile (else act_global / act_amax)
   int32_t sm_limit;        // launch on at most this many SMs (0: all); host side only
 };
 
@@ -146,6 +150,7 @@ int run_grouped_gemm(const void* a_q, const void* a_sf, const void* b_q, const v
                      const int32_t* num_tiles, int max_tiles, int64_t rows_padded, int32_t n, int32_t k,
                      int32_t experts, int epilogue, uint16_t* out, int32_t out_cols, const float* act_global,
                      const uint32_t* act_amax, const float* w_global, uint32_t* amax_out, int sf_layout,
-                     cudaStream_t stream, int sm_limit = 0, int groups_per_weight = 1);
+                     cudaStream_t stream, int sm_limit = 0, int groups_per_weight = 1, uint8_t* q_out = nullptr,
+                     uint8_t* sf_out = nullptr, float fixed_global = 0.0f, float act_global_scalar = 0.0f);
 
 }  // namespace praxis

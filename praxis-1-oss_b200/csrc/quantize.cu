@@ -20,15 +20,9 @@
 // interleave       gate/up row blocks of 64 for the fused SwiGLU GEMM
 #include "common.cuh"
 #include "kernels.h"
+#include "nvfp4_quant.cuh"
 
 namespace praxis {
-
-constexpr float kOneSixth = 0.16666667163372040f;  // f32(1/6)
-
-__device__ __forceinline__ uint32_t sf_offset(int64_t row, int col, int kb) {
-  return (uint32_t)(((row >> 7) * (kb >> 2) + (col >> 2)) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 +
-                    (col & 3));
-}
 
 // Replicated layout (PRAXIS_B200_SF_REPLICATED): the atom of (row group,
 // k-block) is stored four times in a row; a group is 128 rows (activations)
@@ -40,42 +34,19 @@ __device__ __forceinline__ uint32_t sf_offset_rep(int64_t row, int col, int kb, 
                     ((row & 127) >> 5) * 4 + (col & 3));
 }
 
-__device__ __forceinline__ float clamp6(float x) { return fminf(fmaxf(x, -6.0f), 6.0f); }
-
-// Eight floats -> eight E2M1 codes in one word (element 0 in the low nibble).
-__device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 d) {
-  uint32_t out;
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
-      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
-      : "=r"(out)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y), "f"(d.x), "f"(d.y));
-  return out;
-}
-
-// Quantize 16 values with global g (inv_g = div_rn(1, g)); returns the 8
-// code bytes in (lo, hi) and the scale byte. The reference clamps v * rc to
-// [-6, 6] (NaN-ignoring min/max, so NaN -> -6) before the saturating
-// conversion. For finite inputs v * rc stays finite (|v| <= amax, the scale
-// is at least 2^-6), where the saturating conversion alone gives the same
-// codes; blocks holding an infinity or NaN (has_nan) take the clamp.
-// rc_table (optional): rc_table[b] = div_rn(inv_g, e4m3 value of byte b) for
-// the scale bytes 0x08..0x7E the clamp allows (rc_table_entry), one table per
-// global scale, replacing the second division.
-__device__ __forceinline__ float rc_table_entry(float inv_g, uint32_t byte) {
-  return div_rn(inv_g, e4m3_byte_to_f32(byte));
-}
-
+// Quantize 16 values with global g (inv_g = div_rn(1, g)) with the recipe's
+// two IEEE divisions; returns the 8 code bytes in (lo, hi) and the scale
+// byte. The reference clamps v * rc to [-6, 6] (NaN-ignoring min/max, so NaN
+// -> -6) before the saturating conversion. For finite inputs v * rc stays
+// finite (|v| <= amax, the scale is at least 2^-6), where the saturating
+// conversion alone gives the same codes; blocks holding an infinity or NaN
+// (has_nan) take the clamp.
 __device__ __forceinline__ void quantize16(const float (&v)[16], float amax, float g, float inv_g, bool has_nan,
-                                           uint32_t& lo, uint32_t& hi, uint32_t& sf,
-                                           const float* rc_table = nullptr) {
+                                           uint32_t& lo, uint32_t& hi, uint32_t& sf) {
   const float bs = mul_rn(amax, kOneSixth);
   const float sfv = fminf(fmaxf(div_rn(bs, g), 0.015625f), 448.0f);
   sf = f32_to_e4m3_byte(sfv);
-  const float rc = rc_table != nullptr ? rc_table[sf] : rc_table_entry(inv_g, sf);
+  const float rc = div_rn(inv_g, e4m3_byte_to_f32(sf));
   const float2 rc2 = make_float2(rc, rc);
   float2 n[8];
 #pragma unroll
@@ -86,24 +57,6 @@ __device__ __forceinline__ void quantize16(const float (&v)[16], float amax, flo
   }
   lo = e2m1x8(n[0], n[1], n[2], n[3]);
   hi = e2m1x8(n[4], n[5], n[6], n[7]);
-}
-
-// 16 bf16 values -> floats, their max |v| (NaN-ignoring) and whether any is
-// not finite (magnitude bits >= 0x7F80: infinity or NaN).
-__device__ __forceinline__ void load16_bf16(const uint16_t* src, float (&v)[16], float& amax, bool& has_nan) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-  uint4 a = __ldg(s), b = __ldg(s + 1);
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  amax = 0.0f;
-  uint32_t nan_bits = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-    amax = fmaxf(amax, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
-    nan_bits |= (w[i] & 0x7FFF7FFFu) + 0x00800080u;
-  }
-  has_nan = (nan_bits & 0x80008000u) != 0;
 }
 
 // Gather the four scale bytes of lanes 4i..4i+3 into one word (the 4 scales
@@ -140,8 +93,11 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
     uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
-  __shared__ int64_t s_dest[8][8];
+  __shared__ uint8_t* s_qrow[8][8];    // [warp][slot]: the routed row's codes
+  __shared__ int64_t s_sfrow[8][8];    // [warp][slot]: sf_row_base of the routed row (compact layout)
+  __shared__ int64_t s_dest[8][8];     // [warp][slot]: the routed row
   __shared__ float s_g[8][8], s_ig[8][8];
+  __shared__ float s_r8[8][8][8];  // [warp][slot][m]: div_rn(inv_g, 1 + m/8)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb = k_dim / 16;
   if ((int)blockIdx.x >= token_blocks) {
@@ -170,10 +126,15 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
   if (lane < top_k) {
     const int e = route_group(checked_expert(top_idx[t * top_k + lane], experts), t, passes);
     const float g = expert_global(globals, amax_bits, e);
-    s_dest[warp][lane] = (int64_t)pcsr[e] + inverse[t * top_k + lane] - csr[e];
+    const int64_t dest = (int64_t)pcsr[e] + inverse[t * top_k + lane] - csr[e];
+    s_dest[warp][lane] = dest;
+    s_qrow[warp][lane] = q + dest * (k_dim / 2);
+    s_sfrow[warp][lane] = sf_row_base(dest, kb);
     s_g[warp][lane] = g;
     s_ig[warp][lane] = div_rn(1.0f, g);
   }
+  __syncwarp();
+  for (int i = lane; i < top_k * 8; i += 32) s_r8[warp][i >> 3][i & 7] = recip8_entry(s_ig[warp][i >> 3], i & 7);
   __syncwarp();
   const uint16_t* xr = x + t * k_dim;
   for (int j0 = 0; j0 < kb; j0 += 32) {
@@ -182,15 +143,16 @@ __global__ void __launch_bounds__(256) quantize_gather_kernel(
     float v[16];
     float amax = 0.0f;
     bool has_nan = false;
-    if (active) load16_bf16(xr + j * 16, v, amax, has_nan);
+    if (active) load16_bf16_fast(xr + j * 16, v, amax, has_nan);
+    const int64_t sf_col = (int64_t)(j >> 2) * 512 + (j & 3);
     for (int s = 0; s < top_k; ++s) {
       uint32_t lo = 0, hi = 0, sfb = 0;
-      const int64_t dest = s_dest[warp][s];
       if (active) {
-        quantize16(v, amax, s_g[warp][s], s_ig[warp][s], has_nan, lo, hi, sfb);
-        *reinterpret_cast<uint2*>(q + dest * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
+        quantize16_fast(v, amax, s_g[warp][s], s_ig[warp][s], s_r8[warp][s], has_nan, lo, hi, sfb);
+        *reinterpret_cast<uint2*>(s_qrow[warp][s] + (int64_t)j * 8) = make_uint2(lo, hi);
+        if (!rep) sf[s_sfrow[warp][s] + sf_col] = (uint8_t)sfb;
       }
-      store_sf_group(sf, dest, j, kb, sfb, active, rep);
+      if (rep) store_sf_group(sf, s_dest[warp][s], j, kb, sfb, active, true);
     }
   }
 }
@@ -212,13 +174,15 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
   const int64_t row = (int64_t)t.row0 + (item % kTileRows);
   const float g = expert_global(globals, amax_bits, t.expert);
   const float ig = div_rn(1.0f, g);
-  // the block's 8 rows share one expert (tiles are 128 rows): one table of
+  // the block's 8 rows share one group (tiles are 128 rows): one table of
   // the second division for all of them
-  __shared__ float s_rc[128];
-  if (threadIdx.x < 128) s_rc[threadIdx.x] = rc_table_entry(ig, threadIdx.x);
+  __shared__ float s_r8[8];
+  if (threadIdx.x < 8) s_r8[threadIdx.x] = recip8_entry(ig, threadIdx.x);
   __syncthreads();
   const int kb = k_dim / 16;
   const uint16_t* xr = x + row * k_dim;
+  uint8_t* qr = q + row * (k_dim / 2);
+  const int64_t sf_row = sf_row_base(row, kb);
   for (int j0 = 0; j0 < kb; j0 += 32) {
     const int j = j0 + lane;
     const bool active = j < kb;
@@ -227,11 +191,12 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(
       float v[16];
       float amax;
       bool has_nan;
-      load16_bf16(xr + j * 16, v, amax, has_nan);
-      quantize16(v, amax, g, ig, has_nan, lo, hi, sfb, s_rc);
-      *reinterpret_cast<uint2*>(q + row * (k_dim / 2) + (int64_t)j * 8) = make_uint2(lo, hi);
+      load16_bf16_fast(xr + j * 16, v, amax, has_nan);
+      quantize16_fast(v, amax, g, ig, s_r8, has_nan, lo, hi, sfb);
+      *reinterpret_cast<uint2*>(qr + (int64_t)j * 8) = make_uint2(lo, hi);
+      if (!rep) sf[sf_row + (int64_t)(j >> 2) * 512 + (j & 3)] = (uint8_t)sfb;
     }
-    store_sf_group(sf, row, j, kb, sfb, active, rep);
+    if (rep) store_sf_group(sf, row, j, kb, sfb, active, true);
   }
 }
 

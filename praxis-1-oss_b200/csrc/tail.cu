@@ -86,8 +86,10 @@ __global__ void __launch_bounds__(256) combine_tail_kernel(
   if constexpr (MOD) mr = tail.mod + mod_row(t + tail.mod_row0, tail.mod_geom) * 2 * cols;
   float acc_sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // the sums of emulated warps 0..3 at lane `lane`
   for (int c0 = 0; c0 < cols; c0 += 512) {
-    // every load of the 512-column chunk first: 4 vectors per slot per lane
+    // every load of the 512-column chunk first: 4 vectors per slot per lane,
+    // and the residual, shared and modulation vectors of the same columns
     uint2 v[KMAX][4];
+    uint2 xq[4], shq[4], mshq[4], mscq[4];
 #pragma unroll
     for (int s = 0; s < KMAX; ++s)
 #pragma unroll
@@ -95,6 +97,19 @@ __global__ void __launch_bounds__(256) combine_tail_kernel(
         const int c = c0 + 128 * w + 4 * lane;
         if (s < top_k && c < cols) v[s][w] = ldg_stream8(rows + s_src[warp][s] * cols + c);
       }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int c = c0 + 128 * w + 4 * lane;
+      xq[w] = shq[w] = mshq[w] = mscq[w] = make_uint2(0, 0);
+      if (c < cols) {
+        xq[w] = ldg_stream8(xr + c);
+        if (shared != nullptr) shq[w] = ldg_stream8(shared + t * cols + c);
+        if constexpr (MOD) {
+          mshq[w] = *reinterpret_cast<const uint2*>(mr + c);
+          mscq[w] = *reinterpret_cast<const uint2*>(mr + cols + c);
+        }
+      }
+    }
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int c = c0 + 128 * w + 4 * lane;
@@ -118,16 +133,8 @@ __global__ void __launch_bounds__(256) combine_tail_kernel(
           }
         }
       }
-      const uint2 xv = *reinterpret_cast<const uint2*>(xr + c);
-      uint2 sh = make_uint2(0, 0);
-      if (shared != nullptr) sh = *reinterpret_cast<const uint2*>(shared + t * cols + c);
-      uint2 mshift = make_uint2(0, 0), mscale = make_uint2(0, 0);
-      if constexpr (MOD) {
-        mshift = *reinterpret_cast<const uint2*>(mr + c);
-        mscale = *reinterpret_cast<const uint2*>(mr + cols + c);
-      }
-      const uint32_t xw[2] = {xv.x, xv.y}, shw[2] = {sh.x, sh.y};
-      const uint32_t mshw[2] = {mshift.x, mshift.y}, mscw[2] = {mscale.x, mscale.y};
+      const uint32_t xw[2] = {xq[w].x, xq[w].y}, shw[2] = {shq[w].x, shq[w].y};
+      const uint32_t mshw[2] = {mshq[w].x, mshq[w].y}, mscw[2] = {mscq[w].x, mscq[w].y};
       uint32_t xo[2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -177,16 +184,30 @@ __global__ void __launch_bounds__(256) combine_tail_kernel(
     __syncwarp();  // this warp's residual stores above are read back below
     const float s = tail.norm_scale;
     uint16_t* hr = tail.h_out + t * cols;
-    for (int c = 4 * lane; c < cols; c += 128) {
-      const uint2 xv = *reinterpret_cast<const uint2*>(xor_ + c);
-      const float4 wv = *reinterpret_cast<const float4*>(tail.w1 + c);
-      const float2 x01 = unpack_bf16x2(xv.x), x23 = unpack_bf16x2(xv.y);
-      const float o0 = bf16_round(mul_rn(wv.x, mul_rn(r, x01.x)));
-      const float o1 = bf16_round(mul_rn(wv.y, mul_rn(r, x01.y)));
-      const float o2 = bf16_round(mul_rn(wv.z, mul_rn(r, x23.x)));
-      const float o3 = bf16_round(mul_rn(wv.w, mul_rn(r, x23.y)));
-      *reinterpret_cast<uint2*>(hr + c) =
-          make_uint2(cvt_bf16x2(mul_rn(o0, s), mul_rn(o1, s)), cvt_bf16x2(mul_rn(o2, s), mul_rn(o3, s)));
+    for (int c0 = 0; c0 < cols; c0 += 512) {
+      // the chunk's residual (this warp's own stores above) and weight loads first
+      uint2 xq[4];
+      float4 wq[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int c = c0 + 128 * w + 4 * lane;
+        if (c < cols) {
+          xq[w] = *reinterpret_cast<const uint2*>(xor_ + c);
+          wq[w] = *reinterpret_cast<const float4*>(tail.w1 + c);
+        }
+      }
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int c = c0 + 128 * w + 4 * lane;
+        if (c >= cols) continue;
+        const float2 x01 = unpack_bf16x2(xq[w].x), x23 = unpack_bf16x2(xq[w].y);
+        const float o0 = bf16_round(mul_rn(wq[w].x, mul_rn(r, x01.x)));
+        const float o1 = bf16_round(mul_rn(wq[w].y, mul_rn(r, x01.y)));
+        const float o2 = bf16_round(mul_rn(wq[w].z, mul_rn(r, x23.x)));
+        const float o3 = bf16_round(mul_rn(wq[w].w, mul_rn(r, x23.y)));
+        *reinterpret_cast<uint2*>(hr + c) =
+            make_uint2(cvt_bf16x2(mul_rn(o0, s), mul_rn(o1, s)), cvt_bf16x2(mul_rn(o2, s), mul_rn(o3, s)));
+      }
     }
   }
 }

@@ -313,6 +313,27 @@ def grouped_gemm(a_q: Tensor, a_sf: Tensor, b_q: Tensor, b_sf: Tensor, routing: 
     return out
 
 
+def grouped_gemm_swiglu_fp4(a_q: Tensor, a_sf: Tensor, b_q: Tensor, b_sf: Tensor, routing: Routing, *,
+                            act_global: Tensor, w_global: Tensor, hidden_global: float) -> tuple[Tensor, Tensor]:
+    """The gate/up GEMM with SwiGLU and FP4 hidden output at the calibrated
+    global ``hidden_global`` (``gate_up_fp4``, praxis/kernels/nvfp4_swiglu.py:
+    40-74): returns (q [Rp, F/2], sf [Rp, F/16] compact), the bytes that
+    :func:`quantize_rows` gives for the EPI_SWIGLU hidden rows at that
+    global. ``b_q`` / ``b_sf`` in the interleaved gate/up layout."""
+    _need(a_q, "a_q", torch.uint8, 2)
+    rp = a_q.shape[0]
+    e, n, _ = b_q.shape
+    k = a_q.shape[1] * 2
+    f = n // 2
+    q = torch.empty(rp, f // 2, dtype=torch.uint8, device=a_q.device)
+    sf = torch.empty(rp, f // 16, dtype=torch.uint8, device=a_q.device)
+    capi.check(capi.load().praxis_b200_gemm_swiglu_fp4(
+        _p(a_q), _p(a_sf), _p(b_q), _p(b_sf), _p(routing.tiles), _p(routing.num_tiles), rp // 128,
+        rp, n, k, e, _p(act_global), None, _p(w_global), float(hidden_global), _p(q), _p(sf), _dev(a_q),
+        _stream(a_q)))
+    return q, sf
+
+
 def replicate_scales(sf: Tensor, group_rows: int) -> Tensor:
     """Compact swizzled scales [..., rows, K/16] -> the GEMM's replicated
     layout (flat uint8, 4x the size); ``group_rows`` 128 for activation
@@ -543,7 +564,7 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
                 router_bias: Tensor | None = None, top_k: int | None = None, activation: str = "sigmoid",
                 out: Tensor | None = None, gate_up_sf_layout: int | None = None,
                 down_sf_layout: int | None = None, tail: Tail | None = None, tail_out: tuple | None = None,
-                rows: tuple | None = None):
+                rows: tuple | None = None, fc1_output_scale: float | None = None):
     """One dispatch chunk through ``praxis_b200_moe_forward``. With
     ``router_terms`` the router runs too and (out, top_idx, gate) is returned.
     ``gate_up_q/sf`` are in the interleaved kernel layout; the weight scales
@@ -553,7 +574,10 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
     the place of ``out`` (written into ``tail_out`` when given).
     ``rows = (T0, T1)``: x holds a lockstep pair of inputs back to back (the
     reference's forward_pair); one pass of the expert GEMMs serves both and
-    every output row has the bits of its input run alone."""
+    every output row has the bits of its input run alone.
+    ``fc1_output_scale``: the calibrated FC1 output scale (the gate/up GEMM
+    writes FP4 hidden rows at this frozen global, praxis/quantization/
+    nvfp4.py:327-339); None: dynamic hidden globals."""
     _need(x, "x", BF16, 2)
     t, c = x.shape
     e, c_half_f, _ = down_q.shape
@@ -592,6 +616,7 @@ def moe_forward(x: Tensor, top_idx: Tensor | None, gate: Tensor | None, gate_up_
         workspace=ws.data_ptr(), workspace_size=ws_size, device=_dev(x),
         stream=torch.cuda.current_stream(dev).cuda_stream,
         tail=None if st is None else C.addressof(st), passes=npass, pass0_tokens=t0,
+        fc1_output_scale=0.0 if fc1_output_scale is None else float(fc1_output_scale),
     )
     capi.check(lib.praxis_b200_moe_forward(C.byref(args)))
     res = (out,) if tail is None else (residual_out, normed)

@@ -516,3 +516,46 @@ def test_host_pipeline_matches_direct_calls(P):
         want = torch.empty(t, c, dtype=torch.bfloat16, device=DEV)
         layer(hi.to(DEV), want)
         assert torch.equal(ho.view(torch.int16), want.cpu().view(torch.int16))
+
+
+def _midpoint_globals(bs: float, experts: int, seed: int) -> torch.Tensor:
+    """Per-expert global scales that put bs / g within a few ulps of an e4m3
+    rounding midpoint (each expert its own midpoint and offset)."""
+    vals = O.e4m3_values(torch.arange(0x08, 0x7F, dtype=torch.uint8)).double()
+    mids = (vals[:-1] + vals[1:]) / 2
+    g = torch.Generator().manual_seed(seed)
+    pick = mids[torch.randint(0, mids.numel(), (experts,), generator=g)]
+    g0 = (bs / pick).float()
+    step = torch.randint(-6, 7, (experts,), generator=g, dtype=torch.int32)
+    return (g0.view(torch.int32) + step).view(torch.float32)
+
+
+@pytest.mark.parametrize("t,c,e,k", [(512, 1024, 16, 4), (200, 3072, 64, 8)])
+def test_quantize_scales_at_e4m3_midpoints(P, t, c, e, k):
+    """Gather-quantize and row-quantize with global scales that put the block
+    scales next to e4m3 rounding midpoints: the kernels' division-free scale
+    path must take the division there (codes and scale bytes bit-exact)."""
+    top, gate = random_routing(t, e, k, seed=t + c)
+    g = gen(c + 7)
+    x = (torch.randn(t, c, generator=g) * 0.3).to(torch.bfloat16)
+    x[:, ::16] = 1.5  # every 16-block's max |v| = 1.5
+    bs = float(torch.tensor(1.5, dtype=torch.float32) * torch.tensor(1.0 / 6.0, dtype=torch.float32))
+    glob = _midpoint_globals(bs, e, seed=c)
+    xd = x.to(DEV)
+    r = P.ops.dispatch(top.to(DEV), gate.to(DEV), e)
+    q, sf = P.ops.quantize_gather(xd, r, glob.to(DEV))
+    _, _, tokens, _, _, csr = O.dispatch(top, gate, e)
+    pcsr = O.pad_csr(csr)
+    rp = O.padded_rows(t * k, e)
+    oq, osf = O.quantize_activations(x, csr, pcsr, rp, glob, row_indices=tokens)
+    counts = torch.bincount(top.flatten(), minlength=e)
+    rows = torch.cat([torch.arange(int(pcsr[ex]), int(pcsr[ex]) + int(counts[ex])) for ex in range(e)])
+    assert_bytes_equal(q.cpu()[rows], oq[rows])
+    kb = c // 16
+    assert_bytes_equal(O.unswizzle_scales(sf.cpu(), rp, kb)[rows], O.unswizzle_scales(osf, rp, kb)[rows])
+    # the row quantizer on the gathered rows (one global per expert group)
+    gathered = torch.zeros(rp, c, dtype=torch.bfloat16)
+    gathered[rows] = x[tokens]
+    hq, hsf = P.ops.quantize_rows(gathered.to(DEV), r, glob.to(DEV))
+    assert_bytes_equal(hq.cpu()[rows], oq[rows])
+    assert_bytes_equal(O.unswizzle_scales(hsf.cpu(), rp, kb)[rows], O.unswizzle_scales(osf, rp, kb)[rows])

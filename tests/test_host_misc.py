@@ -94,3 +94,29 @@ def test_noalloc_dispatch_outputs_are_checked_before_launch(bad):
     with pytest.raises(ValueError):
         ops.dispatch_noalloc(torch.zeros(t, k, dtype=torch.int64), torch.zeros(t, k, dtype=torch.bfloat16), e,
                              **good)
+
+
+def test_fused_swiglu_scale_contract():
+    """``set_fused_swiglu_scale`` (praxis/quantization/nvfp4.py:235-260): the
+    reference's checks, None goes back to dynamic scales, and loading a
+    state dict clears the runtime scale (it is not a checkpoint buffer)."""
+    import torch
+
+    from oracle import nvfp4_moe_oracle as O
+
+    g = torch.Generator().manual_seed(3)
+    gu = (torch.randn(2, 128, 256, generator=g) * 0.02).to(torch.bfloat16)
+    down = (torch.randn(2, 128, 128, generator=g) * 0.02).to(torch.bfloat16)
+    state = O.pack_routed_experts(gu, down)
+    bank = pkg().B200NVFP4RoutedExperts.from_packed({k: v.clone() for k, v in state.items()})
+    for bad in (0.0, -1.0, float("inf"), float("nan"), True, "1"):
+        with pytest.raises(ValueError):
+            bank.set_fused_swiglu_scale(bad)
+    bank.set_fused_swiglu_scale(2)
+    assert bank._fc1_fp4_scale == 2.0
+    assert "_fc1_fp4_scale" not in bank.state_dict()
+    bank.load_state_dict({k: v.clone() for k, v in state.items()})
+    assert bank._fc1_fp4_scale is None
+    bank.set_fused_swiglu_scale(0.5)
+    bank.set_fused_swiglu_scale(None)
+    assert bank._fc1_fp4_scale is None

@@ -12,6 +12,7 @@ Layers:
     expert_parallel  the bank sharded over GPUs with an all-to-all exchange
     pipeline  host-resident batches with copies overlapped with compute
     torch_ops  the entry points as torch operators (torch.ops.praxis_b200.*)
+    graphs  CUDA-graph capture of the MoE layers (the CudaGraphPool contract)
     build   nvcc build of libpraxis_b200_moe.so (sm_100a)
 """
 
@@ -19,11 +20,11 @@ from __future__ import annotations
 
 import sys
 
-from . import build, capi, expert_parallel, ops, pipeline, torch_ops  # noqa: F401
+from . import build, capi, expert_parallel, graphs, ops, pipeline, torch_ops  # noqa: F401
 from .bank import B200NVFP4RoutedExperts, pack_routed_experts, routed_forward_tail  # noqa: F401
 from .moe import B200MoEFeedForward  # noqa: F401
 
 sys.modules.setdefault("praxis_b200", sys.modules[__name__])
 
 __all__ = ["B200NVFP4RoutedExperts", "B200MoEFeedForward", "pack_routed_experts", "routed_forward_tail",
-           "build", "capi", "ops", "expert_parallel", "pipeline", "torch_ops"]
+           "build", "capi", "ops", "expert_parallel", "graphs", "pipeline", "torch_ops"]

@@ -120,3 +120,24 @@ def test_fused_swiglu_scale_contract():
     bank.set_fused_swiglu_scale(0.5)
     bank.set_fused_swiglu_scale(None)
     assert bank._fc1_fp4_scale is None
+
+
+def test_graph_pool_argument_checks():
+    """The capture pool's constructor rules (praxis/cuda_graphs.py:82-91)
+    and its boundary types, without a GPU."""
+    graphs = pkg().graphs
+    with pytest.raises(ValueError):
+        graphs.CudaGraphPool("cpu")
+    with pytest.raises(ValueError):
+        graphs.CudaGraphPool("cuda:0", warmup=0)
+    with pytest.raises(ValueError):
+        graphs.CudaGraphPool("cuda:0", max_graphs=0)
+    tensors = []
+    with pytest.raises(TypeError):
+        graphs._flatten((object(),), tensors)
+    import torch
+
+    s = graphs._flatten(((torch.zeros(2), [1, torch.ones(3)]), {"k": None}), tensors)
+    assert len(tensors) == 2
+    rebuilt = graphs._rebuild(s, tensors)
+    assert rebuilt[0][1][0] == 1 and rebuilt[1]["k"] is None and rebuilt[0][0] is tensors[0]

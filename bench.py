@@ -863,9 +863,11 @@ def checkpoint_pair(pkg, dev, steps):
 
 def run_expert_parallel(args, cfg):
     """N > 1: the layer expert-parallel over the N GPUs of one node (config 4:
-    each rank routes its own tokens; experts sharded 64/N per rank; NVFP4 rows
-    and scales out, bf16 rows back; by default on the copy engines into
-    IPC-mapped peer buffers, ``--transport nccl`` for NCCL transfers)."""
+    each rank routes its own tokens; gate/up experts sharded 64/N per rank,
+    down weights on every rank; NVFP4 rows and scales out, FP4 hidden rows and
+    scales back, the down GEMM and the combine on the source rank; by default
+    on the copy engines into IPC-mapped peer buffers, ``--transport nccl``
+    for NCCL transfers)."""
     import datetime
 
     import torch
@@ -902,7 +904,8 @@ def run_expert_parallel(args, cfg):
     bank.prepare()
     ep = pkg.expert_parallel.ExpertParallelRoutedExperts(bank, e, transport=args.transport, chunks=args.ep_chunks,
                                                          copy_streams=args.copy_streams,
-                                                         sm_copy_fraction=args.sm_copy_fraction)
+                                                         sm_copy_fraction=args.sm_copy_fraction,
+                                                         down_full=(full.down_q, full.down_sf, full.down_global))
     grouter = torch.Generator().manual_seed(11)
     router = (torch.randn(e, c, generator=grouter) * (1.0 / c) ** 0.5).to(dev)
     terms = ops.split_router_weight(router)
@@ -982,17 +985,19 @@ def run_expert_parallel(args, cfg):
                 "peak_note": "4 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json); rows of this rank's own tokens "
                              "through its local experts' weights, one launch sequence"}
     # bytes this rank's tokens move over NVLink per step: FP4 rows + scales of
-    # whole padded tiles to the other ranks' experts, bf16 rows back; by
-    # symmetry each direction of a rank's links carries about this much
+    # whole padded tiles to the other ranks' experts, FP4 hidden rows +
+    # scales back (and the experts' hidden maxima); by symmetry each
+    # direction of a rank's links carries about this much
     blocks = (pc[el::el] - pc[:-1:el]).tolist()
     off = sum(b for d, b in enumerate(blocks) if d != rank)
-    xbytes = torch.tensor([float(off * (c // 2 + c // 16 + 2 * c))], device=dev)
+    xbytes = torch.tensor([float(off * (c // 2 + c // 16 + f // 2 + f // 16) + 4 * e)], device=dev)
     dist.all_reduce(xbytes, op=dist.ReduceOp.MAX)
     exchange = {"bytes_per_rank_per_step": float(xbytes.item()),
                 "gbs_per_rank": float(xbytes.item()) / (ms / 1e3) / 1e9,
                 "nvlink_peer_copy_gbs_measured": 770.0,
                 "transport": ("copy engines into IPC-mapped peer buffers" if args.transport == "peer" else
-                              "NCCL point-to-point") + ": FP4 rows + UE4M3 scales out, bf16 rows back",
+                              "NCCL point-to-point") + ": FP4 rows + UE4M3 scales out, FP4 hidden rows + scales "
+                             "back, the down GEMM on the source rank",
                 "experts_per_rank": el, "sm_copy_fraction": args.sm_copy_fraction}
     e2e = None
     if not args.no_e2e:

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define PRAXIS_B200_ABI_VERSION 3
+#define PRAXIS_B200_ABI_VERSION 4
 
 enum {
   PRAXIS_B200_OK = 0,
@@ -385,6 +385,14 @@ typedef struct praxis_b200_expert_args {
   size_t workspace_size;
   int device;
   void* stream;
+  /* Hidden-output mode (the down GEMM runs on the source rank): with
+   * hidden_q != NULL the forward stops after the hidden quantize and writes
+   * the FP4 hidden rows [rows, F/2], their compact scales [rows, F/16] and
+   * each segment's max |hidden| (fp32 bits, [segments]); rows_out and the
+   * down weights are not used. */
+  void* hidden_q;
+  void* hidden_sf;
+  uint32_t* hidden_amax;
 } praxis_b200_expert_args;
 
 size_t praxis_b200_expert_workspace_size(int64_t rows, int32_t segments, int32_t dim, int32_t hidden);

@@ -22,7 +22,7 @@ I64 = C.c_int64
 F32 = C.c_float
 SZ = C.c_size_t
 
-ABI_VERSION = 3  # PRAXIS_B200_ABI_VERSION of include/praxis_b200_moe.h
+ABI_VERSION = 4  # PRAXIS_B200_ABI_VERSION of include/praxis_b200_moe.h
 
 OK, EINVAL, ECUDA, EUNSUPPORTED = 0, 1, 2, 3
 SIGMOID, SOFTMAX = 0, 1
@@ -113,6 +113,9 @@ class ExpertArgs(C.Structure):
         ("workspace_size", SZ),
         ("device", C.c_int),
         ("stream", P),
+        ("hidden_q", P),
+        ("hidden_sf", P),
+        ("hidden_amax", P),
     ]
 
 

@@ -449,9 +449,13 @@ size_t praxis_b200_expert_workspace_size(int64_t rows, int32_t segments, int32_t
 int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
   if (!a) return set_error(PRAXIS_B200_EINVAL, "expert_forward: null args");
   PRAXIS_DEVICE_OR_RETURN(a->device);
+  const bool hidden_mode = a->hidden_q != nullptr;
   if (!a->counts || !a->starts || !a->act_global || !a->gate_up_q || !a->gate_up_sf || !a->gate_up_global ||
-      !a->down_q || !a->down_sf || !a->down_global || !a->rows_out || !a->workspace)
+      !a->workspace)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: null pointer");
+  if (hidden_mode ? (!a->hidden_sf || !a->hidden_amax)
+                  : (!a->down_q || !a->down_sf || !a->down_global || !a->rows_out))
+    return set_error(PRAXIS_B200_EINVAL, "expert_forward: null output or down weight");
   if (a->rows < 0 || a->rows % 128 || a->segments < 1 || a->segments > 1024 || a->experts < 1 || a->dim <= 0 ||
       a->hidden <= 0 || a->sm_limit < 0)
     return set_error(PRAXIS_B200_EINVAL, "expert_forward: bad sizes");
@@ -485,12 +489,17 @@ int praxis_b200_expert_forward(const praxis_b200_expert_args* a) {
     if (rc) return rc;
     asf = ws + L.asf;
   }
-  cudaError_t e = cudaMemsetAsync(h_amax, 0, sizeof(uint32_t) * a->segments, s);
+  uint32_t* amax = hidden_mode ? a->hidden_amax : h_amax;
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(uint32_t) * a->segments, s);
   if (e != cudaSuccess) return set_error(PRAXIS_B200_ECUDA, "memset: %s", cudaGetErrorString(e));
   rc = run_grouped_gemm(a->q, asf, a->gate_up_q, a->gate_up_sf, tiles, num_tiles, L.max_tiles, a->rows,
                         2 * a->hidden, a->dim, a->experts, EPI_SWIGLU, hidden, a->hidden, a->act_global, nullptr,
-                        a->gate_up_global, h_amax, gl, s, a->sm_limit);
+                        a->gate_up_global, amax, gl, s, a->sm_limit);
   if (rc) return rc;
+  if (hidden_mode)
+    return run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, amax,
+                             static_cast<uint8_t*>(a->hidden_q), static_cast<uint8_t*>(a->hidden_sf),
+                             PRAXIS_B200_SF_COMPACT, s);
   const bool down_rep = dl == PRAXIS_B200_SF_REPLICATED;
   rc = run_quantize_rows(hidden, a->hidden, tiles, num_tiles, L.max_tiles, nullptr, h_amax, hq,
                          down_rep ? ws + L.hsf_compact : ws + L.hsf, PRAXIS_B200_SF_COMPACT, s);

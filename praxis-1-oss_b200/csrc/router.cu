@@ -13,7 +13,9 @@
 //   gate = bf16(s[top] / sum)   ATen's CUDA reduction order of a k-wide row
 // softmax gating (this build's extension) uses the same selection and gates.
 //
-// logits: tcgen05 kind::f16 MMA, one CTA per 128 tokens. x and the weight
+// logits: tcgen05 kind::f16 MMA over 128-row tiles, one CTA per `rows`
+// tokens (rows <= 128, chosen so that the grid fills the SMs; the rows of a
+// tile past the CTA's own are computed and dropped). x and the weight
 // terms are staged by TMA in 64-column (128-byte swizzled) slabs; an fp32
 // router weight is passed as 3 bf16 terms (hi + mid + lo == the fp32 value),
 // each term's products accumulate in its own tensor-memory columns and the
@@ -36,7 +38,7 @@ constexpr int kRouterSmemBudget = 200 * 1024;
 // reads tensor-memory lanes 32 * (w % 4) .. + 31 = tokens of those rows).
 __global__ void __launch_bounds__(192, 1) router_logits_kernel(
     const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w, int64_t tokens, int dim,
-    int experts, int splits, int e_pad, int stages, uint32_t tmem_cols, float* __restrict__ logits,
+    int experts, int splits, int e_pad, int stages, uint32_t tmem_cols, int rows, float* __restrict__ logits,
     uint16_t* __restrict__ row_amax) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
@@ -50,7 +52,7 @@ __global__ void __launch_bounds__(192, 1) router_logits_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
-  const int64_t row0 = (int64_t)blockIdx.x * kRouterBM;
+  const int64_t row0 = (int64_t)blockIdx.x * rows;
   const int ktiles = (dim + kRouterBK - 1) / kRouterBK;
 
   if (threadIdx.x == 0) {
@@ -171,7 +173,8 @@ __global__ void __launch_bounds__(192, 1) router_logits_kernel(
       if ((int)(lane >> 2) == i) m = r;
     }
     const int64_t grow = row0 + row;
-    if (row_amax != nullptr && grow < tokens) row_amax[grow] = f32_to_bf16(m);
+    const bool mine = row < rows && grow < tokens;
+    if (row_amax != nullptr && mine) row_amax[grow] = f32_to_bf16(m);
     if (ok && mbar_wait(acc_full, 0, kErrTimeoutEpilogue)) {
       tc_fence_after();
       const uint32_t lane_base = tmem + ((quad * 32u) << 16);
@@ -185,7 +188,7 @@ __global__ void __launch_bounds__(192, 1) router_logits_kernel(
 #pragma unroll
           for (int j = 0; j < 16; ++j) acc[j] = s == 0 ? __uint_as_float(r[j]) : add_rn(acc[j], __uint_as_float(r[j]));
         }
-        if (grow < tokens) {
+        if (mine) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             if (e0 + j < experts) out[e0 + j] = acc[j];
@@ -447,9 +450,15 @@ int run_router_logits(const uint16_t* x, const uint16_t* w, int splits, int64_t 
   if (rc) return rc;
   rc = make_bf16_map(&mw, w, (int64_t)splits * experts, dim, e_pad);
   if (rc) return rc;
-  const int64_t blocks = (tokens + kRouterBM - 1) / kRouterBM;
+  // rows per CTA: a multiple of 16, at most one tile, so that the CTAs cover
+  // the SMs once when the tokens allow it (one CTA per SM: shared memory)
+  const int64_t sms = sm_count();
+  int64_t rows = (tokens + sms - 1) / sms;
+  rows = (rows + 15) / 16 * 16;
+  rows = rows < 16 ? 16 : rows > kRouterBM ? kRouterBM : rows;
+  const int64_t blocks = (tokens + rows - 1) / rows;
   launch_pdl(router_logits_kernel, dim3((unsigned)blocks), dim3(192), smem, stream, mx, mw, tokens, dim, experts,
-             splits, e_pad, stages, tmem_cols, logits, row_amax);
+             splits, e_pad, stages, tmem_cols, (int)rows, logits, row_amax);
   return check_launch("router_logits");
 }
 

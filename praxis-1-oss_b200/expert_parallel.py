@@ -20,13 +20,17 @@ rank (its own tokens are one dispatch chunk):
    (``PeerExchange``); ``exchange_forward`` uses NCCL point-to-point
    transfers (and runs over gloo for the CPU tests);
 4. on the expert rank, per source: gate/up GEMM + SwiGLU, hidden quantize with
-   one global scale per (source, expert) segment, down GEMM + rescale
-   (``praxis_b200_expert_forward``);
-5. the bf16 rows travel back into the source's own padded layout: sources
-   are taken in rotating order (step j: compute for rank + j, receive from
+   one global scale per (source, expert) segment (``praxis_b200_expert_forward``
+   in hidden-output mode);
+5. the FP4 hidden rows, their scale atoms and the segments' hidden maxima
+   travel back into the source's own padded layout (F/2 + F/16 bytes a row
+   instead of 2 C bytes of bf16: 7x fewer at C = 3072, F = 1536): sources are
+   taken in rotating order (step j: compute for rank + j, receive from
    rank - j), so each return transfer overlaps the next source's compute;
-   the source combines its tokens with the reference's four-accumulator
-   order.
+6. the source runs the down GEMM + rescale of all its rows against every
+   expert's down weights (replicated on every rank: E * C * F / 2 bytes of
+   FP4 plus scales) and combines its tokens with the reference's
+   four-accumulator order.
 
 Every row meets the same arithmetic as on one GPU, so a rank's output equals
 the single-GPU layer on that rank's tokens bit for bit. The exchange step
@@ -63,10 +67,14 @@ def shard_packed_state(state: Mapping[str, Tensor], rank: int, world: int) -> di
 class CudaBackend:
     """The compute steps on this library's sm_100a kernels. ``transfer_sms``
     SMs are left out of the expert GEMMs' persistent grids so that the
-    transfer kernels of the exchange run beside them."""
+    transfer kernels of the exchange run beside them. ``down_full``: every
+    expert's (down_q, down_sf, down_global), for the down GEMM of the
+    source's own rows."""
 
-    def __init__(self, bank: B200NVFP4RoutedExperts, transfer_sms: int = 16) -> None:
+    def __init__(self, bank: B200NVFP4RoutedExperts, transfer_sms: int = 16, down_full=None) -> None:
         self.bank = bank
+        self.down_full = down_full
+        self.hidden_features = bank.hidden_features
         props = torch.cuda.get_device_properties(bank.gate_up_q.device)
         self.sm_limit = max(2, props.multi_processor_count - transfer_sms) if transfer_sms > 0 else 0
 
@@ -76,19 +84,37 @@ class CudaBackend:
     def quantize(self, x: Tensor, routing) -> tuple[Tensor, Tensor]:
         return ops.quantize_gather(x, routing, routing.act_global)
 
-    def experts(self, q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
-                first: int, last: int, out_ptr: int | None = None) -> Tensor | None:
-        """Segments of local experts [first, last) (segment v: expert first + v % (last - first));
-        with ``out_ptr`` the rows are written to that device address instead."""
+    def _part(self, t: Tensor, first: int, last: int) -> Tensor:
+        """Experts [first, last) of a per-expert buffer (flat when replicated)."""
+        return t[first:last] if t.dim() > 1 else t.view(self.bank.num_experts, -1)[first:last].reshape(-1)
+
+    def hidden(self, q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor, first: int,
+               last: int, out=None) -> tuple[Tensor, Tensor, Tensor]:
+        """Segments of local experts [first, last) (segment v: expert first +
+        v % (last - first)) -> FP4 hidden rows, their scales and the
+        segments' hidden maxima (written into ``out`` when given)."""
         kw = self.bank.kernel_weights()
         b = self.bank
-        n = b.num_experts
+        return ops.expert_hidden(q, sf, counts, starts, act_global, self._part(kw.gate_up_q, first, last),
+                                 self._part(kw.gate_up_sf, first, last), b.gate_up_global[first:last],
+                                 hidden=b.hidden_features, gate_up_sf_layout=kw.gate_up_sf_layout,
+                                 sm_limit=self.sm_limit, out=out)
 
-        def part(t: Tensor) -> Tensor:  # experts [first, last) of a per-expert buffer (flat when replicated)
-            return t[first:last] if t.dim() > 1 else t.view(n, -1)[first:last].reshape(-1)
+    def down(self, hq: Tensor, hsf: Tensor, hamax: Tensor, routing) -> Tensor:
+        """Down GEMM + rescale of the source's padded rows (all experts)."""
+        dq, dsf, dg = self.down_full
+        return ops.grouped_gemm(hq, hsf, dq, dsf, routing, epilogue=capi.EPI_RESCALE, act_amax=hamax, w_global=dg)
 
-        return ops.expert_forward(q, sf, counts, starts, act_global, part(kw.gate_up_q), part(kw.gate_up_sf),
-                                  b.gate_up_global[first:last], part(b.down_q), part(kw.down_sf),
+    def experts(self, q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
+                first: int, last: int, out_ptr: int | None = None) -> Tensor | None:
+        """Both GEMMs of segments of local experts [first, last) on this rank
+        (one launch sequence; the compute of a rank's share of the layer, for
+        timing); with ``out_ptr`` the rows are written to that address."""
+        kw = self.bank.kernel_weights()
+        b = self.bank
+        return ops.expert_forward(q, sf, counts, starts, act_global, self._part(kw.gate_up_q, first, last),
+                                  self._part(kw.gate_up_sf, first, last), b.gate_up_global[first:last],
+                                  self._part(b.down_q, first, last), self._part(kw.down_sf, first, last),
                                   b.down_global[first:last], gate_up_sf_layout=kw.gate_up_sf_layout,
                                   down_sf_layout=kw.down_sf_layout, sm_limit=self.sm_limit, out_ptr=out_ptr)
 
@@ -150,7 +176,12 @@ def exchange_forward(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: i
                 dist.P2POp(dist.isend, sf[lo[d]:lo[d + 1]].contiguous().view(torch.uint8), peer[d], group)]
     outbound = dist.batch_isend_irecv(p2p) if p2p else []
 
-    rows_back = torch.empty(lo[world], x.shape[1], dtype=torch.bfloat16, device=dev)
+    # the source's return buffers: FP4 hidden rows, their scale atoms (tile
+    # rows of F/16 bytes) and the hidden maxima of every expert's segment
+    f = backend.hidden_features
+    hq_back = torch.empty(lo[world], f // 2, dtype=torch.uint8, device=dev)
+    hsf_back = torch.empty(lo[world], f // 16, dtype=torch.uint8, device=dev)
+    hamax = torch.zeros(num_experts, dtype=torch.int32, device=dev)
     chunks = max(1, min(e_local, chunks or 1))
     # every source's segments in one go: counts, starts (relative to its
     # block, then the block end) and global scales, one row per source
@@ -173,16 +204,17 @@ def exchange_forward(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: i
         return (seg_counts[s, a:b].contiguous(), starts_s, seg_global[s, a:b].contiguous()), r0, r1
 
     # this rank's own rows for its own experts: computed while the exchange runs
-    own = None
     if send_rows[rank]:
         seg, _, _ = segments(rank, 0, e_local)
-        own = backend.experts(q[lo[rank]:lo[rank + 1]], sf[lo[rank]:lo[rank + 1]], *seg, 0, e_local)
+        backend.hidden(q[lo[rank]:lo[rank + 1]], sf[lo[rank]:lo[rank + 1]], *seg, 0, e_local,
+                       out=(hq_back[lo[rank]:lo[rank + 1]], hsf_back[lo[rank]:lo[rank + 1]],
+                            hamax[rank * e_local:(rank + 1) * e_local]))
     for w in outbound:
         w.wait()
 
     # the other sources in rotating order: at step j this rank computes the
-    # rows of source (rank + j) and returns them while it receives its own
-    # rows from rank (rank - j), which computes them at the same step; each
+    # hidden rows of source (rank + j) and returns them while it receives its
+    # own from rank (rank - j), which computes them at the same step; each
     # source's experts go in `chunks` groups so the return transfers pipeline
     groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
     keep = []
@@ -194,22 +226,22 @@ def exchange_forward(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_experts: i
             if recv_rows[s]:
                 seg, r0, r1 = segments(s, a, b)
                 if r1 > r0:
-                    res = backend.experts(recv_q[s][r0:r1], recv_sf[s][r0:r1], *seg, a, b)
+                    res = backend.hidden(recv_q[s][r0:r1], recv_sf[s][r0:r1], *seg, a, b)
                     keep.append(res)
-                    p2p.append(dist.P2POp(dist.isend, res.view(torch.uint8), peer[s], group))
+                    p2p += [dist.P2POp(dist.isend, t_.contiguous().view(torch.uint8), peer[s], group) for t_ in res]
             if send_rows[d]:
                 g0 = 0 if chunks == 1 else int(mine[d * e_local + a])
                 g1 = send_rows[d] if chunks == 1 or b == e_local else int(mine[d * e_local + b])
                 if g1 > g0:
-                    dst = rows_back[lo[d] + g0:lo[d] + g1]
-                    p2p.append(dist.P2POp(dist.irecv, dst.view(torch.uint8), peer[d], group))
+                    p2p += [dist.P2POp(dist.irecv, dst.view(torch.uint8), peer[d], group) for dst in (
+                        hq_back[lo[d] + g0:lo[d] + g1], hsf_back[lo[d] + g0:lo[d] + g1],
+                        hamax[d * e_local + a:d * e_local + b])]
             if p2p:
                 returns += dist.batch_isend_irecv(p2p)
-    if own is not None:
-        rows_back[lo[rank]:lo[rank + 1]] = own
     for w in returns:
         w.wait()
-    return backend.combine(rows_back, routing, scaling, shared)
+    rows = backend.down(hq_back, hsf_back, hamax, routing)
+    return backend.combine(rows, routing, scaling, shared)
 
 
 def _padded(rows: int) -> int:
@@ -231,7 +263,8 @@ class PeerExchange:
 
     * ``recv``: one slot per source rank for the FP4 rows and compact scale
       atoms that source sends to this rank's experts;
-    * ``back``: this rank's padded routed rows (bf16), written by the expert
+    * ``back``: this rank's padded routed rows as FP4 hidden rows and their
+      scale atoms, plus every expert's hidden maximum, written by the expert
       ranks with their results.
 
     Buffers grow (collectively: every rank derives the same capacity from the
@@ -254,7 +287,7 @@ class PeerExchange:
         self.rank = dist.get_rank(group)
         self.slot_rows = 0
         self.back_rows = 0
-        self.q_cols = self.sf_cols = self.dim = 0
+        self.q_cols = self.sf_cols = self.hq_cols = self.hsf_cols = self.experts = 0
         self._local: dict[str, tuple[int, int]] = {}  # name -> (pointer, bytes)
         self._peer: dict[str, list[int]] = {}  # name -> pointer per rank (own rank: local)
         self.streams = [torch.cuda.Stream(self.device) for _ in range(copy_streams)]
@@ -283,16 +316,19 @@ class PeerExchange:
                 capi.check(lib.praxis_b200_ipc_free(C.c_void_p(ptr), dev))
         self._local = {}
 
-    def ensure(self, slot_rows: int, back_rows: int, q_cols: int, sf_cols: int, dim: int) -> None:
+    def ensure(self, slot_rows: int, back_rows: int, q_cols: int, sf_cols: int, hq_cols: int, hsf_cols: int,
+               experts: int) -> None:
         """Collective when the buffers grow: every rank must call it with the
         same arguments."""
-        if (slot_rows <= self.slot_rows and back_rows <= self.back_rows and (q_cols, sf_cols, dim) ==
-                (self.q_cols, self.sf_cols, self.dim)):
+        shape = (q_cols, sf_cols, hq_cols, hsf_cols, experts)
+        if (slot_rows <= self.slot_rows and back_rows <= self.back_rows and shape ==
+                (self.q_cols, self.sf_cols, self.hq_cols, self.hsf_cols, self.experts)):
             return
         self._release()
         lib = capi.load()
         dev = self.device.index
-        sizes = {"recv": self.world * slot_rows * (q_cols + sf_cols), "back": back_rows * dim * 2}
+        sizes = {"recv": self.world * slot_rows * (q_cols + sf_cols),
+                 "back": back_rows * (hq_cols + hsf_cols) + experts * 4}
         handles = {}
         for name, nbytes in sizes.items():
             ptr = C.c_void_p()
@@ -315,7 +351,7 @@ class PeerExchange:
                 ptrs.append(int(ptr.value))
             self._peer[name] = ptrs
         self.slot_rows, self.back_rows = slot_rows, back_rows
-        self.q_cols, self.sf_cols, self.dim = q_cols, sf_cols, dim
+        self.q_cols, self.sf_cols, self.hq_cols, self.hsf_cols, self.experts = shape
         self.ready = None
 
     def recv_views(self, s: int, rows: int) -> tuple[Tensor, Tensor]:
@@ -327,18 +363,28 @@ class PeerExchange:
                              device=self.device)
         return q.view(rows, self.q_cols), sf.view(rows, self.sf_cols)
 
-    def back_view(self, rows: int) -> Tensor:
+    def back_views(self, rows: int) -> tuple[Tensor, Tensor, Tensor]:
+        """This rank's returned FP4 hidden rows, their scale atoms and the
+        experts' hidden maxima (int32 bits)."""
         ptr, _ = self._local["back"]
-        t = torch.as_tensor(_DeviceBytes(ptr, rows * self.dim * 2), device=self.device)
-        return t.view(torch.bfloat16).view(rows, self.dim)
+        hq = torch.as_tensor(_DeviceBytes(ptr, rows * self.hq_cols), device=self.device)
+        hsf = torch.as_tensor(_DeviceBytes(ptr + self.back_rows * self.hq_cols, rows * self.hsf_cols),
+                              device=self.device)
+        amax = torch.as_tensor(_DeviceBytes(ptr + self.back_rows * (self.hq_cols + self.hsf_cols), self.experts * 4),
+                               device=self.device)
+        return hq.view(rows, self.hq_cols), hsf.view(rows, self.hsf_cols), amax.view(torch.int32)
 
     def recv_slot(self, d: int, s: int) -> tuple[int, int]:
         """Device addresses (on this rank) of rank d's slot for source s: rows, scales."""
         base = self._peer["recv"][d] + s * self.slot_rows * (self.q_cols + self.sf_cols)
         return base, base + self.slot_rows * self.q_cols
 
-    def back_row(self, d: int, row: int) -> int:
-        return self._peer["back"][d] + row * self.dim * 2
+    def back_ptrs(self, d: int, row: int, expert: int) -> tuple[int, int, int]:
+        """Device addresses (on this rank) of rank d's returned hidden row
+        ``row``, its scales, and its maximum of expert ``expert``."""
+        base = self._peer["back"][d]
+        return (base + row * self.hq_cols, base + self.back_rows * self.hq_cols + row * self.hsf_cols,
+                base + self.back_rows * (self.hq_cols + self.hsf_cols) + expert * 4)
 
     def copy(self, dst: int, src: int, nbytes: int, stream: torch.cuda.Stream,
              after: Sequence[torch.cuda.Event] = ()) -> None:
@@ -418,8 +464,9 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     lo = host[4 * world:5 * world + 1]
     rel_host = [host[5 * world + 1 + i * e_local:5 * world + 1 + (i + 1) * e_local] for i in range(world)]
     max_tokens = max(tokens_all)
+    f = backend.hidden_features
     peers.ensure(_padded(max_tokens * top_k + 127 * e_local), _padded(max_tokens * top_k + 127 * num_experts),
-                 q.shape[1], sf.shape[1], x.shape[1])
+                 q.shape[1], sf.shape[1], f // 2, f // 16, num_experts)
 
     # outbound rows, on the copy engines, into every destination's slot for this rank
     quantized = torch.cuda.Event()
@@ -438,12 +485,13 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     seg_counts = meta_recv[:, :e_local]
     seg_starts = torch.cat([meta_recv[:, e_local:2 * e_local], meta_recv[:, 3 * e_local:3 * e_local + 1]], dim=1)
     seg_global = meta_recv[:, 2 * e_local:3 * e_local].contiguous().view(torch.float32)
-    back = peers.back_view(lo[world])
+    hq_back, hsf_back, hamax = peers.back_views(lo[world])
     returned = [0]
 
     def run(src: int, a: int, b: int) -> None:
-        """Local experts [a, b) on the rows of source ``src``; the results go
-        to their rows of the source's padded layout."""
+        """Local experts [a, b) on the rows of source ``src``: the FP4 hidden
+        rows, their scales and the segments' maxima go to the source's
+        return buffers."""
         if a >= b:
             return
         r0 = rel_host[src][a]
@@ -457,27 +505,33 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
             sq, ssf = rq[r0:r1], rsf[r0:r1]
         counts, starts = seg_counts[src, a:b].contiguous(), (seg_starts[src, a:b + 1] - r0).to(torch.int32)
         ag = seg_global[src, a:b].contiguous()
-        if src == rank:  # own rows: the down GEMM writes into the combine's buffer
-            backend.experts(sq, ssf, counts, starts, ag, a, b, out_ptr=peers.back_row(rank, lo[rank] + r0))
+        if src == rank:  # own rows: straight into this rank's return buffers
+            row = lo[rank] + r0
+            backend.hidden(sq, ssf, counts, starts, ag, a, b,
+                           out=(hq_back[row:row + r1 - r0], hsf_back[row:row + r1 - r0],
+                                hamax[rank * e_local + a:rank * e_local + b]))
             return
         # other sources: local result, then a copy engine writes it into the
-        # source's mapped buffer while the next group computes (the down GEMM
-        # storing into the peer's buffer itself measured slower: its epilogue
-        # becomes bound by the NVLink writes)
-        res = backend.experts(sq, ssf, counts, starts, ag, a, b)
+        # source's mapped buffers while the next group computes
+        hq, hsf, amax = backend.hidden(sq, ssf, counts, starts, ag, a, b)
         done = torch.cuda.Event()
         done.record(compute)
         st = streams[returned[0] % len(streams)]
         returned[0] += 1
-        peers.copy(peers.back_row(src, src_row0[src] + r0), res.data_ptr(), (r1 - r0) * x.shape[1] * 2, st, [done])
+        d_hq, d_hsf, d_amax = peers.back_ptrs(src, src_row0[src] + r0, rank * e_local + a)
+        peers.copy(d_hq, hq.data_ptr(), hq.numel(), st, [done])
+        peers.copy(d_hsf, hsf.data_ptr(), hsf.numel(), st, [done])
+        peers.copy(d_amax, amax.data_ptr(), amax.numel() * 4, st, [done])
         for cs in peers.copy_streams():
-            res.record_stream(cs)
+            for t_ in (hq, hsf, amax):
+                t_.record_stream(cs)
 
     # most of this rank's own rows while its rows travel out (half on 2
     # ranks, three quarters on more, where more rows leave); the other
     # sources in rotating order, in `chunks` expert groups so each result
     # travels back while the next group computes; the rest of the own rows
-    # last, while the final results travel
+    # last, while the final results travel; then the down GEMM of all this
+    # rank's rows and the combine
     tail = e_local // (2 if world <= 2 else 4)
     half = e_local - tail
     run(rank, 0, half)
@@ -492,9 +546,10 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     for st in peers.copy_streams():
         compute.wait_stream(st)
     peers.barrier(compute)  # every result for this rank's rows has landed
+    rows = backend.down(hq_back, hsf_back, hamax, routing)
     peers.ready = torch.cuda.Event()
     peers.ready.record(compute)
-    return backend.combine(back, routing, scaling, shared)
+    return backend.combine(rows, routing, scaling, shared)
 
 
 def chunked_forward(one_chunk, x: Tensor, top_idx: Tensor, gate: Tensor, shared: Tensor | None, chunk_size: int,
@@ -536,20 +591,29 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
     backend = "b200_sm100a_tcgen05_nvfp4_expert_parallel"
     ACCEPTS_DISPATCH = False
 
-    def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *, transport: str = "peer",
-                 transfer_sms: int = 16, chunks: int | None = None, copy_streams: int = 4,
-                 sm_copy_fraction: float = 0.0) -> None:
+    def __init__(self, bank: B200NVFP4RoutedExperts, num_experts: int, group=None, *,
+                 down_full: tuple[Tensor, Tensor, Tensor], transport: str = "peer", transfer_sms: int = 16,
+                 chunks: int | None = None, copy_streams: int = 4, sm_copy_fraction: float = 0.0) -> None:
         """``transport="peer"``: rows move on the copy engines into the peers'
         mapped buffers (``exchange_forward_peer``); ``"nccl"``: NCCL
         point-to-point transfers (``exchange_forward``), with ``transfer_sms``
         SMs kept free of the expert GEMMs for NCCL's kernels. With the peer
         transport, ``sm_copy_fraction`` > 0 moves that share of the bytes with
         a copy kernel on ``transfer_sms`` CTAs beside the copy engines (and
-        keeps those SMs free of the GEMMs)."""
+        keeps those SMs free of the GEMMs). ``down_full``: every expert's
+        (down_q, down_sf, down_global) in the reference's layout (the down
+        GEMM of this rank's rows runs here)."""
         super().__init__()
         world = dist.get_world_size(group)
         if bank.num_experts * world != num_experts:
             raise ValueError("the local bank must hold num_experts / world experts")
+        dq, dsf, dg = down_full
+        if (dq.shape[0] != num_experts or dsf.shape[0] != num_experts or dg.numel() != num_experts
+                or dq.shape[1:] != bank.down_q.shape[1:] or dsf.shape[1:] != bank.down_sf.shape[1:]):
+            raise ValueError("down_full must hold the down weights of every expert")
+        self.register_buffer("down_q_full", dq.detach().contiguous())
+        self.register_buffer("down_sf_full", dsf.detach().contiguous())
+        self.register_buffer("down_global_full", dg.detach().contiguous())
         if transport not in ("peer", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
         self.bank = bank
@@ -558,7 +622,8 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
         self.chunks = chunks
         self.transport = transport if world > 1 else "nccl"
         reserve = self.transport == "nccl" or sm_copy_fraction > 0
-        self._backend = CudaBackend(bank, transfer_sms if world > 1 and reserve else 0)
+        self._backend = CudaBackend(bank, transfer_sms if world > 1 and reserve else 0,
+                                    (self.down_q_full, self.down_sf_full, self.down_global_full))
         self._peers = (PeerExchange(group, bank.gate_up_q.device, copy_streams, sm_copy_fraction, transfer_sms)
                        if self.transport == "peer" else None)
 
@@ -571,12 +636,14 @@ class ExpertParallelRoutedExperts(torch.nn.Module):
         on_host = all(v.device.type == "cpu" for v in shard.values())
         bank = (B200NVFP4RoutedExperts.from_packed(shard) if on_host
                 else B200NVFP4RoutedExperts.from_device_state(shard))
-        return cls(bank, e, group, **kwargs)
+        down_full = tuple(state[n].to(bank.down_q.device) for n in ("down_q", "down_sf", "down_global"))
+        return cls(bank, e, group, down_full=down_full, **kwargs)
 
     def prepare(self) -> None:
         self.bank.prepare()
 
     def _forward(self, x: Tensor, top_idx: Tensor, gate: Tensor, scaling: float, shared: Tensor | None) -> Tensor:
+        self._backend.down_full = (self.down_q_full, self.down_sf_full, self.down_global_full)  # after moves
         if self._peers is not None:
             return exchange_forward_peer(x, top_idx, gate, num_experts=self.num_experts, scaling=scaling,
                                          backend=self._backend, peers=self._peers, shared=shared,

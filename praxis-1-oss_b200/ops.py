@@ -549,6 +549,51 @@ def expert_forward(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_gl
     return out
 
 
+def expert_hidden(q: Tensor, sf: Tensor, counts: Tensor, starts: Tensor, act_global: Tensor,
+                  gate_up_q: Tensor, gate_up_sf: Tensor, gate_up_global: Tensor, *, hidden: int,
+                  gate_up_sf_layout: int, sm_limit: int = 0, out: tuple | None = None
+                  ) -> tuple[Tensor, Tensor, Tensor]:
+    """The gate/up half of the expert rank (``praxis_b200_expert_forward`` in
+    hidden-output mode): received NVFP4 rows in padded segments -> the FP4
+    hidden rows [rows, F/2], their compact scales [rows, F/16] and each
+    segment's max |hidden| (fp32 bits, int32 [segments]), quantized with one
+    global per segment, as the single-GPU path quantizes each (chunk,
+    expert). ``out``: (hq, hsf, hamax) views to write into (e.g. a peer's
+    mapped buffer); else they are allocated."""
+    _need(q, "q", torch.uint8, 2)
+    rows, c_half = q.shape
+    c = c_half * 2
+    f = int(hidden)
+    e_local = gate_up_global.numel()
+    segments = counts.numel()
+    _need(counts, "counts", torch.int32, 1, q.device)
+    _need(starts, "starts", torch.int32, 1, q.device)
+    _need(act_global, "act_global", torch.float32, 1, q.device)
+    if starts.numel() != segments + 1 or act_global.numel() != segments:
+        raise ValueError("starts / act_global do not match the segment count")
+    if out is None:
+        out = (torch.empty(rows, f // 2, dtype=torch.uint8, device=q.device),
+               torch.empty(rows, f // 16, dtype=torch.uint8, device=q.device),
+               torch.empty(segments, dtype=torch.int32, device=q.device))
+    hq, hsf, hamax = out
+    for ten, name, shape in ((hq, "hq", (rows, f // 2)), (hsf, "hsf", (rows, f // 16)), (hamax, "hamax", (segments,))):
+        if tuple(ten.shape) != shape or not ten.is_contiguous() or ten.device != q.device:
+            raise ValueError(f"{name}: expected a contiguous {shape} tensor on {q.device}")
+    lib = capi.load()
+    ws_size = int(lib.praxis_b200_expert_workspace_size(rows, segments, c, f))
+    ws = torch.empty(max(ws_size, 1), dtype=torch.uint8, device=q.device)
+    args = capi.ExpertArgs(
+        q=q.data_ptr(), sf=sf.data_ptr(), rows=rows, counts=counts.data_ptr(), starts=starts.data_ptr(),
+        act_global=act_global.data_ptr(), segments=segments, gate_up_q=gate_up_q.data_ptr(),
+        gate_up_sf=gate_up_sf.data_ptr(), gate_up_global=gate_up_global.data_ptr(),
+        gate_up_sf_layout=int(gate_up_sf_layout), down_sf_layout=capi.SF_COMPACT, dim=c, hidden=f,
+        experts=e_local, sm_limit=int(sm_limit), workspace=ws.data_ptr(), workspace_size=ws.numel(),
+        device=_dev(q), stream=torch.cuda.current_stream(q.device).cuda_stream, hidden_q=hq.data_ptr(),
+        hidden_sf=hsf.data_ptr(), hidden_amax=hamax.data_ptr())
+    capi.check(lib.praxis_b200_expert_forward(C.byref(args)))
+    return hq, hsf, hamax
+
+
 def _layout_of(sf: Tensor, q: Tensor, name: str) -> int:
     """Scale layout told by size: compact = q bytes / 8, replicated = q bytes / 2."""
     if sf.numel() * 8 == q.numel():

@@ -43,7 +43,7 @@ def test_library_is_built_for_sm100a_only():
 
 
 def test_host_helpers(lib):
-    assert lib.praxis_b200_abi_version() == pkg().capi.ABI_VERSION == 3
+    assert lib.praxis_b200_abi_version() == pkg().capi.ABI_VERSION == 4
     assert lib.praxis_b200_padded_rows(65536, 64) == (65536 + 127 * 64) // 128 * 128
     assert pkg().ops.padded_rows(512, 8) == lib.praxis_b200_padded_rows(512, 8)
     ws = lib.praxis_b200_moe_workspace_size(16384, 4, 64, 3072, 1536, 1, 1)

@@ -31,9 +31,11 @@ BF16 = torch.bfloat16
 class OracleBackend:
     """The compute steps of ``CudaBackend`` restated on the CPU."""
 
-    def __init__(self, local_bank: dict, top_k: int):
+    def __init__(self, local_bank: dict, top_k: int, full_bank: dict):
         self.bank = local_bank
+        self.full = full_bank
         self.top_k = top_k
+        self.hidden_features = local_bank["down_q"].shape[2] * 2
 
     def route_rows(self, x, top_idx, gate, num_experts):
         order, inverse, tokens, _sg, offsets, csr = O.dispatch(top_idx, gate, num_experts)
@@ -63,6 +65,40 @@ class OracleBackend:
         raw = O.grouped_gemm(hq, hsf, vb["down_q"], vb["down_sf"], pc, f, c)
         ex = O.expert_of_rows(pc, torch.arange(rows))
         mult = O.bf16_round(hg[ex] * vb["down_global"][ex]).unsqueeze(1)
+        return (raw.to(torch.float32) * mult).to(BF16)
+
+    def hidden(self, q, sf, counts, starts, ag, first, last, out=None):
+        b = {name: v[first:last] for name, v in self.bank.items()}
+        e_local = last - first
+        f = self.hidden_features
+        c = q.shape[1] * 2
+        rows = q.shape[0]
+        seg = torch.arange(counts.numel()) % e_local
+        vb = {k: b[k][seg] for k in ("gate_up_q", "gate_up_sf", "gate_up_global")}
+        pc = starts.long()
+        gu = O.grouped_gemm(q, sf, vb["gate_up_q"], vb["gate_up_sf"], pc, c, 2 * f)
+        hidden, rowmax = O.rescale_swiglu_maximum(gu, pc, ag, vb["gate_up_global"])
+        # each segment's max |hidden| (rows past the last segment count for it)
+        ex = O.expert_of_rows(pc, torch.arange(rows))
+        amax = torch.zeros(counts.numel(), dtype=torch.float32)
+        amax.scatter_reduce_(0, ex, rowmax.to(torch.float32), "amax")
+        hg = O.global_scale_from_amax(amax.to(BF16))
+        hq, hsf = O.quantize_activations(hidden, pc, pc, rows, hg)
+        res = (hq, hsf, amax.view(torch.int32))
+        if out is not None:
+            for dst, src in zip(out, res, strict=True):
+                dst.copy_(src)
+            return out
+        return res
+
+    def down(self, hq, hsf, hamax, r):
+        f = self.hidden_features
+        c = self.full["down_q"].shape[1]
+        pc = r.pcsr.long()
+        raw = O.grouped_gemm(hq, hsf, self.full["down_q"], self.full["down_sf"], pc, f, c)
+        ex = O.expert_of_rows(pc, torch.arange(hq.shape[0]))
+        hg = O.global_scale_from_amax(hamax.view(torch.float32).to(BF16))
+        mult = O.bf16_round(hg[ex] * self.full["down_global"][ex]).unsqueeze(1)
         return (raw.to(torch.float32) * mult).to(BF16)
 
     def combine(self, rows, r, scaling, shared):
@@ -110,7 +146,7 @@ def _worker(rank, world, port, shape, fail_rank, results, chunks=None, chunk_siz
         x, top_idx, gate, shared = _case(rank, t, c, e, k, f)
         if rank == fail_rank:
             raise RuntimeError("planted failure before the exchange")
-        backend = OracleBackend(local, k)
+        backend = OracleBackend(local, k, bank)
 
         def one(xc, tc, gc, sc):
             return ep.exchange_forward(xc, tc, gc, num_experts=e, scaling=2.5, backend=backend, shared=sc,

@@ -1016,11 +1016,13 @@ def run_expert_parallel(args, cfg):
         "layer_tflops": flops * world / (ms / 1e3) / 1e12,
         "roofline": roofline,
         "clocks": clk.summary() if clk is not None else None,
-        # router 2, row max 1, dispatch 3, quantize 1, and per expert-forward call (one per source rank):
-        # tiles 1, GEMM 2, hidden quantize 1 (+ scale replication 1 for replicated weight scales); combine 1
-        # (NCCL's own kernels not counted)
-        "gpu_launches": (8 + (4 + int(bank.kernel_weights().gate_up_sf_layout == pkg.capi.SF_REPLICATED)) * world)
-                        * args.steps,
+        # router 2, row max 1, dispatch 3, quantize 1; per expert-hidden call (two for the rank's own rows
+        # and `chunks` per other source on the peer transport, one and `chunks` on NCCL): tiles 1, gate/up
+        # GEMM 1, hidden quantize 1 (+ scale replication 1 for replicated weight scales); the down GEMM 1 and
+        # the combine 1 (NCCL's own kernels and the copy engines' copies not counted)
+        "gpu_launches": (9 + (3 + int(bank.kernel_weights().gate_up_sf_layout == pkg.capi.SF_REPLICATED))
+                         * ((2 if ep.transport == "peer" else 1)
+                            + (ep.chunks or (2 if ep.transport == "peer" else 1)) * (world - 1))) * args.steps,
         "e2e": e2e,
     }
     if rank == 0:

@@ -450,6 +450,12 @@ int praxis_b200_copy_async(void* dst, const void* src, size_t bytes, int device,
  * e.g. a mapped peer buffer over NVLink): runs beside the copy engines.
  * dst, src and bytes multiples of 16. */
 int praxis_b200_sm_copy(void* dst, const void* src, size_t bytes, int ctas, int device, void* stream);
+/* Stream-ordered wait until the int32 at flag (this device's memory, written
+ * by a peer's copy engine after the data it guards) equals value: one
+ * thread polls with system-scope acquire loads; after timeout_ns it records
+ * error code 5 (peer timeout, praxis_b200_device_error) and returns, so the
+ * stream never hangs. */
+int praxis_b200_wait_value(const int32_t* flag, int32_t value, int64_t timeout_ns, int device, void* stream);
 
 #ifdef __cplusplus
 }

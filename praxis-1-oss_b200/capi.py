@@ -178,6 +178,7 @@ SIGNATURES: dict[str, tuple] = {
     "praxis_b200_ipc_open": (C.c_int, [P, C.c_int, C.POINTER(C.c_void_p)]),
     "praxis_b200_ipc_close": (C.c_int, [P, C.c_int]),
     "praxis_b200_copy_async": (C.c_int, [P, P, C.c_size_t, C.c_int, P]),
+    "praxis_b200_wait_value": (C.c_int, [P, I32, I64, C.c_int, P]),
     "praxis_b200_sm_copy": (C.c_int, [P, P, C.c_size_t, C.c_int, C.c_int, P]),
 }
 

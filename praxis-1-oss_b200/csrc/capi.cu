@@ -658,6 +658,25 @@ __global__ void __launch_bounds__(kPeerCopyThreads) peer_copy_kernel(const uint4
   }
   for (; i < n; i += stride) dst[i] = ldg_stream(src + i);
 }
+
+// One thread waits until *flag (written by another GPU's copy engine into
+// this GPU's memory) equals value, for at most timeout_ns of %globaltimer;
+// past that it records kErrTimeoutPeer and returns, so the stream goes on and
+// the host sees the error at its next check.
+__global__ void wait_value_kernel(const int32_t* flag, int32_t value, int64_t timeout_ns) {
+  if (threadIdx.x != 0) return;
+  const uint64_t start = globaltimer_ns();
+  while (true) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == value) return;
+    if (globaltimer_ns() - start > (uint64_t)timeout_ns) {
+      record_error(kErrTimeoutPeer);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
 }  // namespace praxis
 
 extern "C" {
@@ -723,6 +742,17 @@ int praxis_b200_sm_copy(void* dst, const void* src, size_t bytes, int ctas, int 
   peer_copy_kernel<<<ctas, kPeerCopyThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), static_cast<uint4*>(dst), (int64_t)(bytes / 16));
   return check_launch("sm_copy");
+}
+
+int praxis_b200_wait_value(const int32_t* flag, int32_t value, int64_t timeout_ns, int device, void* stream) {
+  if (flag == nullptr) return set_error(PRAXIS_B200_EINVAL, "wait_value: null pointer");
+  if (((uintptr_t)flag & 3) != 0) return set_error(PRAXIS_B200_EINVAL, "wait_value: flag must be 4-byte aligned");
+  if (timeout_ns <= 0 || timeout_ns > 60000000000ll)
+    return set_error(PRAXIS_B200_EINVAL, "wait_value: timeout must be in (0, 60 s]");
+  int rc = use_device(device);
+  if (rc) return rc;
+  wait_value_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag, value, timeout_ns);
+  return check_launch("wait_value");
 }
 
 int praxis_b200_copy_async(void* dst, const void* src, size_t bytes, int device, void* stream) {

@@ -28,6 +28,7 @@ enum DeviceError : unsigned int {
   kErrTimeoutMma = 2,
   kErrTimeoutEpilogue = 3,
   kErrIndexRange = 4,
+  kErrTimeoutPeer = 5,
 };
 
 __device__ __forceinline__ void record_error(unsigned int code) {

@@ -296,6 +296,10 @@ class PeerExchange:
         self.sm_stream = torch.cuda.Stream(self.device) if sm_copy_fraction > 0 else None
         self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ready: torch.cuda.Event | None = None  # the previous forward's last barrier
+        # per-source arrival flags: a source's copy stream writes the
+        # forward's epoch into the destination's flag after the rows
+        self.epoch = 0
+        self.epoch_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     # -- buffers ------------------------------------------------------------
     def _release(self) -> None:
@@ -328,12 +332,15 @@ class PeerExchange:
         lib = capi.load()
         dev = self.device.index
         sizes = {"recv": self.world * slot_rows * (q_cols + sf_cols),
-                 "back": back_rows * (hq_cols + hsf_cols) + experts * 4}
+                 "back": back_rows * (hq_cols + hsf_cols) + experts * 4, "flags": self.world * 4}
         handles = {}
         for name, nbytes in sizes.items():
             ptr = C.c_void_p()
             capi.check(lib.praxis_b200_ipc_alloc(nbytes, dev, C.byref(ptr)))
             self._local[name] = (int(ptr.value), nbytes)
+            if name == "flags":  # no epoch yet
+                torch.as_tensor(_DeviceBytes(int(ptr.value), nbytes), device=self.device).zero_()
+                torch.cuda.synchronize(self.device)
             h = (C.c_ubyte * capi.IPC_HANDLE_BYTES)()
             capi.check(lib.praxis_b200_ipc_handle(ptr, dev, h))
             handles[name] = bytes(h)
@@ -385,6 +392,25 @@ class PeerExchange:
         base = self._peer["back"][d]
         return (base + row * self.hq_cols, base + self.back_rows * self.hq_cols + row * self.hsf_cols,
                 base + self.back_rows * (self.hq_cols + self.hsf_cols) + expert * 4)
+
+    def signal(self, d: int, stream: torch.cuda.Stream) -> None:
+        """After everything queued for rank d on ``stream`` (and on the SM copy
+        stream): write this forward's epoch into d's flag for this source."""
+        lib = capi.load()
+        if self.sm_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record(self.sm_stream)
+            stream.wait_event(ev)
+        dst = self._peer["flags"][d] + 4 * self.rank
+        capi.check(lib.praxis_b200_copy_async(C.c_void_p(dst), C.c_void_p(self.epoch_buf.data_ptr()), 4,
+                                               self.device.index, C.c_void_p(stream.cuda_stream)))
+
+    def wait_source(self, s: int, stream: torch.cuda.Stream, timeout_s: float = 10.0) -> None:
+        """``stream`` waits (bounded, on the GPU) until source s's rows of this
+        forward have landed in this rank's slot."""
+        flag = self._local["flags"][0] + 4 * s
+        capi.check(capi.load().praxis_b200_wait_value(C.c_void_p(flag), self.epoch, int(timeout_s * 1e9),
+                                                       self.device.index, C.c_void_p(stream.cuda_stream)))
 
     def copy(self, dst: int, src: int, nbytes: int, stream: torch.cuda.Stream,
              after: Sequence[torch.cuda.Event] = ()) -> None:
@@ -468,16 +494,26 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     peers.ensure(_padded(max_tokens * top_k + 127 * e_local), _padded(max_tokens * top_k + 127 * num_experts),
                  q.shape[1], sf.shape[1], f // 2, f // 16, num_experts)
 
-    # outbound rows, on the copy engines, into every destination's slot for this rank
+    # outbound rows, on the copy engines, into every destination's slot for
+    # this rank, each destination's rows followed by this forward's epoch in
+    # its flag for this rank (destinations in rotating order, so each expert
+    # rank's sources land spread out in time)
+    peers.epoch = (peers.epoch + 1) & 0x7FFFFFFF
+    peers.epoch_buf.fill_(peers.epoch)
     quantized = torch.cuda.Event()
     quantized.record(compute)
     streams = peers.streams
     after = [quantized] + ([peers.ready] if peers.ready is not None else [])
-    for k, d in enumerate(d for d in range(world) if d != rank and send_rows[d]):
+    for k, d in enumerate((rank + j) % world for j in range(1, world)):
         st = streams[k % len(streams)]
-        dq, dsf = peers.recv_slot(d, rank)
-        peers.copy(dq, q.data_ptr() + lo[d] * q.shape[1], send_rows[d] * q.shape[1], st, after)
-        peers.copy(dsf, sf.data_ptr() + lo[d] * sf.shape[1], send_rows[d] * sf.shape[1], st, after)
+        if send_rows[d]:
+            dq, dsf = peers.recv_slot(d, rank)
+            peers.copy(dq, q.data_ptr() + lo[d] * q.shape[1], send_rows[d] * q.shape[1], st, after)
+            peers.copy(dsf, sf.data_ptr() + lo[d] * sf.shape[1], send_rows[d] * sf.shape[1], st, after)
+        else:
+            for ev in after:
+                st.wait_event(ev)
+        peers.signal(d, st)
     for st in peers.copy_streams():
         q.record_stream(st)
         sf.record_stream(st)
@@ -535,13 +571,13 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     tail = e_local // (2 if world <= 2 else 4)
     half = e_local - tail
     run(rank, 0, half)
-    for st in peers.copy_streams():
-        compute.wait_stream(st)
-    peers.barrier(compute)  # every slot of this rank is filled
     groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
     for j in range(1, world):
+        src = (rank - j) % world  # the source whose rows were sent to this rank j-th
+        if recv_rows[src]:
+            peers.wait_source(src, compute)
         for a, b in groups:
-            run((rank + j) % world, a, b)
+            run(src, a, b)
     run(rank, half, e_local)
     for st in peers.copy_streams():
         compute.wait_stream(st)

@@ -226,3 +226,25 @@ def test_peer_exchange_two_ranks(P, sm_copy_fraction):
     for proc in procs:
         proc.join(timeout=120)
     assert all(ok for ok, _ in res.values()), res
+
+
+def test_peer_flag_wait_is_bounded(P):
+    """The exchange's arrival wait (``praxis_b200_wait_value``): a flag that
+    is already set passes; a flag that nothing sets gives up after its limit
+    with the peer-timeout error code instead of hanging the stream."""
+    import ctypes as C
+
+    lib = P.capi.load()
+    dev = torch.cuda.current_device()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flag = torch.tensor([7], dtype=torch.int32, device=DEV)
+    P.capi.device_error(dev)  # clear
+    P.capi.check(lib.praxis_b200_wait_value(C.c_void_p(flag.data_ptr()), 7, 1_000_000_000, dev, stream))
+    torch.cuda.synchronize()
+    assert P.capi.device_error(dev) == 0
+    P.capi.check(lib.praxis_b200_wait_value(C.c_void_p(flag.data_ptr()), 8, 2_000_000, dev, stream))
+    torch.cuda.synchronize()
+    assert P.capi.device_error(dev) == 5
+    assert P.capi.device_error(dev) == 0  # read and cleared
+    with pytest.raises(ValueError):  # a wait must have a limit
+        P.capi.check(lib.praxis_b200_wait_value(C.c_void_p(flag.data_ptr()), 7, 0, dev, stream))

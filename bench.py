@@ -138,31 +138,45 @@ def make_inputs(cfg, seed, device):
     return x, router, bias, gu, down
 
 
-class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region (index
-    None: every GPU of the node from one process)."""
+def _smi_ids(ordinals) -> list[str]:
+    """nvidia-smi ids of CUDA device ordinals (through CUDA_VISIBLE_DEVICES)."""
+    vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    return [vis[i] if i < len(vis) else str(i) for i in ordinals]
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons of the GPUs in use (CUDA
+    ordinals ``ordinals``) during the timed region: a 20 ms sampling loop
+    started before the region; the summary keeps the samples whose own
+    timestamps fall inside the region (the nearest one per GPU when the
+    region is shorter than the loop)."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, ordinals):
+        self.ids = _smi_ids(ordinals)
         self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = 0.0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", *(["-i", str(self.index)] if self.index is not None else []),
-                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", "-i", ",".join(self.ids), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.4)  # the loop is running before the region starts
         except OSError:
             self.proc = None
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *exc):
+        self.t1 = time.time()
         if self.proc is not None:
-            time.sleep(0.25)
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
@@ -170,25 +184,33 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
-        else:
-            self.lines = []
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
+        import datetime
+
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        samples = []  # (time, gpu, sm MHz, max MHz, reasons)
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             try:
-                sm.append(float(parts[0]))
-                mx = max(mx, float(parts[1]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((ts, parts[1], float(parts[2]), float(parts[3]),
+                                {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
             except (ValueError, IndexError):
                 continue
-            for name, val in zip(names, parts[3:7]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        inside = [x for x in samples if self.t0 - 0.01 <= x[0] <= self.t1 + 0.01]
+        if not inside:  # region shorter than the loop: the nearest sample of each GPU
+            best = {}
+            for x in samples:
+                d = min(abs(x[0] - self.t0), abs(x[0] - self.t1))
+                if x[1] not in best or d < best[x[1]][0]:
+                    best[x[1]] = (d, x)
+            inside = [v[1] for v in best.values()]
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set().union(*(x[4] for x in inside))
+        return {"sm_mhz": statistics.median(x[2] for x in inside), "sm_max_mhz": max(x[3] for x in inside),
+                "reasons": sorted(reasons), "samples": len(inside), "gpus": sorted({x[1] for x in inside})}
 
 
 def cpu_port_forward(prep, x, router, bias, cfg, routing=None):
@@ -472,7 +494,7 @@ def run_b200(args, cfg):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler([dev.index]) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -942,7 +964,7 @@ def run_expert_parallel(args, cfg):
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # one sampler process for the node (rank 0), not one per rank
-    clk = ClockSampler(None) if rank == 0 else None
+    clk = ClockSampler(range(world)) if rank == 0 else None
     with clk if clk is not None else contextlib.nullcontext():
         ev0.record(stream)
         for _ in range(args.steps):

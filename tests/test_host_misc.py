@@ -141,3 +141,31 @@ def test_graph_pool_argument_checks():
     assert len(tensors) == 2
     rebuilt = graphs._rebuild(s, tensors)
     assert rebuilt[0][1][0] == 1 and rebuilt[1]["k"] is None and rebuilt[0][0] is tensors[0]
+
+
+def test_clock_sampler_keeps_the_timed_window():
+    """The bench's clock record: samples inside the timed window only (idle
+    time before and after does not count), the nearest sample of each GPU
+    when the window is shorter than the sampling loop, and the throttle
+    reasons seen in it."""
+    import datetime
+
+    b = _bench()
+    cs = b.ClockSampler([0, 1])
+
+    def line(t, gpu, mhz, cap="Not Active"):
+        ts = datetime.datetime.fromtimestamp(t).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+        return f"{ts}, {gpu}, {mhz}, 1965, 500.0, Not Active, Not Active, Not Active, {cap}"
+
+    t0 = 1_800_000_000.0
+    cs.t0, cs.t1 = t0, t0 + 0.05
+    cs.lines = [line(t0 - 0.3, 0, 345), line(t0 + 0.02, 0, 1965), line(t0 + 0.02, 1, 1900, "Active"),
+                line(t0 + 0.4, 1, 345)]
+    s = cs.summary()
+    assert s["samples"] == 2 and s["sm_mhz"] == (1965 + 1900) / 2 and s["reasons"] == ["sw_power_cap"]
+    cs.t1 = t0 + 0.005  # shorter than the loop: nearest sample per GPU
+    cs.lines = [line(t0 - 0.3, 0, 345), line(t0 + 0.015, 0, 1965), line(t0 + 0.012, 1, 1965)]
+    s = cs.summary()
+    assert s["samples"] == 2 and s["sm_mhz"] == 1965 and s["gpus"] == ["0", "1"]
+    cs.lines = []
+    assert cs.summary()["reasons"] == ["unavailable"]

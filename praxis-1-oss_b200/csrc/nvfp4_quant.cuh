@@ -49,10 +49,11 @@ __device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 
 //    global scale.
 __device__ __forceinline__ float recip8_entry(float inv_g, int m) { return div_rn(inv_g, 1.0f + 0.125f * (float)m); }
 
-__device__ __forceinline__ void quantize16_fast(const float (&v)[16], float amax, float g, float inv_g,
-                                                const float* recip8, bool has_nan, uint32_t& lo, uint32_t& hi,
-                                                uint32_t& sf) {
-  const float bs = mul_rn(amax, kOneSixth);
+// bs = mul_rn(amax, f32(1/6)), the block's scale before the global one (the
+// same for every global scale a block is quantized with).
+__device__ __forceinline__ void quantize16_bs(const float (&v)[16], float bs, float g, float inv_g,
+                                              const float* recip8, bool has_nan, uint32_t& lo, uint32_t& hi,
+                                              uint32_t& sf) {
   float qv = mul_rn(bs, inv_g);
   const uint32_t dropped = __float_as_uint(qv) & 0xFFFFFu;
   if (has_nan || dropped - (0x80000u - 16u) <= 32u) qv = div_rn(bs, g);
@@ -68,6 +69,12 @@ __device__ __forceinline__ void quantize16_fast(const float (&v)[16], float amax
   }
   lo = e2m1x8(n[0], n[1], n[2], n[3]);
   hi = e2m1x8(n[4], n[5], n[6], n[7]);
+}
+
+__device__ __forceinline__ void quantize16_fast(const float (&v)[16], float amax, float g, float inv_g,
+                                                const float* recip8, bool has_nan, uint32_t& lo, uint32_t& hi,
+                                                uint32_t& sf) {
+  quantize16_bs(v, mul_rn(amax, kOneSixth), g, inv_g, recip8, has_nan, lo, hi, sf);
 }
 
 // Byte offset of row `row`'s scale of k-block 0 in the compact layout; the

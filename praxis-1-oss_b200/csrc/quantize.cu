@@ -85,74 +85,116 @@ __device__ __forceinline__ float expert_global(const float* g, const uint32_t* a
 // ---------------------------------------------------------------------------
 // Gather quantize of the GEMM1 input (one warp per token)
 // ---------------------------------------------------------------------------
+constexpr int kGatherWarps = 8;
+
+// Zero the padding rows of partly filled tiles (the reference allocates
+// these buffers with zeros, praxis/kernels/nvfp4.py:227-231); one CTA per tile.
+__device__ __forceinline__ void gather_zero_padding(int m, int k_dim, const TileEntry* __restrict__ tiles,
+                                                    const int32_t* __restrict__ num_tiles, uint8_t* __restrict__ q,
+                                                    uint8_t* __restrict__ sf, bool rep) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = k_dim / 16;
+  if (m >= *num_tiles) return;
+  const TileEntry t = tiles[m];
+  for (int r = t.valid + warp; r < kTileRows; r += kGatherWarps) {
+    const int64_t row = (int64_t)t.row0 + r;
+    uint4* qr = reinterpret_cast<uint4*>(q + row * (k_dim / 2));
+    for (int i = lane; i < k_dim / 32; i += 32) qr[i] = make_uint4(0, 0, 0, 0);
+    for (int g4 = lane; g4 < kb / 4; g4 += 32) {
+      if (rep) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint32_t*>(sf + sf_offset_rep(row, g4 * 4, kb, 128, c)) = 0u;
+      } else {
+        *reinterpret_cast<uint32_t*>(sf + sf_offset(row, g4 * 4, kb)) = 0u;
+      }
+    }
+  }
+}
+
+// Token-major gather: each token row is read once and quantized for each of
+// its K routed rows with that row's global scale. One warp per token, lane
+// j0 + l owning 16-block j0 + l of each 512-element chunk. The first chunk's
+// loads go out before the routed rows are resolved (top-k -> group ->
+// csr / pcsr / global: two dependent loads), and each chunk's loads before
+// the previous chunk is quantized. Lane s resolves routed row s; the rows'
+// code and scale pointers and global scales then sit in every lane's
+// registers (K is a template argument), the per-row tables of the second
+// division (recip8) in shared memory. CTAs token_blocks.. zero the padding
+// rows of partly filled tiles, one tile each.
+template <int K>
 __global__ void __launch_bounds__(256) quantize_gather_kernel(
     const uint16_t* __restrict__ x, int64_t tokens, int k_dim, const int64_t* __restrict__ top_idx,
     const int64_t* __restrict__ inverse, const int32_t* __restrict__ csr, const int32_t* __restrict__ pcsr,
-    const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int top_k, int experts, Passes passes,
+    const float* __restrict__ globals, const uint32_t* __restrict__ amax_bits, int experts, Passes passes,
     const TileEntry* __restrict__ tiles, const int32_t* __restrict__ num_tiles, int token_blocks,
     uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bool rep) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
-  __shared__ uint8_t* s_qrow[8][8];    // [warp][slot]: the routed row's codes
-  __shared__ int64_t s_sfrow[8][8];    // [warp][slot]: sf_row_base of the routed row (compact layout)
-  __shared__ int64_t s_dest[8][8];     // [warp][slot]: the routed row
-  __shared__ float s_g[8][8], s_ig[8][8];
-  __shared__ float s_r8[8][8][8];  // [warp][slot][m]: div_rn(inv_g, 1 + m/8)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kb = k_dim / 16;
+  __shared__ float s_r8[kGatherWarps][K][8];  // [warp][routed row][m]: div_rn(1/g, 1 + m/8)
   if ((int)blockIdx.x >= token_blocks) {
-    // Zero the padding rows of partly filled tiles (the reference allocates
-    // these buffers with zeros, praxis/kernels/nvfp4.py:227-231).
-    const int m = blockIdx.x - token_blocks;
-    if (m >= *num_tiles) return;
-    const TileEntry t = tiles[m];
-    for (int r = t.valid + warp; r < kTileRows; r += 8) {
-      const int64_t row = (int64_t)t.row0 + r;
-      uint4* qr = reinterpret_cast<uint4*>(q + row * (k_dim / 2));
-      for (int i = lane; i < k_dim / 32; i += 32) qr[i] = make_uint4(0, 0, 0, 0);
-      for (int g4 = lane; g4 < kb / 4; g4 += 32) {
-        if (rep) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) *reinterpret_cast<uint32_t*>(sf + sf_offset_rep(row, g4 * 4, kb, 128, c)) = 0u;
-        } else {
-          *reinterpret_cast<uint32_t*>(sf + sf_offset(row, g4 * 4, kb)) = 0u;
-        }
-      }
-    }
+    gather_zero_padding(blockIdx.x - token_blocks, k_dim, tiles, num_tiles, q, sf, rep);
     return;
   }
-  const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kGatherWarps + warp;
   if (t >= tokens) return;
-  if (lane < top_k) {
-    const int e = route_group(checked_expert(top_idx[t * top_k + lane], experts), t, passes);
-    const float g = expert_global(globals, amax_bits, e);
-    const int64_t dest = (int64_t)pcsr[e] + inverse[t * top_k + lane] - csr[e];
-    s_dest[warp][lane] = dest;
-    s_qrow[warp][lane] = q + dest * (k_dim / 2);
-    s_sfrow[warp][lane] = sf_row_base(dest, kb);
-    s_g[warp][lane] = g;
-    s_ig[warp][lane] = div_rn(1.0f, g);
+  const int kb = k_dim / 16;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + t * k_dim);
+  uint4 na = make_uint4(0, 0, 0, 0), nb = na;
+  if (lane < kb) {
+    na = __ldg(xr + 2 * lane);
+    nb = __ldg(xr + 2 * lane + 1);
+  }
+  int64_t my_dest = 0;
+  float my_g = 1.0f;
+  if (lane < K) {
+    const int e = route_group(checked_expert(top_idx[t * K + lane], experts), t, passes);
+    my_g = expert_global(globals, amax_bits, e);
+    my_dest = (int64_t)pcsr[e] + inverse[t * K + lane] - csr[e];
+  }
+  const float my_ig = div_rn(1.0f, my_g);
+#pragma unroll
+  for (int i0 = 0; i0 < K * 8; i0 += 32) {
+    const int i = i0 + lane;
+    const float ig_i = __shfl_sync(0xffffffffu, my_ig, (i >> 3) & 31);
+    if (i < K * 8) s_r8[warp][i >> 3][i & 7] = recip8_entry(ig_i, i & 7);
   }
   __syncwarp();
-  for (int i = lane; i < top_k * 8; i += 32) s_r8[warp][i >> 3][i & 7] = recip8_entry(s_ig[warp][i >> 3], i & 7);
-  __syncwarp();
-  const uint16_t* xr = x + t * k_dim;
+  uint8_t* qrow[K];
+  int64_t sfrow[K], dest[K];
+  float g[K], ig[K];
+#pragma unroll
+  for (int s = 0; s < K; ++s) {
+    dest[s] = (int64_t)__shfl_sync(0xffffffffu, (unsigned long long)my_dest, s);
+    qrow[s] = q + dest[s] * (k_dim / 2);
+    sfrow[s] = sf_row_base(dest[s], kb);
+    g[s] = __shfl_sync(0xffffffffu, my_g, s);
+    ig[s] = __shfl_sync(0xffffffffu, my_ig, s);
+  }
   for (int j0 = 0; j0 < kb; j0 += 32) {
+    const uint32_t w[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+    const int jn = j0 + 32 + lane;
+    if (jn < kb) {
+      na = __ldg(xr + 2 * jn);
+      nb = __ldg(xr + 2 * jn + 1);
+    }
     const int j = j0 + lane;
     const bool active = j < kb;
     float v[16];
-    float amax = 0.0f;
-    bool has_nan = false;
-    if (active) load16_bf16_fast(xr + j * 16, v, amax, has_nan);
+    float amax;
+    bool has_nan;
+    unpack16_bf16(w, v, amax, has_nan);
+    const float bs = mul_rn(amax, kOneSixth);
     const int64_t sf_col = (int64_t)(j >> 2) * 512 + (j & 3);
-    for (int s = 0; s < top_k; ++s) {
+#pragma unroll
+    for (int s = 0; s < K; ++s) {
       uint32_t lo = 0, hi = 0, sfb = 0;
       if (active) {
-        quantize16_fast(v, amax, s_g[warp][s], s_ig[warp][s], s_r8[warp][s], has_nan, lo, hi, sfb);
-        *reinterpret_cast<uint2*>(s_qrow[warp][s] + (int64_t)j * 8) = make_uint2(lo, hi);
-        if (!rep) sf[s_sfrow[warp][s] + sf_col] = (uint8_t)sfb;
+        quantize16_bs(v, bs, g[s], ig[s], s_r8[warp][s], has_nan, lo, hi, sfb);
+        *reinterpret_cast<uint2*>(qrow[s] + (int64_t)j * 8) = make_uint2(lo, hi);
+        if (!rep) sf[sfrow[s] + sf_col] = (uint8_t)sfb;
       }
-      if (rep) store_sf_group(sf, s_dest[warp][s], j, kb, sfb, active, true);
+      if (rep) store_sf_group(sf, dest[s], j, kb, sfb, active, true);
     }
   }
 }
@@ -296,11 +338,17 @@ int run_quantize_gather(const uint16_t* x, int64_t tokens, int k_dim, const int6
   if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
   if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
     return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
-  const int token_blocks = (int)((tokens + 7) / 8);
-  const int grid = token_blocks + max_tiles;
+  if (((uintptr_t)x | (uintptr_t)q) & 15)
+    return set_error(PRAXIS_B200_EINVAL, "quantize_gather: x and q must be 16-byte aligned");
+  const int64_t token_blocks = (tokens + kGatherWarps - 1) / kGatherWarps;
+  const int64_t grid = token_blocks + max_tiles;
   if (grid == 0) return PRAXIS_B200_OK;
-  launch_pdl(quantize_gather_kernel, dim3(grid), dim3(256), 0, stream, x, tokens, k_dim, top_idx, inverse, csr, pcsr,
-             globals, amax_bits, top_k, experts, passes, tiles, num_tiles, token_blocks, q, sf,
+  using Kernel = decltype(&quantize_gather_kernel<1>);
+  static const Kernel kernels[8] = {quantize_gather_kernel<1>, quantize_gather_kernel<2>, quantize_gather_kernel<3>,
+                                    quantize_gather_kernel<4>, quantize_gather_kernel<5>, quantize_gather_kernel<6>,
+                                    quantize_gather_kernel<7>, quantize_gather_kernel<8>};
+  launch_pdl(kernels[top_k - 1], dim3((unsigned)grid), dim3(256), 0, stream, x, tokens, k_dim, top_idx, inverse, csr,
+             pcsr, globals, amax_bits, experts, passes, tiles, num_tiles, (int)token_blocks, q, sf,
              sf_layout == PRAXIS_B200_SF_REPLICATED);
   return check_launch("quantize_gather");
 }

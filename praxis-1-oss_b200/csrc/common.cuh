@@ -252,15 +252,38 @@ __device__ __forceinline__ uint32_t rescale_pair(float a0, float a1, float mult)
   return cvt_bf16x2(v.x, v.y);
 }
 
+// a * b per bf16 lane, rounded once to bf16 (round to nearest even). For
+// bf16 operands the f32 product is exact wherever it is normal, so this is
+// bf16(f32(a) * f32(b)) for every product of at least 2^-126 in magnitude
+// (and for overflow, which gives infinity both ways).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// rescale_pair with the multiplier given as a packed bf16x2 pair (mult_bf2 =
+// cvt_bf16x2(mult, mult), mult a bf16 value): one conversion and one bf16x2
+// multiply. It equals rescale_pair whenever the products are normal, which
+// the GEMM epilogues' accumulators times a bf16(g_a * g_w) multiplier are
+// (|acc| is 0 or at least the FP4 product quantum, the global scales at least
+// 1e-12 / 2688 each).
+__device__ __forceinline__ uint32_t rescale_pair_bf2(float a0, float a1, uint32_t mult_bf2) {
+  return mul_bf16x2(cvt_bf16x2(a0, a1), mult_bf2);
+}
+
 // The SwiGLU element of swiglu_element<> for two adjacent columns of one row
 // (gate accumulators g0, g1; up accumulators u0, u1); returns h packed as
 // bf16x2. The sigmoid's division 1 / d (d = 1 + 2^t >= 1) is recip_rn_ge1
 // unrolled: for d <= 2^64 its scale is 1, so
 //   y1 = y0 + y0 (1 - d y0);  q = y1 + (1 - d y1) y1
 // on both lanes at once; larger (or infinite) d take the scalar form.
-__device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, float u1, float mult) {
-  const float2 g = unpack_bf16x2(rescale_pair(g0, g1, mult));
-  const float2 u = unpack_bf16x2(rescale_pair(u0, u1, mult));
+template <bool kBf2>
+__device__ __forceinline__ uint32_t swiglu_pair_impl(float g0, float g1, float u0, float u1, float mult,
+                                                     uint32_t mult_bf2) {
+  const uint32_t gp = kBf2 ? rescale_pair_bf2(g0, g1, mult_bf2) : rescale_pair(g0, g1, mult);
+  const uint32_t up = kBf2 ? rescale_pair_bf2(u0, u1, mult_bf2) : rescale_pair(u0, u1, mult);
+  const float2 g = unpack_bf16x2(gp);
   const float2 t = mul2_rn(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
   // The flush-to-zero form gives the same d = 1 + 2^t as the reference's
   // ex2.approx.f32: a subnormal t gives 2^t = 1 either way, and a subnormal
@@ -271,7 +294,7 @@ __device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, fl
   const float2 one = make_float2(1.0f, 1.0f);
   const float2 d = add2_rn(one, make_float2(e0, e1));
   float2 s;
-  if (d.x > 1.8446744073709552e19f || d.y > 1.8446744073709552e19f) {
+  if (fmaxf(d.x, d.y) > 1.8446744073709552e19f) {  // d >= 1: never NaN
     s = make_float2(recip_rn_ge1(d.x), recip_rn_ge1(d.y));
   } else {
     float2 y0;
@@ -284,9 +307,23 @@ __device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, fl
     s = fma2_rn(fma2_rn(nd, y0, one), y0, y0);
   }
   const float2 gs = mul2_rn(g, s);
-  const float2 silu = unpack_bf16x2(cvt_bf16x2(gs.x, gs.y));
-  const float2 h = mul2_rn(silu, u);
-  return cvt_bf16x2(h.x, h.y);
+  if constexpr (kBf2) {
+    return mul_bf16x2(cvt_bf16x2(gs.x, gs.y), up);
+  } else {
+    const float2 silu = unpack_bf16x2(cvt_bf16x2(gs.x, gs.y));
+    const float2 h = mul2_rn(silu, unpack_bf16x2(up));
+    return cvt_bf16x2(h.x, h.y);
+  }
+}
+
+__device__ __forceinline__ uint32_t swiglu_pair(float g0, float g1, float u0, float u1, float mult) {
+  return swiglu_pair_impl<false>(g0, g1, u0, u1, mult, 0u);
+}
+
+// The same with the bf16x2 multiplies of rescale_pair_bf2 (and h = silu * u
+// as one bf16x2 multiply of two bf16 pairs): the GEMM epilogue's form.
+__device__ __forceinline__ uint32_t swiglu_pair_bf2(float g0, float g1, float u0, float u1, uint32_t mult_bf2) {
+  return swiglu_pair_impl<true>(g0, g1, u0, u1, 0.0f, mult_bf2);
 }
 
 // ---------------------------------------------------------------------------

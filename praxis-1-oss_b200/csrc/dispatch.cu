@@ -159,13 +159,26 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
   const int te = t % experts, tp = t / experts;
   const int span = (segments + parts - 1) / parts;
   const int s0 = tp * span, s1 = min(segments, s0 + span);
+  // (the loads of kScanBatch segments go out together: a thread's range is
+  // read in a few memory latencies instead of one per segment)
+  constexpr int kScanBatch = 8;
   int local = 0;
   uint32_t lmax = 0;
   if (tp < parts) {
-    for (int s = s0; s < s1; ++s) {
-      const int64_t i = (int64_t)s * experts + te;
-      local += seg_count[i];
-      lmax = max(lmax, seg_max[i]);
+    for (int s = s0; s < s1; s += kScanBatch) {
+      int c[kScanBatch];
+      uint32_t mx[kScanBatch];
+#pragma unroll
+      for (int u = 0; u < kScanBatch; ++u) {
+        const int64_t i = (int64_t)(s + u) * experts + te;
+        c[u] = s + u < s1 ? seg_count[i] : 0;
+        mx[u] = s + u < s1 ? seg_max[i] : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kScanBatch; ++u) {
+        local += c[u];
+        lmax = max(lmax, mx[u]);
+      }
     }
     s_part[t] = local;
     s_pmax[t] = lmax;
@@ -175,11 +188,15 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
     int before = 0;
     for (int q = 0; q < tp; ++q) before += s_part[q * experts + te];
     int run = before;
-    for (int s = s0; s < s1; ++s) {
-      const int64_t i = (int64_t)s * experts + te;
-      const int c = seg_count[i];
-      seg_count[i] = run;
-      run += c;
+    for (int s = s0; s < s1; s += kScanBatch) {
+      int c[kScanBatch];
+#pragma unroll
+      for (int u = 0; u < kScanBatch; ++u) c[u] = s + u < s1 ? seg_count[(int64_t)(s + u) * experts + te] : 0;
+#pragma unroll
+      for (int u = 0; u < kScanBatch; ++u) {
+        if (s + u < s1) seg_count[(int64_t)(s + u) * experts + te] = run;
+        run += c[u];
+      }
     }
   }
   const int e = threadIdx.x;

@@ -226,13 +226,15 @@ __device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int o) {
   return ((uint64_t)hi << 32) | lo;
 }
 
-// P = experts per lane (experts <= 32 * P).
-template <int P>
+// P = experts per lane (experts <= 32 * P), K = top_k (the selection, tie
+// and order loops unroll to K entries).
+template <int P, int K>
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
-                                                    int64_t tokens, int experts, int top_k, int activation,
+                                                    int64_t tokens, int experts, int activation,
                                                     int64_t* __restrict__ top_idx, uint16_t* __restrict__ gate) {
   pdl_wait();  // the previous kernel of the stream has completed
   pdl_trigger();
+  constexpr int top_k = K;
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
@@ -470,18 +472,16 @@ int run_route(const float* logits, const float* bias, int64_t tokens, int expert
     return set_error(PRAXIS_B200_EINVAL, "unknown router activation");
   if (tokens == 0) return PRAXIS_B200_OK;
   const unsigned blocks = (unsigned)((tokens + 7) / 8);
-  if (experts <= 32)
-    launch_pdl(route_kernel<1>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
-               top_idx, gate);
-  else if (experts <= 64)
-    launch_pdl(route_kernel<2>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
-               top_idx, gate);
-  else if (experts <= 128)
-    launch_pdl(route_kernel<4>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
-               top_idx, gate);
-  else
-    launch_pdl(route_kernel<8>, dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, top_k, activation,
-               top_idx, gate);
+  using Kernel = decltype(&route_kernel<1, 1>);
+#define PRAXIS_ROUTE_ROW(P)                                                                                     \
+  {route_kernel<P, 1>, route_kernel<P, 2>, route_kernel<P, 3>, route_kernel<P, 4>, route_kernel<P, 5>,         \
+   route_kernel<P, 6>, route_kernel<P, 7>, route_kernel<P, 8>}
+  static const Kernel kernels[4][8] = {PRAXIS_ROUTE_ROW(1), PRAXIS_ROUTE_ROW(2), PRAXIS_ROUTE_ROW(4),
+                                       PRAXIS_ROUTE_ROW(8)};
+#undef PRAXIS_ROUTE_ROW
+  const int pi = experts <= 32 ? 0 : experts <= 64 ? 1 : experts <= 128 ? 2 : 3;
+  launch_pdl(kernels[pi][top_k - 1], dim3(blocks), dim3(256), 0, stream, logits, bias, tokens, experts, activation,
+             top_idx, gate);
   return check_launch("route");
 }
 

@@ -52,6 +52,12 @@ __global__ void row_amax_kernel(const uint16_t* __restrict__ x, int64_t rows, in
   if (lane == 0) out[row] = f32_to_bf16(m);
 }
 
+// Token of routed position p (positions < 2^31, checked on the host: a
+// 32-bit division).
+__device__ __forceinline__ int64_t token_of(int64_t p, int top_k) {
+  return (int64_t)((uint32_t)p / (uint32_t)top_k);
+}
+
 // ---------------------------------------------------------------------------
 // 1. count
 // ---------------------------------------------------------------------------
@@ -86,8 +92,8 @@ __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const
       for (int u = 0; u < kDispatchUnroll; ++u) {
         const int64_t p = base + 32 * u + lane;
         const bool live = p < end;
-        ev[u] = live ? route_group(checked_expert(top_idx[p], experts), p / top_k, passes) : -1;
-        mv[u] = (live && row_amax != nullptr) ? __float_as_uint(bf16_to_f32(row_amax[p / top_k])) : 0u;
+        ev[u] = live ? route_group(checked_expert(top_idx[p], experts), token_of(p, top_k), passes) : -1;
+        mv[u] = (live && row_amax != nullptr) ? __float_as_uint(bf16_to_f32(row_amax[token_of(p, top_k)])) : 0u;
       }
 #pragma unroll
       for (int u = 0; u < kDispatchUnroll; ++u) {
@@ -354,7 +360,7 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
     for (int u = 0; u < kDispatchUnroll; ++u) {
       const int64_t p = base + 32 * u + lane;
       const bool live = p < end;
-      ev[u] = live ? route_group(checked_expert(top_idx[p], experts), p / top_k, passes) : -1;
+      ev[u] = live ? route_group(checked_expert(top_idx[p], experts), token_of(p, top_k), passes) : -1;
       gv[u] = (live && sorted_gate) ? gate[p] : (uint16_t)0;
     }
 #pragma unroll
@@ -372,8 +378,9 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
       if (live) {
         if (order) order[dest] = p;
         if (inverse) inverse[p] = dest;
-        if (tokens) tokens[dest] = p / top_k;
-        if (tokens32) tokens32[dest] = (int32_t)(p / top_k);
+        const int32_t tok = (int32_t)token_of(p, top_k);
+        if (tokens) tokens[dest] = tok;
+        if (tokens32) tokens32[dest] = tok;
         if (sorted_gate) sorted_gate[dest] = gv[u];
       }
     }
@@ -384,9 +391,11 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
 // Host entry
 // ---------------------------------------------------------------------------
 static void dispatch_geometry(int64_t positions, int* seg_len, int* segments) {
-  // Segments of >= 256 positions, at most 2048 of them (bounds the serial
-  // per-expert scan of the single-CTA pass).
-  int64_t len = 256;
+  // Segments of >= 128 positions (one warp each: enough warps to cover the
+  // memory latency of the count and scatter passes, few enough segments for
+  // the single-CTA scan; config 2: 27.5 us for the three passes against 29.7
+  // with 64 or 256), at most 2048 of them.
+  int64_t len = 128;
   while ((positions + len - 1) / len > 2048) len *= 2;
   *seg_len = (int)len;
   *segments = (int)((positions + len - 1) / len);

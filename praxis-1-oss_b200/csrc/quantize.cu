@@ -360,6 +360,8 @@ int run_quantize_rows(const uint16_t* x, int k_dim, const TileEntry* tiles, cons
   if (globals == nullptr && amax_bits == nullptr) return set_error(PRAXIS_B200_EINVAL, "no global scales");
   if (sf_layout != PRAXIS_B200_SF_COMPACT && sf_layout != PRAXIS_B200_SF_REPLICATED)
     return set_error(PRAXIS_B200_EINVAL, "unknown scale layout %d", sf_layout);
+  if (((uintptr_t)x | (uintptr_t)q) & 15)
+    return set_error(PRAXIS_B200_EINVAL, "quantize_rows: x and q must be 16-byte aligned");
   const int64_t blocks = (int64_t)max_tiles * kTileRows / 8;
   if (blocks == 0) return PRAXIS_B200_OK;
   launch_pdl(quantize_rows_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, x, k_dim, tiles, num_tiles, globals,

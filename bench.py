@@ -543,6 +543,7 @@ def run_b200(args, cfg):
         "config": workload_config(cfg, args.config, 1),
         "layer_tflops": layer_flops / (ms / 1e3) / 1e12,
         "stages_ms": stages,
+        "read_floor": read_floor(x, reps=max(3, min(args.steps, 10))),
         "roofline": roofline,
         "expert_rows": {"max": int(counts.max()), "min": int(counts.min()), "top_expert_token_share": float(
             counts.max()) / t},
@@ -1102,6 +1103,32 @@ def graph_latency(step, dev, calls=50, euler_steps=10):
             "euler_steps_per_loop": euler_steps, "capture": "whole layer incl. router in one CUDA graph",
             "l2": "back-to-back replays of the Euler loop reuse the weights (113 MB, L2-resident)",
             "p50_ms_l2_flushed": cold[len(cold) // 2], "p90_ms_l2_flushed": cold[(len(cold) * 9) // 10]}
+
+
+def read_floor(x, reps=5):
+    """A plain read of the layer input (torch's amax reduction, one launch)
+    timed like the stages (L2 flushed by a 256 MB write first, CUDA events
+    around the launch): what a single launch that only streams these bytes
+    reaches, the context for the HBM kernels' fractions of the copy peak."""
+    import torch
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    total = 0.0
+    for rep in range(reps + 1):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(1_000_000)
+        e0.record(stream)
+        torch.amax(x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if rep:
+            total += e0.elapsed_time(e1)
+    ms = total / reps
+    nbytes = x.numel() * x.element_size()
+    return {"what": "torch.amax over the layer input (bf16), L2 flushed, CUDA events around the launch",
+            "bytes": nbytes, "ms": ms, "gbs": nbytes / (ms / 1e3) / 1e9}
 
 
 def time_stages(pkg, x, terms, mod, bank, kw, cfg, reps=5):

@@ -300,6 +300,12 @@ class PeerExchange:
         # forward's epoch into the destination's flag after the rows
         self.epoch = 0
         self.epoch_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # this rank's results for the other sources before they travel back:
+        # one region per source (like the receive slots), kept across
+        # forwards so the return copies need no per-call allocation or
+        # stream bookkeeping (each forward ends with the compute stream
+        # waiting for every copy stream)
+        self.res_hq = self.res_hsf = self.res_amax = None
 
     # -- buffers ------------------------------------------------------------
     def _release(self) -> None:
@@ -359,6 +365,10 @@ class PeerExchange:
             self._peer[name] = ptrs
         self.slot_rows, self.back_rows = slot_rows, back_rows
         self.q_cols, self.sf_cols, self.hq_cols, self.hsf_cols, self.experts = shape
+        u8 = dict(dtype=torch.uint8, device=self.device)
+        self.res_hq = torch.empty(self.world, slot_rows, hq_cols, **u8)
+        self.res_hsf = torch.empty(self.world, slot_rows, hsf_cols, **u8)
+        self.res_amax = torch.empty(self.world, experts, dtype=torch.int32, device=self.device)
         self.ready = None
 
     def recv_views(self, s: int, rows: int) -> tuple[Tensor, Tensor]:
@@ -380,6 +390,11 @@ class PeerExchange:
         amax = torch.as_tensor(_DeviceBytes(ptr + self.back_rows * (self.hq_cols + self.hsf_cols), self.experts * 4),
                                device=self.device)
         return hq.view(rows, self.hq_cols), hsf.view(rows, self.hsf_cols), amax.view(torch.int32)
+
+    def result_views(self, s: int, r0: int, r1: int, a: int, b: int) -> tuple[Tensor, Tensor, Tensor]:
+        """Where this rank computes source s's hidden rows [r0, r1) and the
+        maxima of its segments [a, b) before they travel back."""
+        return self.res_hq[s, r0:r1], self.res_hsf[s, r0:r1], self.res_amax[s, a:b]
 
     def recv_slot(self, d: int, s: int) -> tuple[int, int]:
         """Device addresses (on this rank) of rank d's slot for source s: rows, scales."""
@@ -432,6 +447,15 @@ class PeerExchange:
         capi.check(lib.praxis_b200_copy_async(C.c_void_p(dst + head), C.c_void_p(src + head), nbytes - head, dev,
                                                C.c_void_p(stream.cuda_stream)))
 
+    def copy_many(self, items: Sequence[tuple[int, int, int]], stream: torch.cuda.Stream,
+                  after: Sequence[torch.cuda.Event] = ()) -> None:
+        """``copy`` of several (dst, src, nbytes) on one stream behind the
+        same events (each waited for once)."""
+        for ev in after:
+            stream.wait_event(ev)
+        for dst, src, nbytes in items:
+            self.copy(dst, src, nbytes, stream, () if self.sm_stream is None else after)
+
     def copy_streams(self) -> list[torch.cuda.Stream]:
         """Every stream the copies run on."""
         return self.streams + ([self.sm_stream] if self.sm_stream is not None else [])
@@ -464,7 +488,6 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     chunks = max(1, min(e_local, chunks))
 
     routing = backend.route_rows(x, top_idx, gate, num_experts)
-    q, sf = backend.quantize(x, routing)
     csr = routing.csr.to(torch.int64)
     pcsr = routing.pcsr.to(torch.int64)
     counts = (csr[1:] - csr[:-1]).view(world, e_local)
@@ -491,6 +514,9 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
     rel_host = [host[5 * world + 1 + i * e_local:5 * world + 1 + (i + 1) * e_local] for i in range(world)]
     max_tokens = max(tokens_all)
     f = backend.hidden_features
+    # the quantize is queued after the host read, so the GPU runs it while
+    # the host queues the transfers and the expert groups below
+    q, sf = backend.quantize(x, routing)
     peers.ensure(_padded(max_tokens * top_k + 127 * e_local), _padded(max_tokens * top_k + 127 * num_experts),
                  q.shape[1], sf.shape[1], f // 2, f // 16, num_experts)
 
@@ -518,9 +544,18 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
         q.record_stream(st)
         sf.record_stream(st)
 
-    seg_counts = meta_recv[:, :e_local]
+    # per source and expert group: segment counts, segment starts relative
+    # to the group's first row, and global scales, as contiguous rows (a few
+    # batched ops here instead of three small copies per source and group)
+    seg_counts = meta_recv[:, :e_local].contiguous()
     seg_starts = torch.cat([meta_recv[:, e_local:2 * e_local], meta_recv[:, 3 * e_local:3 * e_local + 1]], dim=1)
     seg_global = meta_recv[:, 2 * e_local:3 * e_local].contiguous().view(torch.float32)
+    groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
+    # this rank's own rows: most of them while its rows travel out (half on
+    # 2 ranks, three quarters on more, where more rows leave), the rest last
+    half = e_local - e_local // (2 if world <= 2 else 4)
+    group_starts = {(a, b): (seg_starts[:, a:b + 1] - seg_starts[:, a:a + 1]).to(torch.int32).contiguous()
+                    for a, b in set(groups + [(0, half), (half, e_local)]) if a < b}
     hq_back, hsf_back, hamax = peers.back_views(lo[world])
     returned = [0]
 
@@ -539,39 +574,31 @@ def exchange_forward_peer(x: Tensor, top_idx: Tensor, gate: Tensor, *, num_exper
         else:
             rq, rsf = peers.recv_views(src, recv_rows[src])
             sq, ssf = rq[r0:r1], rsf[r0:r1]
-        counts, starts = seg_counts[src, a:b].contiguous(), (seg_starts[src, a:b + 1] - r0).to(torch.int32)
-        ag = seg_global[src, a:b].contiguous()
+        counts, starts, ag = seg_counts[src, a:b], group_starts[(a, b)][src], seg_global[src, a:b]
         if src == rank:  # own rows: straight into this rank's return buffers
             row = lo[rank] + r0
             backend.hidden(sq, ssf, counts, starts, ag, a, b,
                            out=(hq_back[row:row + r1 - r0], hsf_back[row:row + r1 - r0],
                                 hamax[rank * e_local + a:rank * e_local + b]))
             return
-        # other sources: local result, then a copy engine writes it into the
-        # source's mapped buffers while the next group computes
-        hq, hsf, amax = backend.hidden(sq, ssf, counts, starts, ag, a, b)
+        # other sources: the result in this rank's region for the source,
+        # then a copy engine writes it into the source's mapped buffers while
+        # the next group computes
+        hq, hsf, amax = peers.result_views(src, r0, r1, a, b)
+        backend.hidden(sq, ssf, counts, starts, ag, a, b, out=(hq, hsf, amax))
         done = torch.cuda.Event()
         done.record(compute)
         st = streams[returned[0] % len(streams)]
         returned[0] += 1
         d_hq, d_hsf, d_amax = peers.back_ptrs(src, src_row0[src] + r0, rank * e_local + a)
-        peers.copy(d_hq, hq.data_ptr(), hq.numel(), st, [done])
-        peers.copy(d_hsf, hsf.data_ptr(), hsf.numel(), st, [done])
-        peers.copy(d_amax, amax.data_ptr(), amax.numel() * 4, st, [done])
-        for cs in peers.copy_streams():
-            for t_ in (hq, hsf, amax):
-                t_.record_stream(cs)
+        peers.copy_many([(d_hq, hq.data_ptr(), hq.numel()), (d_hsf, hsf.data_ptr(), hsf.numel()),
+                         (d_amax, amax.data_ptr(), amax.numel() * 4)], st, [done])
 
-    # most of this rank's own rows while its rows travel out (half on 2
-    # ranks, three quarters on more, where more rows leave); the other
-    # sources in rotating order, in `chunks` expert groups so each result
-    # travels back while the next group computes; the rest of the own rows
-    # last, while the final results travel; then the down GEMM of all this
-    # rank's rows and the combine
-    tail = e_local // (2 if world <= 2 else 4)
-    half = e_local - tail
+    # the own rows' first part; the other sources in rotating order, in
+    # `chunks` expert groups so each result travels back while the next
+    # group computes; the rest of the own rows last, while the final results
+    # travel; then the down GEMM of all this rank's rows and the combine
     run(rank, 0, half)
-    groups = [(c * e_local // chunks, (c + 1) * e_local // chunks) for c in range(chunks)]
     for j in range(1, world):
         src = (rank - j) % world  # the source whose rows were sent to this rank j-th
         if recv_rows[src]:

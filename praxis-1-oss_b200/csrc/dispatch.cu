@@ -10,7 +10,8 @@
 //                                         tiles that hold routed rows)
 //   praxis/kernels/nvfp4_moe.py:15-57     row max |x| and per-expert global scale
 //
-// Three launches, no host synchronisation and no atomics on the data path:
+// Three launches (one, of all three passes in one CTA, when the routed rows
+// fit 32 segments), no host synchronisation and no atomics on the data path:
 //   1. count   one warp per segment of positions: per-segment expert
 //              histogram and max row-amax (warp-aggregated shared atomics)
 //   2. scan    one CTA: per-expert exclusive scan over segments, block scan
@@ -63,6 +64,45 @@ __device__ __forceinline__ int64_t token_of(int64_t p, int top_k) {
 // ---------------------------------------------------------------------------
 // `experts` counts the routed experts, `groups` = experts * passes.n the
 // histogram bins (route_group).
+// One warp's segment: its per-group histogram h and max row-amax hm (this
+// warp's zeroed shared rows), then written to seg_count / seg_max.
+__device__ __forceinline__ void count_segment(const int64_t* __restrict__ top_idx,
+                                              const uint16_t* __restrict__ row_amax, int64_t positions, int top_k,
+                                              int experts, Passes passes, int groups, int seg_len, int seg,
+                                              uint32_t* h, uint32_t* hm, int32_t* __restrict__ seg_count,
+                                              uint32_t* __restrict__ seg_max) {
+  const int lane = threadIdx.x & 31;
+  const int64_t begin = (int64_t)seg * seg_len;
+  const int64_t end = min(positions, begin + seg_len);
+  // the loads of 8 passes of 32 positions go out before the histogram work
+  for (int64_t base = begin; base < end; base += 32 * kDispatchUnroll) {
+    int ev[kDispatchUnroll];
+    uint32_t mv[kDispatchUnroll];
+#pragma unroll
+    for (int u = 0; u < kDispatchUnroll; ++u) {
+      const int64_t p = base + 32 * u + lane;
+      const bool live = p < end;
+      ev[u] = live ? route_group(checked_expert(top_idx[p], experts), token_of(p, top_k), passes) : -1;
+      mv[u] = (live && row_amax != nullptr) ? __float_as_uint(bf16_to_f32(row_amax[token_of(p, top_k)])) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kDispatchUnroll; ++u) {
+      if (base + 32 * u >= end) break;
+      const int e = ev[u];
+      const bool live = e >= 0;
+      const uint32_t peers = __match_any_sync(0xffffffffu, e);
+      const int leader = __ffs(peers) - 1;
+      if (live && lane == leader) atomicAdd(&h[e], (uint32_t)__popc(peers));
+      if (live && row_amax != nullptr) atomicMax(&hm[e], mv[u]);
+    }
+  }
+  __syncwarp();
+  for (int e = lane; e < groups; e += 32) {
+    seg_count[(int64_t)seg * groups + e] = (int32_t)h[e];
+    seg_max[(int64_t)seg * groups + e] = hm[e];
+  }
+}
+
 __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ row_amax,
                                       int64_t positions, int top_k, int experts, Passes passes, int groups,
                                       int seg_len, int segments, int32_t* __restrict__ seg_count,
@@ -72,48 +112,16 @@ __global__ void dispatch_count_kernel(const int64_t* __restrict__ top_idx, const
   extern __shared__ uint32_t s_dc[];
   uint32_t* hist = s_dc;                                 // [warps][groups]
   uint32_t* hmax = s_dc + kDispatchWarps * groups;       // [warps][groups]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < kDispatchWarps * groups; i += blockDim.x) {
     hist[i] = 0;
     hmax[i] = 0;
   }
   __syncthreads();
   const int seg = blockIdx.x * kDispatchWarps + warp;
-  if (seg < segments) {
-    const int64_t begin = (int64_t)seg * seg_len;
-    const int64_t end = min(positions, begin + seg_len);
-    uint32_t* h = hist + warp * groups;
-    uint32_t* hm = hmax + warp * groups;
-    // the loads of 8 passes of 32 positions go out before the histogram work
-    for (int64_t base = begin; base < end; base += 32 * kDispatchUnroll) {
-      int ev[kDispatchUnroll];
-      uint32_t mv[kDispatchUnroll];
-#pragma unroll
-      for (int u = 0; u < kDispatchUnroll; ++u) {
-        const int64_t p = base + 32 * u + lane;
-        const bool live = p < end;
-        ev[u] = live ? route_group(checked_expert(top_idx[p], experts), token_of(p, top_k), passes) : -1;
-        mv[u] = (live && row_amax != nullptr) ? __float_as_uint(bf16_to_f32(row_amax[token_of(p, top_k)])) : 0u;
-      }
-#pragma unroll
-      for (int u = 0; u < kDispatchUnroll; ++u) {
-        if (base + 32 * u >= end) break;
-        const int e = ev[u];
-        const bool live = e >= 0;
-        const uint32_t peers = __match_any_sync(0xffffffffu, e);
-        const int leader = __ffs(peers) - 1;
-        if (live && lane == leader) atomicAdd(&h[e], (uint32_t)__popc(peers));
-        if (live && row_amax != nullptr) atomicMax(&hm[e], mv[u]);
-      }
-    }
-  }
-  __syncwarp();
-  if (seg < segments) {
-    for (int e = lane; e < groups; e += 32) {
-      seg_count[(int64_t)seg * groups + e] = (int32_t)hist[warp * groups + e];
-      seg_max[(int64_t)seg * groups + e] = hmax[warp * groups + e];
-    }
-  }
+  if (seg < segments)
+    count_segment(top_idx, row_amax, positions, top_k, experts, passes, groups, seg_len, seg, hist + warp * groups,
+                  hmax + warp * groups, seg_count, seg_max);
 }
 
 // Block-wide exclusive scan of one value per thread (blockDim.x <= 1024).
@@ -146,13 +154,11 @@ __device__ int block_exclusive_scan(int v, int* s_warp, int* total) {
 // ---------------------------------------------------------------------------
 // 2. scan (single CTA of 1024 threads; experts <= 1024)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) dispatch_scan_kernel(
+__device__ void scan_segments(
     int32_t* __restrict__ seg_count, const uint32_t* __restrict__ seg_max, int segments, int experts,
     int64_t positions, int align, int32_t* __restrict__ offsets, int32_t* __restrict__ csr,
     int32_t* __restrict__ pcsr, TileEntry* __restrict__ tiles, int max_tiles, int32_t* __restrict__ num_tiles,
     float* __restrict__ act_global, uint32_t* __restrict__ act_amax_bits) {
-  pdl_wait();  // the previous kernel of the stream has completed
-  pdl_trigger();
   __shared__ int s_warp[32];
   __shared__ int s_part[1024];
   __shared__ uint32_t s_pmax[1024];
@@ -273,6 +279,18 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(
   }
 }
 
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(
+    int32_t* __restrict__ seg_count, const uint32_t* __restrict__ seg_max, int segments, int experts,
+    int64_t positions, int align, int32_t* __restrict__ offsets, int32_t* __restrict__ csr,
+    int32_t* __restrict__ pcsr, TileEntry* __restrict__ tiles, int max_tiles, int32_t* __restrict__ num_tiles,
+    float* __restrict__ act_global, uint32_t* __restrict__ act_amax_bits) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
+  scan_segments(seg_count, seg_max, segments, experts, positions, align, offsets, csr, pcsr, tiles, max_tiles,
+                num_tiles, act_global, act_amax_bits);
+}
+
+
 // ---------------------------------------------------------------------------
 // Tile tables of received segments (expert parallelism): segment v holds
 // counts[v] routed rows from padded row starts[v] (128-aligned); the 128-row
@@ -334,22 +352,15 @@ int run_segment_tiles(const int32_t* counts, const int32_t* starts, int segments
 // ---------------------------------------------------------------------------
 // 3. scatter
 // ---------------------------------------------------------------------------
-__global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate,
-                                        int64_t positions, int top_k, int experts, Passes passes, int groups,
-                                        int seg_len, int segments,
-                                        const int32_t* __restrict__ seg_start, const int32_t* __restrict__ csr,
-                                        int64_t* __restrict__ order, int64_t* __restrict__ inverse,
-                                        int64_t* __restrict__ tokens, int32_t* __restrict__ tokens32,
-                                        uint16_t* __restrict__ sorted_gate) {
-  pdl_wait();  // the previous kernel of the stream has completed
-  pdl_trigger();
-  extern __shared__ int32_t s_cursor[];  // [warps][groups]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int seg = blockIdx.x * kDispatchWarps + warp;
-  if (seg >= segments) return;
-  int32_t* cur = s_cursor + warp * groups;
-  for (int e = lane; e < groups; e += 32) cur[e] = csr[e] + seg_start[(int64_t)seg * groups + e];
-  __syncwarp();
+// One warp's segment: its routed positions in order into their rows, from
+// the warp's cursor row (cur[g] = csr[g] + the segment's start in group g).
+__device__ __forceinline__ void scatter_segment(const int64_t* __restrict__ top_idx,
+                                                const uint16_t* __restrict__ gate, int64_t positions, int top_k,
+                                                int experts, Passes passes, int seg_len, int seg, int32_t* cur,
+                                                int64_t* __restrict__ order, int64_t* __restrict__ inverse,
+                                                int64_t* __restrict__ tokens, int32_t* __restrict__ tokens32,
+                                                uint16_t* __restrict__ sorted_gate) {
+  const int lane = threadIdx.x & 31;
   const int64_t begin = (int64_t)seg * seg_len;
   const int64_t end = min(positions, begin + seg_len);
   const uint32_t lt = (1u << lane) - 1u;
@@ -384,6 +395,70 @@ __global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, con
         if (sorted_gate) sorted_gate[dest] = gv[u];
       }
     }
+  }
+}
+
+__global__ void dispatch_scatter_kernel(const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate,
+                                        int64_t positions, int top_k, int experts, Passes passes, int groups,
+                                        int seg_len, int segments,
+                                        const int32_t* __restrict__ seg_start, const int32_t* __restrict__ csr,
+                                        int64_t* __restrict__ order, int64_t* __restrict__ inverse,
+                                        int64_t* __restrict__ tokens, int32_t* __restrict__ tokens32,
+                                        uint16_t* __restrict__ sorted_gate) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
+  extern __shared__ int32_t s_cursor[];  // [warps][groups]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seg = blockIdx.x * kDispatchWarps + warp;
+  if (seg >= segments) return;
+  int32_t* cur = s_cursor + warp * groups;
+  for (int e = lane; e < groups; e += 32) cur[e] = csr[e] + seg_start[(int64_t)seg * groups + e];
+  __syncwarp();
+  scatter_segment(top_idx, gate, positions, top_k, experts, passes, seg_len, seg, cur, order, inverse, tokens,
+                  tokens32, sorted_gate);
+}
+
+// ---------------------------------------------------------------------------
+// Small batches: the three passes in one CTA of 32 warps (one per segment,
+// segments <= 32), with the same arithmetic and results; the passes meet at
+// __syncthreads (the scan's and the scatter's reads of seg_count / csr in
+// global memory follow the writes of the same CTA).
+// ---------------------------------------------------------------------------
+constexpr int kFusedWarps = 32;
+constexpr int kFusedMaxGroups = 256;
+
+__global__ void __launch_bounds__(1024) dispatch_fused_kernel(
+    const int64_t* __restrict__ top_idx, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ row_amax,
+    int64_t positions, int top_k, int experts, Passes passes, int groups, int seg_len, int segments,
+    int32_t* __restrict__ seg_count, uint32_t* __restrict__ seg_max, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ csr, int32_t* __restrict__ pcsr, TileEntry* __restrict__ tiles, int max_tiles,
+    int32_t* __restrict__ num_tiles, float* __restrict__ act_global, uint32_t* __restrict__ act_amax_bits,
+    int64_t* __restrict__ order, int64_t* __restrict__ inverse, int64_t* __restrict__ tokens,
+    int32_t* __restrict__ tokens32, uint16_t* __restrict__ sorted_gate) {
+  pdl_wait();  // the previous kernel of the stream has completed
+  pdl_trigger();
+  extern __shared__ uint32_t s_df[];
+  uint32_t* hist = s_df;                        // [warps][groups], then the scatter cursors
+  uint32_t* hmax = s_df + kFusedWarps * groups;  // [warps][groups]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kFusedWarps * groups; i += blockDim.x) {
+    hist[i] = 0;
+    hmax[i] = 0;
+  }
+  __syncthreads();
+  if (warp < segments)
+    count_segment(top_idx, row_amax, positions, top_k, experts, passes, groups, seg_len, warp, hist + warp * groups,
+                  hmax + warp * groups, seg_count, seg_max);
+  __syncthreads();
+  scan_segments(seg_count, seg_max, segments, groups, positions, (int)kTileRows, offsets, csr, pcsr, tiles, max_tiles,
+                num_tiles, act_global, act_amax_bits);
+  __syncthreads();
+  if (positions > 0 && warp < segments) {
+    int32_t* cur = reinterpret_cast<int32_t*>(hist) + warp * groups;
+    for (int e = lane; e < groups; e += 32) cur[e] = csr[e] + seg_count[(int64_t)warp * groups + e];
+    __syncwarp();
+    scatter_segment(top_idx, gate, positions, top_k, experts, passes, seg_len, warp, cur, order, inverse, tokens,
+                    tokens32, sorted_gate);
   }
 }
 
@@ -441,11 +516,22 @@ int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* r
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(dispatch_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kDispatchWarps * kMaxExperts * 4);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(dispatch_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               2 * kFusedWarps * kFusedMaxGroups * 4);
     if (e != cudaSuccess)
       return set_error(PRAXIS_B200_ECUDA, "dispatch smem attribute (device %d): %s", dev, cudaGetErrorString(e));
     return (int)PRAXIS_B200_OK;
   });
   if (rc) return rc;
+  if (segments <= kFusedWarps && groups <= kFusedMaxGroups) {
+    // small batch (<= 32 segments): one launch instead of three
+    launch_pdl(dispatch_fused_kernel, dim3(1), dim3(32 * kFusedWarps), (size_t)2 * kFusedWarps * groups * 4, stream,
+               top_idx, gate, row_amax, positions, top_k, experts, passes, groups, seg_len, segments, seg_count,
+               seg_max, offsets, csr, pcsr, tiles, max_tiles, num_tiles, row_amax ? act_global : nullptr,
+               row_amax ? act_amax_bits : nullptr, order, inverse, tokens_out, tokens32, sorted_gate);
+    return check_launch("dispatch_fused");
+  }
   launch_pdl(dispatch_count_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_count, stream, top_idx, row_amax,
              positions, top_k, experts, passes, groups, seg_len, segments, seg_count, seg_max);
   rc = check_launch("dispatch_count");
@@ -457,8 +543,8 @@ int run_dispatch(const int64_t* top_idx, const uint16_t* gate, const uint16_t* r
   if (rc) return rc;
   if (positions > 0) {
     launch_pdl(dispatch_scatter_kernel, dim3(blocks), dim3(32 * kDispatchWarps), smem_scatter, stream, top_idx, gate,
-               positions, top_k, experts, passes, groups, seg_len, segments, seg_count, csr, order, inverse, tokens_out, tokens32,
-               sorted_gate);
+               positions, top_k, experts, passes, groups, seg_len, segments, seg_count, csr, order, inverse, tokens_out,
+               tokens32, sorted_gate);
     rc = check_launch("dispatch_scatter");
   }
   return rc;

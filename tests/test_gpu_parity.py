@@ -148,6 +148,9 @@ def test_router_logits_and_row_amax(P, splits_dtype):
 @pytest.mark.parametrize("t,e,k,mode", [
     (256, 8, 2, "plain"), (1000, 64, 4, "plain"), (1000, 64, 4, "concentrated"),
     (33, 16, 2, "empty"), (1, 8, 2, "plain"), (4099, 128, 8, "plain"), (20000, 64, 4, "plain"),
+    # 4,096 routed rows = 32 segments: the single-CTA dispatch; one token
+    # more takes the three-pass launches
+    (1024, 64, 4, "concentrated"), (1025, 64, 4, "plain"), (100, 256, 8, "empty"),
 ])
 def test_dispatch_bit_exact(P, t, e, k, mode):
     top, gate = random_routing(t, e, k, seed=t + e, concentrated=mode == "concentrated",

@@ -959,14 +959,18 @@ def run_expert_parallel(args, cfg):
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # one sampler process for the node (rank 0), not one per rank
+    # one sampler process for the node (rank 0), not one per rank; it starts
+    # (and waits for its first samples) before the barrier, so no rank's
+    # timed region holds rank 0's start-up
     clk = ClockSampler(range(world)) if rank == 0 else None
     with clk if clk is not None else contextlib.nullcontext():
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        if clk is not None:
+            clk.t0 = time.time()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -1013,6 +1017,12 @@ def run_expert_parallel(args, cfg):
     # direction of a rank's links carries about this much
     blocks = (pc[el::el] - pc[:-1:el]).tolist()
     off = sum(b for d, b in enumerate(blocks) if d != rank)
+    # whether every pair of this node's ranks has direct peer access (NVLink
+    # P2P); without it the copy engines stage through host memory
+    peer = torch.tensor([int(all(torch.cuda.can_device_access_peer(local, j)
+                                 for j in range(torch.cuda.device_count()) if j != local))], device=dev)
+    dist.all_reduce(peer, op=dist.ReduceOp.MIN)
+    peer_ok = bool(peer.item())
     xbytes = torch.tensor([float(off * (c // 2 + c // 16 + f // 2 + f // 16) + 4 * e)], device=dev)
     dist.all_reduce(xbytes, op=dist.ReduceOp.MAX)
     exchange = {"bytes_per_rank_per_step": float(xbytes.item()),
@@ -1021,7 +1031,8 @@ def run_expert_parallel(args, cfg):
                 "transport": ("copy engines into IPC-mapped peer buffers" if args.transport == "peer" else
                               "NCCL point-to-point") + ": FP4 rows + UE4M3 scales out, FP4 hidden rows + scales "
                              "back, the down GEMM on the source rank",
-                "experts_per_rank": el, "sm_copy_fraction": args.sm_copy_fraction}
+                "experts_per_rank": el, "sm_copy_fraction": args.sm_copy_fraction,
+                "peer_access_all_pairs": peer_ok}
     e2e = None
     if not args.no_e2e:
         torch.cuda.synchronize()

@@ -1206,6 +1206,11 @@ def time_e2e(pkg, layer, x_cpu, out, args, dev, t, world):
     pipe = pkg.pipeline.HostPipeline(layer, x_cpu.shape, out.shape, out.dtype, dev)
     pipe.run([host_in] * 2, [host_out] * 2)
     torch.cuda.synchronize()
+    if world > 1:  # every rank starts its timed steps together
+        import torch.distributed as dist
+
+        dist.barrier()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(pipe.copy_in)
     pipe.run([host_in] * args.steps, [host_out] * args.steps)
